@@ -1,0 +1,281 @@
+"""CPU oracle for the NVFP4 linear path.  TEST INFRASTRUCTURE ONLY.
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline leg may import this
+module, and only as the checker (or as the timed CPU baseline).  The product path in
+``radiance_b200`` never imports it; the CUDA extension is the only implementation that ships.
+
+This is a numpy restatement of radiance's pure-torch NVFP4 emulation,
+``src/radiance/nvfp4/quantize.py`` in jamespa16/radiance.  Each function names the reference lines
+it follows.  Parity is pinned: ``tests/test_oracle_golden.py`` checks every function here against
+vectors produced by the reference itself (``tests/golden/make_golden.py`` imports the reference and
+writes ``tests/golden/nvfp4_golden.npz``), bit-exactly on packed nibbles and scale bytes.
+
+Arithmetic is float32 throughout, one IEEE rounding per operation, exactly as torch's CPU kernels
+do it: numpy float32 ``/`` and ``*`` are correctly rounded, so ``x / (divisor * gs)`` here is the
+same two roundings as the reference's ``xb / (divisor * global_scale)``.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+# Format constants -- quantize.py:16-32.
+FP4_VALUES = (0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0)
+FP4_MAX = np.float32(6.0)
+E4M3_MAX = np.float32(448.0)
+BLOCK = 16
+TINY = np.float32(1e-12)
+
+_F32 = np.float32
+
+
+def _e4m3_table() -> np.ndarray:
+    """Value of every non-negative finite e4m3fn byte 0x00..0x7E (0x7F is NaN)."""
+    vals = np.zeros(127, dtype=np.float64)
+    for b in range(127):
+        e, m = b >> 3, b & 7
+        vals[b] = (m / 8.0) * 2.0**-6 if e == 0 else (1.0 + m / 8.0) * 2.0 ** (e - 7)
+    return vals.astype(np.float32)
+
+
+E4M3_VALUES = _e4m3_table()
+
+
+def bf16_to_f32(bits: np.ndarray) -> np.ndarray:
+    """uint16 bf16 bit patterns -> float32 (exact)."""
+    return (bits.astype(np.uint32) << 16).view(np.float32)
+
+
+def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
+    """float32 -> bf16 bit patterns, round to nearest even (torch's ``.to(torch.bfloat16)``)."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    nan = np.isnan(x)
+    rounded = (u + 0x7FFF + ((u >> 16) & 1)) >> 16
+    out = rounded.astype(np.uint16)
+    out[nan] = 0x7FC0
+    return out
+
+
+def global_scale_of(x: np.ndarray) -> np.float32:
+    """quantize.py:205-213 -- ``(|x|.amax().float() / (6 * 448)).clamp(min=1e-12)``, one fp32 divide."""
+    amax = np.abs(x.astype(np.float32)).max() if x.size else _F32(0.0)
+    return np.maximum(_F32(amax) / _F32(FP4_MAX * E4M3_MAX), TINY)
+
+
+def scale_denominator(gs) -> np.float32:
+    """quantize.py:190-202 -- ``6 * global_scale``, one fp32 multiply."""
+    return _F32(FP4_MAX * _F32(gs))
+
+
+def block_scale(amax: np.ndarray, gs) -> tuple[np.ndarray, np.ndarray]:
+    """quantize.py:160-187 -- block amax -> (e4m3 byte, fp32 divisor).
+
+    ``scale = clamp(amax / denom, 1e-12, 448)``; the byte is the smallest e4m3 value >= scale (the
+    reference casts round-to-nearest-even and bumps one code up when the cast landed below, never
+    onto 0x7F); the divisor is that value, or 1.0 for an all-zero block.
+    """
+    amax = amax.astype(np.float32)
+    scale = np.minimum(np.maximum(amax / scale_denominator(gs), TINY), E4M3_MAX)
+    byte = np.searchsorted(E4M3_VALUES, scale, side="left").astype(np.int64)
+    byte = np.minimum(byte, 0x7E).astype(np.uint8)
+    divisor = np.where(amax > 0, E4M3_VALUES[byte], _F32(1.0)).astype(np.float32)
+    return byte, divisor
+
+
+def encode_e2m1(a: np.ndarray, sign: np.ndarray, u: np.ndarray | None = None) -> np.ndarray:
+    """quantize.py:93-139 -- magnitudes in [0, 6] -> 4-bit codes, sign in bit 3.
+
+    Without ``u``: the round-to-nearest-even ladder (``>`` and ``>=`` alternate so ties go to the
+    even code).  With ``u`` (uniform [0, 1) per element): stochastic rounding, up with probability
+    ``(a - lo) / (hi - lo)``.
+    """
+    a = a.astype(np.float32)
+    if u is None:
+        code = (
+            (a > 0.25).astype(np.uint8)
+            + (a >= 0.75)
+            + (a > 1.25)
+            + (a >= 1.75)
+            + (a > 2.5)
+            + (a >= 3.5)
+            + (a > 5.0)
+        ).astype(np.uint8)
+    else:
+        lo = (
+            (a >= 0.5).astype(np.uint8)
+            + (a >= 1.0)
+            + (a >= 1.5)
+            + (a >= 2.0)
+            + (a >= 3.0)
+            + (a >= 4.0)
+            + (a >= 6.0)
+        ).astype(np.uint8)
+        levels = np.array(FP4_VALUES + (6.0,), dtype=np.float32)
+        lo_v = levels[lo]
+        hi_v = levels[lo + 1]
+        span = np.maximum(hi_v - lo_v, TINY)
+        with np.errstate(invalid="ignore", divide="ignore"):
+            frac = np.where(hi_v > lo_v, (a - lo_v) / span, _F32(0.0)).astype(np.float32)
+        code = np.minimum(lo + (u.astype(np.float32) < frac), 7).astype(np.uint8)
+    return (code | (sign.astype(np.uint8) << 3)).astype(np.uint8)
+
+
+def pack_nibbles(code: np.ndarray) -> np.ndarray:
+    """quantize.py:142-149 -- element 2i in the low nibble of byte i, 2i+1 in the high nibble."""
+    return (code[..., 0::2] | (code[..., 1::2] << 4)).astype(np.uint8)
+
+
+def unpack_nibbles(packed: np.ndarray) -> np.ndarray:
+    """quantize.py:152-157."""
+    low = packed & 0x0F
+    high = packed >> 4
+    return np.stack([low, high], axis=-1).reshape(*packed.shape[:-1], packed.shape[-1] * 2)
+
+
+def _quantize_blocks(xb: np.ndarray, gs, axis: int, u: np.ndarray | None):
+    """Shared body of the two quantizers: amax over ``axis`` (the 16-wide block axis), the block
+    scale, the IEEE divide by ``divisor * gs``, the +-6 clamp and the encode."""
+    gs = _F32(gs)
+    amax = np.abs(xb).max(axis=axis, keepdims=True)
+    byte, divisor = block_scale(amax, gs)
+    with np.errstate(invalid="ignore", divide="ignore", over="ignore"):
+        q = np.clip(xb / (divisor * gs), -FP4_MAX, FP4_MAX).astype(np.float32)
+    code = encode_e2m1(np.abs(q), q < 0, u)
+    return code, byte
+
+
+def quantize_rowblock(x: np.ndarray, gs, u: np.ndarray | None = None):
+    """quantize.py:216-232 -- (M, K) -> packed (M, K/2) uint8, unswizzled scale bytes (M, K/16)."""
+    m, k = x.shape
+    xb = x.astype(np.float32).reshape(m, k // BLOCK, BLOCK)
+    ub = None if u is None else u.reshape(m, k // BLOCK, BLOCK)
+    code, byte = _quantize_blocks(xb, gs, 2, ub)
+    return pack_nibbles(code.reshape(m, k)), byte.reshape(m, k // BLOCK)
+
+
+def rotate_blocks(xb: np.ndarray, hadamard: np.ndarray) -> np.ndarray:
+    """quantize.py:261-262 -- ``einsum("ij,bjk->bik", H.T, xb)`` in float32.
+
+    torch's CPU einsum sums over ``j`` left to right with one rounding per add (checked against the
+    reference on bf16 and fp32 inputs by ``tests/test_oracle_golden.py``), so this is the same
+    sequential sum.  With the +-0.25 entries of a normalised Hadamard every product is exact.
+    """
+    ht = hadamard.astype(np.float32).T
+    out = np.empty_like(xb)
+    for i in range(BLOCK):
+        acc = ht[i, 0] * xb[:, 0, :]
+        for j in range(1, BLOCK):
+            acc = (acc + ht[i, j] * xb[:, j, :]).astype(np.float32)
+        out[:, i, :] = acc
+    return out
+
+
+def quantize_colblock(x: np.ndarray, gs, hadamard: np.ndarray | None = None, u: np.ndarray | None = None):
+    """quantize.py:235-268 -- blocks along dim 0, output transposed.
+
+    (M, K) -> packed (K, M/2) uint8, unswizzled scale bytes (K, M/16).  ``u`` is indexed by the
+    original (M, K) position, as in the reference.
+    """
+    m, k = x.shape
+    xb = x.astype(np.float32).reshape(m // BLOCK, BLOCK, k)
+    if hadamard is not None:
+        xb = rotate_blocks(xb, hadamard)
+    ub = None if u is None else u.reshape(m // BLOCK, BLOCK, k)
+    code, byte = _quantize_blocks(xb, gs, 1, ub)
+    code = code.reshape(m, k).T.copy()
+    return pack_nibbles(code), byte.reshape(m // BLOCK, k).T.copy()
+
+
+def to_blocked(scale: np.ndarray) -> np.ndarray:
+    """quantize.py:271-290 -- (rows, cols) scale bytes -> flat SWIZZLE_32_4_4, zero-padded to whole
+    128x4 tiles."""
+    rows, cols = scale.shape
+    nrt, nct = (rows + 127) // 128, (cols + 3) // 4
+    padded = np.zeros((nrt * 128, nct * 4), dtype=scale.dtype)
+    padded[:rows, :cols] = scale
+    tiles = padded.reshape(nrt, 128, nct, 4).transpose(0, 2, 1, 3)
+    return tiles.reshape(-1, 4, 32, 4).transpose(0, 2, 1, 3).reshape(-1).copy()
+
+
+def from_blocked(flat: np.ndarray, rows: int, cols: int) -> np.ndarray:
+    """Inverse of ``to_blocked`` (drops the padding)."""
+    nrt, nct = (rows + 127) // 128, (cols + 3) // 4
+    tiles = flat.reshape(nrt * nct, 32, 4, 4).transpose(0, 2, 1, 3).reshape(nrt, nct, 128, 4)
+    return tiles.transpose(0, 2, 1, 3).reshape(nrt * 128, nct * 4)[:rows, :cols].copy()
+
+
+def blocked_offset(r, c, n_col_tiles: int):
+    """quantize.py:293-305 -- byte offset of scale element (r, c) in the SWIZZLE_32_4_4 layout."""
+    return ((r // 128) * n_col_tiles + c // 4) * 512 + (r % 32) * 16 + ((r % 128) // 32) * 4 + (c % 4)
+
+
+def hadamard_signs_seed0() -> np.ndarray:
+    """Row signs of the reference's ``hadamard_matrix(16, seed=0)`` (quantize.py:647-659), as the
+    reference itself produces them (pinned by the golden fixture)."""
+    return np.array([-1, 1, -1, -1, -1, 1, -1, 1, -1, 1, -1, -1, -1, -1, -1, 1], dtype=np.float32)
+
+
+def sylvester(n: int = BLOCK) -> np.ndarray:
+    h = np.ones((1, 1), dtype=np.float32)
+    while h.shape[0] < n:
+        h = np.block([[h, h], [h, -h]])
+    return h.astype(np.float32)
+
+
+def hadamard_matrix(signs: np.ndarray | None = None) -> np.ndarray:
+    """quantize.py:647-659 -- Sylvester Hadamard / sqrt(16) with row signs."""
+    s = hadamard_signs_seed0() if signs is None else signs.astype(np.float32)
+    return (sylvester(BLOCK) / np.float32(4.0) * s[:, None]).astype(np.float32)
+
+
+def dequantize(packed: np.ndarray, scale: np.ndarray, gs) -> np.ndarray:
+    """quantize.py:308-320 -- packed nibbles + unswizzled scale bytes -> fp32."""
+    code = unpack_nibbles(packed)
+    values = np.array(FP4_VALUES, dtype=np.float32)
+    mag = values[code & 7]
+    signed = np.where(code >= 8, -mag, mag).astype(np.float32)
+    rows, cols = signed.shape
+    blocks = signed.reshape(rows, cols // BLOCK, BLOCK)
+    s = (E4M3_VALUES[scale].astype(np.float32) * _F32(gs)).astype(np.float32)
+    return (blocks * s[..., None]).reshape(rows, cols).astype(np.float32)
+
+
+def quantize_supported_shape(rows: int, cols: int) -> bool:
+    """quantize.py:662-669."""
+    return rows % 128 == 0 and cols % 64 == 0
+
+
+def quantize(x: np.ndarray, axis: int, gs=None, hadamard=None, u=None):
+    """quantize.py:412-433 (``quantize_reference``) -> (packed, swizzled flat scale, gs)."""
+    if gs is None:
+        gs = global_scale_of(x)
+    if axis in (-1, x.ndim - 1):
+        packed, scale = quantize_rowblock(x, gs, u=u)
+    elif axis == 0:
+        packed, scale = quantize_colblock(x, gs, hadamard=hadamard, u=u)
+    else:
+        raise ValueError(f"nvfp4.quantize supports axis 0 or -1, got {axis}")
+    return packed, to_blocked(scale), _F32(gs)
+
+
+def gemm_reference(a_packed, a_scale_flat, a_gs, b_packed, b_scale_flat, b_gs) -> np.ndarray:
+    """The GEMM oracle: dequantize both operands (quantize.py:308-320, global scales included) and
+    take ``a @ b.T`` in float64.  The reference's ``mm`` (quantize.py:400-409) computes the same
+    product in the tensor cores and rounds to bf16 before multiplying the global scales back in."""
+    ra, ka = a_packed.shape[0], a_packed.shape[1] * 2
+    rb, kb = b_packed.shape[0], b_packed.shape[1] * 2
+    assert ka == kb
+    sa = from_blocked(a_scale_flat, ra, ka // BLOCK)
+    sb = from_blocked(b_scale_flat, rb, kb // BLOCK)
+    da = dequantize(a_packed, sa, a_gs).astype(np.float64)
+    db = dequantize(b_packed, sb, b_gs).astype(np.float64)
+    return da @ db.T
+
+
+def linear_forward_reference(x: np.ndarray, w: np.ndarray) -> np.ndarray:
+    """The reference's CPU emulation of one FP4 linear forward: global scales,
+    rowblock quantize of both operands, dequantize, fp32 matmul.  Returns float32."""
+    gx, gw = global_scale_of(x), global_scale_of(w)
+    xp, xs = quantize_rowblock(x, gx)
+    wp, ws = quantize_rowblock(w, gw)
+    return (dequantize(xp, xs, gx) @ dequantize(wp, ws, gw).T).astype(np.float32)

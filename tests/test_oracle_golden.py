@@ -1,0 +1,128 @@
+"""The oracle against vectors produced by the reference implementation itself.
+
+``tests/golden/nvfp4_golden.npz`` was written by ``tests/golden/make_golden.py``, which imports
+radiance's pure-torch NVFP4 emulation (src/radiance/nvfp4/quantize.py).  Every comparison here is
+bit-exact (packed nibbles, swizzled scale bytes, global-scale bits); these are the assertions that
+let the GPU tests trust the oracle.
+"""
+
+import hashlib
+
+import numpy as np
+import pytest
+
+from oracle import nvfp4_oracle as O
+
+
+def _x(golden, name):
+    raw = golden[f"{name}/x"]
+    return O.bf16_to_f32(raw) if int(golden[f"{name}/dtype"]) == 0 else raw.astype(np.float32)
+
+
+def _cases(golden):
+    return [str(c) for c in golden["cases"]]
+
+
+def test_hadamard_matrix_matches_reference(golden):
+    np.testing.assert_array_equal(O.hadamard_matrix(), golden["hadamard_seed0"])
+    signs1 = np.sign(golden["hadamard_seed1"][:, 0])
+    np.testing.assert_array_equal(O.hadamard_matrix(signs1), golden["hadamard_seed1"])
+
+
+def test_global_scale_bits(golden):
+    for name in _cases(golden):
+        gs = O.global_scale_of(_x(golden, name))
+        assert np.float32(gs).view(np.uint32) == golden[f"{name}/gs"].view(np.uint32), name
+
+
+@pytest.mark.parametrize("tag", ["row", "col", "colh", "colh1"])
+def test_quantize_bit_exact(golden, tag):
+    had = {"colh": golden["hadamard_seed0"], "colh1": golden["hadamard_seed1"]}.get(tag)
+    for name in _cases(golden):
+        x = _x(golden, name)
+        gs = golden[f"{name}/gs"]
+        packed, scale, _ = O.quantize(x, -1 if tag == "row" else 0, gs=gs, hadamard=had)
+        np.testing.assert_array_equal(packed, golden[f"{name}/{tag}_packed"], err_msg=f"{name} {tag}")
+        np.testing.assert_array_equal(scale, golden[f"{name}/{tag}_scale"], err_msg=f"{name} {tag}")
+
+
+def test_stochastic_rounding_bit_exact_for_a_given_draw(golden):
+    name = "rand1"
+    x, gs, u = _x(golden, name), golden[f"{name}/gs"], golden[f"{name}/u"]
+    p, s = O.quantize_rowblock(x, gs, u=u)
+    np.testing.assert_array_equal(p, golden[f"{name}/sr_row_packed"])
+    np.testing.assert_array_equal(O.to_blocked(s), golden[f"{name}/sr_row_scale"])
+    p, s = O.quantize_colblock(x, gs, hadamard=golden["hadamard_seed0"], u=u)
+    np.testing.assert_array_equal(p, golden[f"{name}/sr_colh_packed"])
+    np.testing.assert_array_equal(O.to_blocked(s), golden[f"{name}/sr_colh_scale"])
+
+
+@pytest.mark.parametrize("shape", [(128, 4), (256, 8), (4096, 80), (100, 16), (64, 16)])
+def test_blocked_layout(golden, shape):
+    rows, cols = shape
+    scale = golden[f"blocked/{rows}x{cols}/scale"]
+    expected = golden[f"blocked/{rows}x{cols}/expected"]
+    np.testing.assert_array_equal(O.to_blocked(scale), expected)
+    r, c = np.meshgrid(np.arange(rows), np.arange(cols), indexing="ij")
+    got = np.zeros_like(expected)
+    got[O.blocked_offset(r, c, (cols + 3) // 4).reshape(-1)] = scale.reshape(-1)
+    np.testing.assert_array_equal(got, expected)
+    np.testing.assert_array_equal(O.from_blocked(expected, rows, cols), scale)
+
+
+def test_encode_tables(golden):
+    ties = np.array([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0], dtype=np.float32)
+    np.testing.assert_array_equal(O.encode_e2m1(ties, np.zeros(7, bool)), golden["encode/ties"])
+    np.testing.assert_array_equal(golden["encode/ties"], [0, 2, 2, 4, 4, 6, 6])
+    a, u = golden["encode/grid"], golden["encode/grid_u"]
+    np.testing.assert_array_equal(O.encode_e2m1(a, np.zeros(a.shape, bool)), golden["encode/grid_rn"])
+    np.testing.assert_array_equal(O.encode_e2m1(a, np.zeros(a.shape, bool), u), golden["encode/grid_sr"])
+
+
+def test_pack_is_low_nibble_first():
+    code = np.array([[1, 2, 3, 4]], dtype=np.uint8)
+    np.testing.assert_array_equal(O.pack_nibbles(code), [[0x21, 0x43]])
+    np.testing.assert_array_equal(O.unpack_nibbles(O.pack_nibbles(code)), code)
+
+
+def test_dequantize(golden):
+    x = O.bf16_to_f32(golden["dequant/x"])
+    gs = O.global_scale_of(x)
+    p, s = O.quantize_rowblock(x, gs)
+    np.testing.assert_array_equal(O.dequantize(p, s, gs), golden["dequant/out"])
+
+
+def test_config1_forward_matches_reference(golden):
+    """BASELINE config 1 (the reference's CPU-runnable case): identical inputs, the oracle's
+    forward, rounded to bf16, equals the reference's to within one bf16 ulp (the fp32 matmul's
+    summation order is BLAS-dependent; everything before it is bit-exact)."""
+    torch = pytest.importorskip("torch")
+    torch.manual_seed(0)
+    x = torch.randn(256, 1024).bfloat16()
+    w = (torch.randn(1024, 1024) * 0.02).bfloat16()
+    xb = x.view(torch.int16).numpy().view(np.uint16)
+    wb = w.view(torch.int16).numpy().view(np.uint16)
+    assert hashlib.sha256(xb.tobytes()).hexdigest() == str(golden["config1/x_sha256"])
+    assert hashlib.sha256(wb.tobytes()).hexdigest() == str(golden["config1/w_sha256"])
+    xf, wf = O.bf16_to_f32(xb), O.bf16_to_f32(wb)
+    gx, gw = O.global_scale_of(xf), O.global_scale_of(wf)
+    assert gx.view(np.uint32) == golden["config1/gx"].view(np.uint32)
+    assert gw.view(np.uint32) == golden["config1/gw"].view(np.uint32)
+    xp, _ = O.quantize_rowblock(xf, gx)
+    wp, _ = O.quantize_rowblock(wf, gw)
+    assert hashlib.sha256(xp.tobytes()).hexdigest() == str(golden["config1/x_packed_sha256"])
+    assert hashlib.sha256(wp.tobytes()).hexdigest() == str(golden["config1/w_packed_sha256"])
+    y = O.linear_forward_reference(xf, wf)
+    ref = O.bf16_to_f32(golden["config1/y_bf16"])
+    got = O.bf16_to_f32(O.f32_to_bf16_bits(y))
+    # One bf16 ulp of the reference value, or 1e-5 of the output's range for the few elements
+    # whose fp32 sum cancels (there the BLAS summation order decides the last bits).
+    tol = np.maximum(np.abs(ref) * 2.0**-7, 1e-5 * np.abs(ref).max())
+    assert (np.abs(got - ref) <= tol).all()
+    assert (got == ref).mean() > 0.99
+
+
+def test_unsupported_axis_raises():
+    O.quantize(np.random.randn(32, 32).astype(np.float32), 1)
+    with pytest.raises(ValueError, match="axis 0 or -1"):
+        O.quantize(np.random.randn(32, 32).astype(np.float32), 2)
