@@ -1,0 +1,124 @@
+/*
+ * radiance_nvfp4 -- C ABI of the B200-native NVFP4 linear-layer path.
+ *
+ * Plain pointers and sizes only: every tensor argument is a device pointer the caller owns
+ * (allocated by any allocator), every call is asynchronous on the caller's CUDA stream
+ * (`stream` is a cudaStream_t, NULL for the legacy default stream), and no call synchronises the
+ * host.  Global scales, the stochastic-rounding seed and the GEMM's alpha are read on the device
+ * through pointers, so a sequence of calls can be captured in a CUDA graph.
+ *
+ * Return value: 0 on success, otherwise an RB_ERR_* code with a message available from
+ * rb_nvfp4_last_error() (thread-local).  Kernels never trap: a device-side wait that runs out
+ * records a code readable with rb_nvfp4_device_status().
+ *
+ * Layouts (identical to radiance's; src/radiance/nvfp4/quantize.py in jamespa16/radiance):
+ *   packed  : uint8, two e2m1 codes per byte, element 2i in the low nibble (quantize.py:142-149).
+ *   scale   : uint8 e4m3 block scales, one per 16 elements along the contraction dimension, in
+ *             the flat SWIZZLE_32_4_4 order of quantize.py:271-305: scale (r, c) lives at byte
+ *             ((r/128)*ceil(cols/4) + c/4)*512 + (r%32)*16 + ((r%128)/32)*4 + c%4, zero-padded
+ *             to whole 128x4 tiles.
+ *   rowblock: (rows, cols) -> packed (rows, cols/2), scale tiles (rows/128) x (cols/64).
+ *   colblock: (rows, cols) -> packed (cols, rows/2), scale tiles ceil(cols/128) x (rows/64)
+ *             (blocks run along dim 0 and the output is transposed; quantize.py:235-268).
+ */
+#ifndef RADIANCE_NVFP4_H_
+#define RADIANCE_NVFP4_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define RB_NVFP4_ABI_VERSION 1
+
+/* Input element types. */
+#define RB_DTYPE_BF16 0
+#define RB_DTYPE_F32 1
+
+/* Output element types of the GEMMs. */
+#define RB_OUT_BF16 0
+#define RB_OUT_F32 1
+
+/* Return codes. */
+#define RB_OK 0
+#define RB_ERR_SHAPE 1   /* a shape violates the contract (message names it, e.g. "rows % 128") */
+#define RB_ERR_ARG 2     /* bad pointer, alignment, dtype or flag */
+#define RB_ERR_CUDA 3    /* a CUDA runtime/driver call failed */
+#define RB_ERR_DEVICE 4  /* the current device is not an sm_100 (B200-class) GPU */
+
+/* Message for the last failing call on this thread. */
+const char* rb_nvfp4_last_error(void);
+
+/* RB_NVFP4_ABI_VERSION of the loaded library. */
+int rb_nvfp4_abi_version(void);
+
+/*
+ * First non-zero status recorded by any kernel of this library on the current device since the
+ * last clear (a bounded device-side wait that ran out); 0 if none.  Synchronises the device.
+ * Test and debugging aid; no counterpart in the reference.
+ */
+int rb_nvfp4_device_status(int clear);
+
+/*
+ * Per-tensor global scale: *gs_out = max(amax(|x|) / (6 * 448), 1e-12) as fp32, one IEEE divide.
+ * Replaces `global_scale_of` (quantize.py:205-213).
+ *   x         : rows x cols elements of `dtype`, row stride `ld` elements (ld >= cols).
+ *   workspace : 8 bytes of device memory, zero before the first call; every call leaves it zero
+ *               again.  Calls that share a workspace must be ordered (same stream).
+ */
+int rb_nvfp4_global_scale(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld, float* gs_out,
+                          void* workspace, void* stream);
+
+/*
+ * NVFP4 quantizer: one pass over x writes the rowblock form, the colblock form, or both.
+ * Replaces `quantize` (quantize.py:672-736) and its two Triton kernels (quantize.py:538-644);
+ * bit-identical to `quantize_reference` / `ref_quantize_rowblock` / `ref_quantize_colblock`
+ * (quantize.py:216-268, :412-433) on codes and scale bytes for round-to-nearest.
+ *   x          : rows x cols of `dtype`, row stride ld elements; rows % 128 == 0, cols % 64 == 0,
+ *                16-byte aligned base and ld*elemsize % 16 == 0.
+ *   gs         : device fp32 global scale (the quantizer divides by 6*gs once per block).
+ *   hadamard   : NULL or a device 16x16 fp32 matrix R; the colblock form quantizes R^T applied to
+ *                every 16-row group (quantize.py:261-262).  Not applied to the rowblock form.
+ *   seed       : device int64 seed for stochastic rounding (read on the device); NULL = round to
+ *                nearest even.  With a seed both forms use stochastic rounding, unbiased in
+ *                distribution (quantize.py:122-138 defines the rounding rule).
+ *   row_packed : NULL or rows x cols/2 bytes;  row_scale: NULL or (rows/128)*(cols/64)*512 bytes.
+ *   col_packed : NULL or cols x rows/2 bytes;  col_scale: NULL or ceil(cols/128)*(rows/64)*512 bytes
+ *                (padding rows are written as zero).
+ * At least one of the two forms must be requested; each form needs both of its pointers.
+ */
+int rb_nvfp4_quantize(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld, const float* gs,
+                      const float* hadamard, const int64_t* seed, void* row_packed, void* row_scale,
+                      void* col_packed, void* col_scale, void* stream);
+
+/*
+ * Block-scaled NVFP4 GEMM on the tcgen05 tensor cores:
+ *   out[i, j] = (alpha_a * alpha_b) * sum_k deq(a)[i, k] * deq(b)[j, k]  (+ bias[j])
+ * with deq() the e2m1 codes times their e4m3 block scales.  Replaces `nvfp4_mm` + `mm`
+ * (quantize.py:359-409: torch._scaled_mm_v2 followed by the global-scale multiply and cast) and
+ * the bias add of linear.py:82-83, fused into one kernel.
+ *   a_packed/a_scale : rowblock-layout operand, m rows, k contraction (a "rows x contraction"
+ *                      NVFP4Tensor, quantize.py:328-356).  b_packed/b_scale: likewise, n rows.
+ *   alpha_a, alpha_b : device fp32 global scales of the two operands (NULL = 1).
+ *   bias             : NULL or n elements of `bias_dtype` (RB_DTYPE_BF16 / RB_DTYPE_F32).
+ *   out              : m x n of `out_dtype`, row stride ldo elements.
+ *   m % 128 == 0, n % 128 == 0, k % 64 == 0.
+ */
+int rb_nvfp4_gemm(const void* a_packed, const void* a_scale, const void* b_packed, const void* b_scale, int64_t m,
+                  int64_t n, int64_t k, const float* alpha_a, const float* alpha_b, const void* bias, int bias_dtype,
+                  void* out, int out_dtype, int64_t ldo, void* stream);
+
+/*
+ * Self-test of the quantizer's division: for i < n, compares the library's correctly rounded
+ * quotient x[i] / d[i] (reciprocal plus two residual corrections) with the IEEE quotient and
+ * counts mismatching bit patterns into *mismatches (device uint32, accumulated).  Test aid; no
+ * counterpart in the reference.
+ */
+int rb_nvfp4_selftest_division(const float* x, const float* d, int64_t n, uint32_t* mismatches, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RADIANCE_NVFP4_H_ */

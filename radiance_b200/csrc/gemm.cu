@@ -1,0 +1,442 @@
+// Block-scaled NVFP4 GEMM for B200 on the 5th-generation tensor cores (tcgen05, sm_100a).
+//
+//   out[i, j] = alpha * sum_k (e2m1(a[i,k]) * e4m3(sa[i, k/16])) * (e2m1(b[j,k]) * e4m3(sb[j, k/16])) (+ bias[j])
+//
+// Replaces torch._scaled_mm_v2 (cuBLASLt) behind radiance's nvfp4_mm/mm
+// (src/radiance/nvfp4/quantize.py:359-409), with the global-scale fold, bias add and output cast
+// of quantize.py:408-409 and linear.py:82-83 fused into the epilogue.
+//
+// Design: one persistent CTA per SM, 6 warps, warp-specialised.
+//   warp 0 (one lane)  : producer.  Per 256-element K step it TMA-loads the A tile (128 rows x
+//                        128 B, 128-byte swizzle), the B tile (256 rows x 128 B) and, with plain
+//                        bulk copies, the matching e4m3 scale atoms.  The scale layout written by
+//                        the quantizer (SWIZZLE_32_4_4: one 512-byte atom per 128 rows x 4 scale
+//                        columns) is exactly what tcgen05.cp.32x128b.warpx4 moves into tensor
+//                        memory, so scales go global -> shared -> TMEM untouched.
+//   warp 1 (one lane)  : MMA issuer.  tcgen05.cp for the scales, then four
+//                        tcgen05.mma.kind::mxf4nvf4.block_scale.scale_vec::4X (128 x 256 x 64) per
+//                        K step into a TMEM accumulator; tcgen05.commit frees the smem stage.
+//   warps 2-5          : epilogue.  tcgen05.ld the accumulator (each warp owns 32 TMEM lanes =
+//                        32 output rows), alpha = ga * gb and bias applied in fp32, one rounding to
+//                        bf16 or fp32, stored straight to global memory.
+// The two accumulator buffers share TMEM columns: buffer 0 is columns [0, 256), buffer 1 is
+// [192, 448), and the scale factors live in [448, 512).  The epilogue drains the shared 64
+// columns first and releases them, so the next tile's MMAs start while the rest drains.
+// No TMA multicast is used (the same kernel serves multi-GPU jobs).
+#include "common.cuh"
+#include "../../include/radiance_nvfp4.h"
+
+namespace rb {
+
+__device__ uint32_t g_gemm_status;
+
+constexpr int kBM = 128;            // tile rows (M) = TMEM lanes
+constexpr int kBN = 256;            // tile cols (N)
+constexpr int kStepBytes = 128;     // packed bytes of one K step (256 e2m1 values)
+constexpr int kStages = 4;
+constexpr int kOverlap = 64;        // TMEM columns shared by the two accumulator buffers
+constexpr int kAcc1Col = kBN - kOverlap;   // 192
+constexpr int kSfaCol = 512 - kOverlap;    // 448: 4 columns per 64-wide K block (16 total)
+constexpr int kSfbCol = kSfaCol + 16;      // 464: 8 columns per K block (32 total)
+constexpr int kGemmThreads = 192;
+constexpr int kEpiChunk = 64;       // accumulator columns per epilogue step
+constexpr int kGroupM = 8;          // raster: tiles visited in groups of 8 M-tiles
+
+struct GemmSmem {
+  uint8_t a[kStages][kBM * kStepBytes];   // 16 KB per stage
+  uint8_t b[kStages][kBN * kStepBytes];   // 32 KB per stage
+  uint8_t sfa[kStages][4 * 512];          // 4 K-blocks x one 128-row atom
+  uint8_t sfb[kStages][8 * 512];          // [row half h][K-block kb] at (4h + kb) * 512
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+  uint64_t acc_full;
+  uint64_t acc_empty;
+  uint64_t drain;
+  uint32_t tmem_base;
+};
+
+struct GemmArgs {
+  int64_t M, N, K;
+  const uint8_t* a_scale;
+  const uint8_t* b_scale;
+  const float* alpha_a;
+  const float* alpha_b;
+  const void* bias;
+  int bias_f32;
+  void* out;
+  int out_f32;
+  int64_t ldo;
+  int tiles_m, tiles_n, n_tiles;
+  int k_steps, k_blocks;   // K/256 rounded up, K/64
+};
+
+// ---------------------------------------------------------------------------------------------
+// tcgen05 wrappers (inline PTX)
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_cp_scale(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+__device__ __forceinline__ void tc_mma_nvf4(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t sfa_tmem, uint32_t sfb_tmem, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.scale_vec::4X [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(
+          d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+
+#define RB_TMEM_LD_X32(taddr, r)                                                                              \
+  asm volatile(                                                                                               \
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "  \
+      "%14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"      \
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),       \
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), \
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]),             \
+        "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),             \
+        "=r"(r[30]), "=r"(r[31])                                                                              \
+      : "r"(taddr))
+
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor, K-major with 128-byte swizzle: 8-row groups 1024 B apart.
+__device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+// Descriptor of one 512-byte scale atom (32 rows x 16 B, no swizzle, 8-row groups 128 B apart).
+__device__ __forceinline__ uint64_t sdesc_scale(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(128 >> 4) << 32) |
+         ((uint64_t)1 << 46);
+}
+// Instruction descriptor: kind::mxf4nvf4, A = B = e2m1 (packed), K-major, ue4m3 scales, M = 128.
+__host__ __device__ constexpr uint32_t idesc_nvf4(int n) {
+  return (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+}
+
+__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int& mt, int& nt) {
+  const int group = t / (kGroupM * tiles_n);
+  const int first_m = group * kGroupM;
+  const int gm = min(tiles_m - first_m, kGroupM);
+  const int r = t - group * kGroupM * tiles_n;
+  mt = first_m + r % gm;
+  nt = r / gm;
+}
+
+__device__ __forceinline__ void st_global_v4(void* p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.global.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+// ---------------------------------------------------------------------------------------------
+// The kernel
+// ---------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                      const GemmArgs g) {
+  extern __shared__ uint8_t smem_raw[];
+  GemmSmem& sm = *reinterpret_cast<GemmSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_my = ((int)blockIdx.x < g.n_tiles) ? (g.n_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], 1);
+    }
+    mbar_init(&sm.acc_full, 1);
+    mbar_init(&sm.acc_empty, 4);
+    mbar_init(&sm.drain, 1);
+    fence_mbar_init();
+    prefetch_tensormap(&tmA);
+    prefetch_tensormap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(&sm.tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int i = 0; i < n_my && ok; ++i) {
+        int mt, nt;
+        tile_coords((int)blockIdx.x + i * (int)gridDim.x, g.tiles_m, g.tiles_n, mt, nt);
+        const bool two_halves = (int64_t)nt * kBN + 128 < g.N;
+        for (int ks = 0; ks < g.k_steps; ++ks) {
+          if (!mbar_wait(&sm.empty[stage], phase ^ 1u)) {
+            record_status(&g_gemm_status, kStatusTimeoutProducer);
+            ok = false;
+            break;
+          }
+          const int nkb = min(4, g.k_blocks - 4 * ks);
+          const uint32_t sf_bytes = (uint32_t)nkb * 512u;
+          mbar_arrive_expect_tx(&sm.full[stage], kBM * kStepBytes + kBN * kStepBytes + sf_bytes * (two_halves ? 3u : 2u));
+          tma_load_2d(sm.a[stage], &tmA, &sm.full[stage], ks * kStepBytes, mt * kBM);
+          tma_load_2d(sm.b[stage], &tmB, &sm.full[stage], ks * kStepBytes, nt * kBN);
+          bulk_load(sm.sfa[stage], g.a_scale + ((int64_t)mt * g.k_blocks + 4 * ks) * 512, sf_bytes, &sm.full[stage]);
+          bulk_load(sm.sfb[stage], g.b_scale + ((int64_t)(2 * nt) * g.k_blocks + 4 * ks) * 512, sf_bytes,
+                    &sm.full[stage]);
+          if (two_halves)
+            bulk_load(sm.sfb[stage] + 4 * 512, g.b_scale + ((int64_t)(2 * nt + 1) * g.k_blocks + 4 * ks) * 512,
+                      sf_bytes, &sm.full[stage]);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int i = 0; i < n_my && ok; ++i) {
+        int mt, nt;
+        tile_coords((int)blockIdx.x + i * (int)gridDim.x, g.tiles_m, g.tiles_n, mt, nt);
+        const int width = (int)min((int64_t)kBN, g.N - (int64_t)nt * kBN);
+        const uint32_t idesc = idesc_nvf4(width);
+        const uint32_t acc = tmem + ((i & 1) ? kAcc1Col : 0);
+        if (i >= 1 && !mbar_wait(&sm.acc_empty, (uint32_t)((i - 1) & 1))) {
+          record_status(&g_gemm_status, kStatusTimeoutEpilogue);
+          break;
+        }
+        tc_fence_after();
+        for (int ks = 0; ks < g.k_steps; ++ks) {
+          if (!mbar_wait(&sm.full[stage], phase)) {
+            record_status(&g_gemm_status, kStatusTimeoutTma);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const int nkb = min(4, g.k_blocks - 4 * ks);
+          const uint32_t sfa_s = smem_u32(sm.sfa[stage]), sfb_s = smem_u32(sm.sfb[stage]);
+          for (int kb = 0; kb < nkb; ++kb) {
+            tc_cp_scale(tmem + kSfaCol + 4 * kb, sdesc_scale(sfa_s + kb * 512));
+            tc_cp_scale(tmem + kSfbCol + 8 * kb, sdesc_scale(sfb_s + kb * 512));
+            if (width > 128) tc_cp_scale(tmem + kSfbCol + 8 * kb + 4, sdesc_scale(sfb_s + (4 + kb) * 512));
+          }
+          const uint32_t a_s = smem_u32(sm.a[stage]), b_s = smem_u32(sm.b[stage]);
+          for (int kb = 0; kb < nkb; ++kb) {
+            tc_mma_nvf4(acc, sdesc_sw128(a_s + 32 * kb), sdesc_sw128(b_s + 32 * kb), idesc, tmem + kSfaCol + 4 * kb,
+                        tmem + kSfbCol + 8 * kb, (ks > 0 || kb > 0) ? 1u : 0u);
+          }
+          tc_commit(&sm.empty[stage]);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (ok) tc_commit(&sm.acc_full);
+      }
+      // Every MMA this thread issued has finished once `drain` completes.
+      tc_commit(&sm.drain);
+      mbar_wait(&sm.drain, 0);
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue (warps 2..5)
+    const int q = warp & 3;  // TMEM lanes 32q .. 32q+31
+    float alpha = 1.0f;
+    if (g.alpha_a != nullptr) alpha = *g.alpha_a;
+    if (g.alpha_b != nullptr) alpha = __fmul_rn(alpha, *g.alpha_b);
+    for (int i = 0; i < n_my; ++i) {
+      int mt, nt;
+      tile_coords((int)blockIdx.x + i * (int)gridDim.x, g.tiles_m, g.tiles_n, mt, nt);
+      const int width = (int)min((int64_t)kBN, g.N - (int64_t)nt * kBN);
+      const int buf = i & 1;
+      const int base_col = buf ? kAcc1Col : 0;
+      if (!mbar_wait(&sm.acc_full, (uint32_t)(i & 1))) {
+        record_status(&g_gemm_status, kStatusTimeoutMma);
+        break;
+      }
+      tc_fence_after();
+      const int nch = width / kEpiChunk;
+      // Chunks of this buffer that lie in the shared columns [192, 256) go first.
+      const int first = (buf == 0) ? ((width == kBN) ? nch - 1 : -1) : 0;
+      if (first < 0 && lane == 0) mbar_arrive(&sm.acc_empty);
+      const int64_t row = (int64_t)mt * kBM + 32 * q + lane;
+      for (int step = 0; step < nch; ++step) {
+        const int c = (first < 0) ? step : (step == 0 ? first : (buf == 0 ? step - 1 : step));
+        uint32_t r[kEpiChunk];
+        const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(base_col + c * kEpiChunk);
+        RB_TMEM_LD_X32(taddr, r);
+        RB_TMEM_LD_X32(taddr + 32, (r + 32));
+        tmem_ld_wait();
+        if (step == 0 && first >= 0) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sm.acc_empty);
+        }
+        const int64_t col0 = (int64_t)nt * kBN + c * kEpiChunk;
+        float v[kEpiChunk];
+#pragma unroll
+        for (int j = 0; j < kEpiChunk; ++j) v[j] = __fmul_rn(__uint_as_float(r[j]), alpha);
+        if (g.bias != nullptr) {
+          if (g.bias_f32) {
+            const float* bp = reinterpret_cast<const float*>(g.bias) + col0;
+#pragma unroll
+            for (int j = 0; j < kEpiChunk; ++j) v[j] = __fadd_rn(v[j], __ldg(bp + j));
+          } else {
+            const __nv_bfloat16* bp = reinterpret_cast<const __nv_bfloat16*>(g.bias) + col0;
+#pragma unroll
+            for (int j = 0; j < kEpiChunk; ++j) v[j] = __fadd_rn(v[j], __bfloat162float(bp[j]));
+          }
+        }
+        if (g.out_f32) {
+          float* op = reinterpret_cast<float*>(g.out) + row * g.ldo + col0;
+#pragma unroll
+          for (int j = 0; j < kEpiChunk; j += 4)
+            st_global_v4(op + j, __float_as_uint(v[j]), __float_as_uint(v[j + 1]), __float_as_uint(v[j + 2]),
+                         __float_as_uint(v[j + 3]));
+        } else {
+          __nv_bfloat16* op = reinterpret_cast<__nv_bfloat16*>(g.out) + row * g.ldo + col0;
+#pragma unroll
+          for (int j = 0; j < kEpiChunk; j += 8)
+            st_global_v4(op + j, pack_bf16x2(v[j], v[j + 1]), pack_bf16x2(v[j + 2], v[j + 3]),
+                         pack_bf16x2(v[j + 4], v[j + 5]), pack_bf16x2(v[j + 6], v[j + 7]));
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
+}  // namespace rb
+
+// =============================================================================================
+// Host entry points
+// =============================================================================================
+using namespace rb;
+
+extern "C" {
+
+uint32_t rb_internal_gemm_status(int clear) {
+  uint32_t v = 0;
+  cudaDeviceSynchronize();
+  cudaMemcpyFromSymbol(&v, rb::g_gemm_status, sizeof(v));
+  if (clear) {
+    const uint32_t z = 0;
+    cudaMemcpyToSymbol(rb::g_gemm_status, &z, sizeof(z));
+  }
+  return v;
+}
+
+int rb_nvfp4_gemm(const void* a_packed, const void* a_scale, const void* b_packed, const void* b_scale, int64_t m,
+                  int64_t n, int64_t k, const float* alpha_a, const float* alpha_b, const void* bias, int bias_dtype,
+                  void* out, int out_dtype, int64_t ldo, void* stream) {
+  if (m <= 0 || n <= 0 || k <= 0 || m % 128 != 0 || n % 128 != 0 || k % 64 != 0) {
+    rb_host::set_error("nvfp4 gemm needs m %% 128 == 0, n %% 128 == 0 and k %% 64 == 0, got (%lld, %lld, %lld)",
+                       (long long)m, (long long)n, (long long)k);
+    return RB_ERR_SHAPE;
+  }
+  if (a_packed == nullptr || a_scale == nullptr || b_packed == nullptr || b_scale == nullptr || out == nullptr) {
+    rb_host::set_error("nvfp4 gemm: null pointer argument");
+    return RB_ERR_ARG;
+  }
+  if (out_dtype != RB_OUT_BF16 && out_dtype != RB_OUT_F32) {
+    rb_host::set_error("nvfp4 gemm: unsupported output dtype %d", out_dtype);
+    return RB_ERR_ARG;
+  }
+  if (bias != nullptr && bias_dtype != RB_DTYPE_BF16 && bias_dtype != RB_DTYPE_F32) {
+    rb_host::set_error("nvfp4 gemm: unsupported bias dtype %d", bias_dtype);
+    return RB_ERR_ARG;
+  }
+  const int oesize = out_dtype == RB_OUT_F32 ? 4 : 2;
+  const auto misaligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) != 0; };
+  if (misaligned(a_packed) || misaligned(b_packed) || misaligned(a_scale) || misaligned(b_scale) || misaligned(out) ||
+      ldo < n || ((uint64_t)ldo * oesize) % 16 != 0) {
+    rb_host::set_error("nvfp4 gemm: operands and output must be 16-byte aligned with 16-byte row strides");
+    return RB_ERR_ARG;
+  }
+  int dev = rb_host::current_device();
+  int major = 0;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  if (major != 10) {
+    rb_host::set_error("nvfp4 gemm: the current device is not an sm_100 GPU");
+    return RB_ERR_DEVICE;
+  }
+  CUtensorMap tmA, tmB;
+  if (!rb_host::make_tmap_2d(&tmA, a_packed, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)(k / 2), (uint64_t)m,
+                             (uint64_t)(k / 2), kStepBytes, kBM, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !rb_host::make_tmap_2d(&tmB, b_packed, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)(k / 2), (uint64_t)n,
+                             (uint64_t)(k / 2), kStepBytes, kBN, CU_TENSOR_MAP_SWIZZLE_128B))
+    return RB_ERR_CUDA;
+  GemmArgs g;
+  g.M = m;
+  g.N = n;
+  g.K = k;
+  g.a_scale = reinterpret_cast<const uint8_t*>(a_scale);
+  g.b_scale = reinterpret_cast<const uint8_t*>(b_scale);
+  g.alpha_a = alpha_a;
+  g.alpha_b = alpha_b;
+  g.bias = bias;
+  g.bias_f32 = bias_dtype == RB_DTYPE_F32;
+  g.out = out;
+  g.out_f32 = out_dtype == RB_OUT_F32;
+  g.ldo = ldo;
+  g.tiles_m = (int)(m / kBM);
+  g.tiles_n = (int)((n + kBN - 1) / kBN);
+  g.n_tiles = g.tiles_m * g.tiles_n;
+  g.k_blocks = (int)(k / 64);
+  g.k_steps = (g.k_blocks + 3) / 4;
+  const size_t smem = sizeof(GemmSmem) + 1024;
+  static bool configured[64] = {false};
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    if (cudaFuncSetAttribute(nvfp4_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess) {
+      rb_host::set_error("cudaFuncSetAttribute(gemm) failed: %s", cudaGetErrorString(cudaGetLastError()));
+      return RB_ERR_CUDA;
+    }
+    configured[dev] = true;
+  }
+  const int sms = rb_host::num_sms(dev);
+  const int grid = g.n_tiles < sms ? g.n_tiles : sms;
+  nvfp4_gemm_kernel<<<grid, kGemmThreads, smem, reinterpret_cast<cudaStream_t>(stream)>>>(tmA, tmB, g);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    rb_host::set_error("nvfp4 gemm launch failed: %s", cudaGetErrorString(e));
+    return RB_ERR_CUDA;
+  }
+  return RB_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,789 @@
+// NVFP4 quantizer and global-scale (amax) kernels for B200 (sm_100a).
+//
+// Semantics follow radiance's pure-torch emulation, src/radiance/nvfp4/quantize.py:
+//   global scale  gs    = max(amax|x| / 2688, 1e-12)                         (:205-213)
+//   block scale   s     = clamp(amax_block / (6*gs), 1e-12, 448), rounded UP to e4m3 (:160-202)
+//   divisor       D     = e4m3(s) * gs   (one fp32 multiply; 1*gs for an all-zero block)
+//   code          q     = RN(x / D), encoded round-to-nearest-even on the e2m1 grid (:93-139)
+//   colblock + R  y_i   = sum_j R[j][i] * x_j, j = 0..15 left to right in fp32 (:261-262)
+// and the codes/scale bytes are bit-identical to the reference for round-to-nearest.
+//
+// Design (one persistent CTA pair per SM, 256 threads each):
+//   * A 128 x 64 input tile is brought into shared memory by TMA (128-byte swizzle, so both the
+//     row-major and the column-major walks below are bank-conflict free), S tiles in flight.
+//   * The rowblock form reads each 16-element run along a row; the colblock form reads 16 rows of
+//     two adjacent columns and works on float2 pairs with Blackwell's packed f32x2 FMA path.
+//   * x / D is never computed with a divide instruction.  Each block looks up D and
+//     Y = RN(1/D) in a 127-entry table (one entry per e4m3 byte, built per CTA with the IEEE
+//     reciprocal) and refines q0 = x*Y with two residual corrections r = x - q*D, q += r*Y, each a
+//     single fused multiply-add.  That is Markstein's correctly rounded division (P. Markstein,
+//     "Computation of elementary functions on the IBM RISC System/6000 processor", IBM J. R&D
+//     34(1), 1990; see also Muller et al., Handbook of Floating-Point Arithmetic, ch. 4): after the
+//     first correction q is faithful, and a faithful q with a correctly rounded reciprocal gives
+//     the correctly rounded quotient after the second.  It holds while the residual x - q*d is a
+//     normal number, i.e. for every quotient above ~1e-20 -- far below 0.25, the smallest quotient
+//     with a non-zero e2m1 code.  Smaller quotients only decide the sign bit of a zero code, and
+//     that sign is fixed up exactly (see underflow_mask8).
+//     rb_nvfp4_selftest_division checks the identity against the IEEE divide on the GPU.
+//   * Codes come from the hardware round-to-nearest-even convert cvt.rn.satfinite.e2m1x2.f32,
+//     which rounds exactly like the reference's comparison ladder (ties to the even code).
+//   * The Hadamard fast path: radiance's rotation is a Sylvester matrix with row signs, scaled by
+//     1/4 (quantize.py:647-659).  Then y_i = 1/4 * sum_j syl(j,i) * (s_j x_j) with the same
+//     left-to-right rounding, since scaling by a power of two commutes with every rounding; the
+//     kernel sums the sign-flipped inputs with packed adds and folds the 1/4 into the divisor.
+//     Any other 16x16 matrix takes a general path (multiply then add, j = 0..15).
+#include <stdio.h>
+
+#include "common.cuh"
+#include "../../include/radiance_nvfp4.h"
+
+namespace rb {
+
+__device__ uint32_t g_quant_status;
+
+constexpr int kQThreads = 256;
+constexpr int kQRows = 128;
+constexpr int kQCols = 64;
+
+struct QuantArgs {
+  int64_t M, K;
+  const float* gs;
+  const float* hadamard;
+  const int64_t* seed;
+  uint8_t* row_packed;
+  uint8_t* row_scale;
+  uint8_t* col_packed;
+  uint8_t* col_scale;
+  int tiles_k;
+  int n_tiles;
+};
+
+template <bool F32IN>
+struct QCfg {
+  static constexpr int kTileBytes = F32IN ? 32768 : 16384;
+  static constexpr int kStages = F32IN ? 3 : 4;
+};
+
+struct QHeader {
+  uint64_t full[4];
+  float2 table[128];  // (D, RN(1/D)) for each e4m3 byte; entry 127 unused
+  float had[256];
+  uint32_t sign_mask[16];
+  int had_fast;
+};
+
+template <bool F32IN>
+constexpr size_t quant_smem_bytes() {
+  return 1024 + (size_t)QCfg<F32IN>::kTileBytes * QCfg<F32IN>::kStages + sizeof(QHeader);
+}
+
+// ---------------------------------------------------------------------------------------------
+// Scalar helpers
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ float e4m3_value(uint32_t b) {
+  const uint32_t e = b >> 3, m = b & 7u;
+  if (e == 0) return __uint2float_rn(m) * 0.001953125f;  // m * 2^-9 (subnormal)
+  return __uint_as_float(((e + 120u) << 23) | (m << 20));
+}
+
+// Smallest e4m3 byte whose value is >= s, for s in [1e-12, 448] (quantize.py:180-184).
+__device__ __forceinline__ uint32_t e4m3_ceil_byte(float s) {
+  if (s >= 0.015625f) {
+    const uint32_t b = (__float_as_uint(s) + 0xFFFFFu) & 0xFFF00000u;
+    return (b >> 20) - 960u;
+  }
+  return (uint32_t)ceilf(s * 512.0f);
+}
+
+__device__ __forceinline__ uint32_t block_scale_byte(float amax, float denom) {
+  float s = __fdiv_rn(amax, denom);
+  s = fminf(fmaxf(s, 1e-12f), 448.0f);
+  return e4m3_ceil_byte(s);
+}
+
+// q = RN(x / d) for a float2, given nd = -d and y = RN(1/d) (Markstein, two corrections).
+__device__ __forceinline__ float2 div2(float2 x, float2 nd, float2 y) {
+  float2 q = __fmul2_rn(x, y);
+  float2 r = __ffma2_rn(q, nd, x);
+  q = __ffma2_rn(r, y, q);
+  r = __ffma2_rn(q, nd, x);
+  return __ffma2_rn(r, y, q);
+}
+
+// Eight quotients (element order a.x, a.y, b.x, ...) -> one 32-bit word of packed e2m1 codes,
+// element 0 in the low nibble.
+__device__ __forceinline__ uint32_t e2m1x8(float e0, float e1, float e2, float e3, float e4, float e5, float e6,
+                                           float e7) {
+  uint32_t out;
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b1, %4, %3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b2, %6, %5;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b3, %8, %7;\n\t"
+      "mov.b32 %0, {b0, b1, b2, b3};\n\t}"
+      : "=r"(out)
+      : "f"(e0), "f"(e1), "f"(e2), "f"(e3), "f"(e4), "f"(e5), "f"(e6), "f"(e7));
+  return out;
+}
+
+// Counter-based random bits: the PCG output permutation applied to one LCG step of the input
+// (M. O'Neill, "PCG: a family of simple fast space-efficient statistically good algorithms for
+// random number generation", 2014; used as a hash in Jarzynski & Olano, "Hash Functions for GPU
+// Rendering", JCGT 9(3), 2020).
+__device__ __forceinline__ uint32_t pcg_hash(uint32_t v) {
+  const uint32_t s = v * 747796405u + 2891336453u;
+  const uint32_t w = ((s >> ((s >> 28u) + 4u)) ^ s) * 277803737u;
+  return (w >> 22u) ^ w;
+}
+
+// Stochastic rounding of a quotient q (already RN(x/D)) to a signed e2m1 code (quantize.py:122-138):
+// lo = the grid level at or below min(|q|, 6), round up with probability (a - lo) / (hi - lo).
+// The fraction is read straight from the fp32 bits: on [1, 8) the e2m1 grid keeps one mantissa
+// bit, so the 22 bits below it are the fraction in units of 2^-22; [0, 1) is shifted to [1, 2),
+// where the grid spacing (0.5) is the same.  The draw uses 22 random bits.
+__device__ __forceinline__ uint32_t sr_code(float q, uint32_t rnd) {
+  const float a = fminf(fabsf(q), 6.0f);
+  const bool sub = a < 1.0f;
+  const float t = sub ? __fadd_rn(a, 1.0f) : a;
+  const uint32_t bits = __float_as_uint(t);
+  uint32_t code = (bits >> 22) - (sub ? 254u : 252u);
+  code += ((rnd >> 10) < (bits & 0x3FFFFFu)) ? 1u : 0u;
+  return code | (q < 0.0f ? 8u : 0u);
+}
+
+__device__ __forceinline__ uint32_t sr_key(const int64_t* seed) {
+  const uint64_t s = (uint64_t)(*seed);
+  return pcg_hash((uint32_t)s ^ 0x9E3779B9u) ^ pcg_hash((uint32_t)(s >> 32) + 0x7F4A7C15u);
+}
+
+// Random bits for element index `lin` (row * cols + col of the original tensor, the same index
+// for both layouts, as in quantize.py:564-567 and :620-623).
+__device__ __forceinline__ uint32_t sr_bits(uint32_t key, uint64_t lin) {
+  const uint32_t hi = (uint32_t)(lin >> 32);
+  return pcg_hash((uint32_t)lin ^ key ^ (hi ? pcg_hash(hi) : 0u));
+}
+
+// A quotient that rounds to +-0 must produce nibble 0 (the reference's sign is `q < 0`, false for
+// -0).  Values with |v| <= T0 = RD(Dv * 2^-150) are exactly those; they can only exist in a block
+// whose divisor is large compared with the smallest non-zero input magnitude, so this runs only
+// for such (rare) blocks.
+__device__ __forceinline__ uint32_t underflow_mask8(const float* v, int stride, float dv) {
+  const float t0 = __fmul_rd(dv * 2.98023223876953125e-8f /* 2^-25 */, 2.35098870164457501594e-38f /* 2^-125 */);
+  uint32_t keep = 0xFFFFFFFFu;
+#pragma unroll
+  for (int e = 0; e < 8; ++e)
+    if (fabsf(v[e * stride]) <= t0) keep &= ~(0xFu << (4 * e));
+  return keep;
+}
+
+// ---------------------------------------------------------------------------------------------
+// Shared-memory reads of the swizzled tile
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ uint2 lds64(uint32_t addr) {
+  uint2 v;
+  asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+  return v;
+}
+
+__device__ __forceinline__ float2 bf16x2_to_float2(uint32_t w) {
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+}
+
+__device__ __forceinline__ void st_global_v2(void* p, uint32_t a, uint32_t b) {
+  asm volatile("st.global.v2.b32 [%0], {%1, %2};" ::"l"(p), "r"(a), "r"(b) : "memory");
+}
+
+// Byte offset of scale (r, c) in the SWIZZLE_32_4_4 layout with `nct` 4-column tiles per 128-row
+// tile (quantize.py:293-305).
+__device__ __forceinline__ int64_t blocked_offset(int64_t r, int64_t c, int64_t nct) {
+  return ((r >> 7) * nct + (c >> 2)) * 512 + (r & 31) * 16 + ((r & 127) >> 5) * 4 + (c & 3);
+}
+
+// ---------------------------------------------------------------------------------------------
+// The rowblock form: thread (warp w, lane l) handles rows 16w + 8p + l/4 (p = 0, 1), block l % 4.
+// ---------------------------------------------------------------------------------------------
+template <bool F32IN, bool SR>
+__device__ __forceinline__ void row_blocks(uint32_t tile, const QHeader* hdr, const QuantArgs& a, int64_t m0,
+                                           int64_t k0, int mt, int kt, float denom, uint32_t key) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = lane & 3;
+#pragma unroll
+  for (int p = 0; p < 2; ++p) {
+    const int r = 16 * warp + 8 * p + (lane >> 2);
+    float2 v[8];
+    if constexpr (!F32IN) {
+      const uint32_t row = tile + r * 128;
+      const uint4 c0 = lds128(row + (((2 * b) ^ (r & 7)) << 4));
+      const uint4 c1 = lds128(row + (((2 * b + 1) ^ (r & 7)) << 4));
+      v[0] = bf16x2_to_float2(c0.x); v[1] = bf16x2_to_float2(c0.y);
+      v[2] = bf16x2_to_float2(c0.z); v[3] = bf16x2_to_float2(c0.w);
+      v[4] = bf16x2_to_float2(c1.x); v[5] = bf16x2_to_float2(c1.y);
+      v[6] = bf16x2_to_float2(c1.z); v[7] = bf16x2_to_float2(c1.w);
+    } else {
+      const uint32_t row = tile + (b >> 1) * 16384 + r * 128;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const uint4 w = lds128(row + ((((b & 1) * 4 + c) ^ (r & 7)) << 4));
+        v[2 * c] = make_float2(__uint_as_float(w.x), __uint_as_float(w.y));
+        v[2 * c + 1] = make_float2(__uint_as_float(w.z), __uint_as_float(w.w));
+      }
+    }
+    float amax = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fmaxf(fabsf(v[e].x), fabsf(v[e].y)));
+    const uint32_t sbyte = block_scale_byte(amax, denom);
+    const float2 dy = hdr->table[sbyte];
+    const float2 nd = make_float2(-dy.x, -dy.x), yy = make_float2(dy.y, dy.y);
+    float2 q[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) q[e] = div2(v[e], nd, yy);
+    uint32_t w0, w1;
+    if constexpr (SR) {
+      const uint64_t lin0 = (uint64_t)(m0 + r) * (uint64_t)a.K + (uint64_t)(k0 + 16 * b);
+      uint32_t c[16];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        c[2 * e] = sr_code(q[e].x, sr_bits(key, lin0 + 2 * e));
+        c[2 * e + 1] = sr_code(q[e].y, sr_bits(key, lin0 + 2 * e + 1));
+      }
+      w0 = w1 = 0;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        w0 |= c[e] << (4 * e);
+        w1 |= c[8 + e] << (4 * e);
+      }
+    } else {
+      w0 = e2m1x8(q[0].x, q[0].y, q[1].x, q[1].y, q[2].x, q[2].y, q[3].x, q[3].y);
+      w1 = e2m1x8(q[4].x, q[4].y, q[5].x, q[5].y, q[6].x, q[6].y, q[7].x, q[7].y);
+    }
+    const float risk = F32IN ? 1.0f : 65536.0f;
+    if (dy.x >= risk) {
+      w0 &= underflow_mask8(&v[0].x, 1, dy.x);
+      w1 &= underflow_mask8(&v[4].x, 1, dy.x);
+    }
+    st_global_v2(a.row_packed + (m0 + r) * (a.K >> 1) + (k0 >> 1) + 8 * b, w0, w1);
+    // Gather the four block scales of this row (lanes l..l+3) into one 32-bit store.
+    uint32_t s4 = sbyte;
+    s4 |= __shfl_down_sync(0xFFFFFFFFu, sbyte, 1) << 8;
+    s4 |= __shfl_down_sync(0xFFFFFFFFu, sbyte, 2) << 16;
+    s4 |= __shfl_down_sync(0xFFFFFFFFu, sbyte, 3) << 24;
+    if (b == 0) {
+      uint8_t* atom = a.row_scale + ((int64_t)mt * a.tiles_k + kt) * 512;
+      *reinterpret_cast<uint32_t*>(atom + (r & 31) * 16 + (r >> 5) * 4) = s4;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// The colblock form: thread (warp g, lane cp) handles rows 16g..16g+15 of columns 2cp, 2cp+1.
+// ---------------------------------------------------------------------------------------------
+template <bool F32IN, bool HAD, bool SR>
+__device__ __forceinline__ void col_unit(uint32_t tile, const QHeader* hdr, const QuantArgs& a, int64_t m0,
+                                         int64_t k0, float denom, uint32_t key) {
+  const int g = threadIdx.x >> 5, cp = threadIdx.x & 31;
+  float2 v[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const int r = 16 * g + j;
+    uint32_t sm = 0;
+    if constexpr (HAD) sm = hdr->had_fast ? hdr->sign_mask[j] : 0u;
+    if constexpr (!F32IN) {
+      uint32_t w = lds32(tile + r * 128 + ((((cp >> 2) ^ (j & 7)) << 4) | ((cp & 3) << 2)));
+      v[j] = bf16x2_to_float2(w ^ (sm & 0x80008000u));
+    } else {
+      const int cpp = cp & 15;
+      uint2 w = lds64(tile + (cp >> 4) * 16384 + r * 128 + ((((cpp >> 1) ^ (j & 7)) << 4) | ((cpp & 1) << 3)));
+      v[j] = make_float2(__uint_as_float(w.x ^ (sm & 0x80000000u)), __uint_as_float(w.y ^ (sm & 0x80000000u)));
+    }
+  }
+  float scale_fold = 1.0f;  // divisor multiplier: 4 on the Hadamard fast path (y = acc / 4)
+  if constexpr (HAD) {
+    float2 y[16];
+    if (hdr->had_fast) {
+      const float2 pos = make_float2(1.0f, 1.0f), neg = make_float2(-1.0f, -1.0f);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        float2 acc = v[0];
+#pragma unroll
+        for (int j = 1; j < 16; ++j) acc = __ffma2_rn(v[j], (__popc(i & j) & 1) ? neg : pos, acc);
+        y[i] = acc;
+      }
+      scale_fold = 4.0f;
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        float h = hdr->had[i];
+        float2 acc = make_float2(__fmul_rn(h, v[0].x), __fmul_rn(h, v[0].y));
+#pragma unroll
+        for (int j = 1; j < 16; ++j) {
+          h = hdr->had[j * 16 + i];
+          acc.x = __fadd_rn(acc.x, __fmul_rn(h, v[j].x));
+          acc.y = __fadd_rn(acc.y, __fmul_rn(h, v[j].y));
+        }
+        y[i] = acc;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = y[i];
+  }
+  float ax = 0.0f, ay = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    ax = fmaxf(ax, fabsf(v[i].x));
+    ay = fmaxf(ay, fabsf(v[i].y));
+  }
+  const float unfold = 1.0f / scale_fold;  // exact (1 or 1/4)
+  const uint32_t bx = block_scale_byte(ax * unfold, denom);
+  const uint32_t by = block_scale_byte(ay * unfold, denom);
+  const float2 tx = hdr->table[bx], ty = hdr->table[by];
+  const float dx = tx.x * scale_fold, dyv = ty.x * scale_fold;
+  const float2 nd = make_float2(-dx, -dyv), yy = make_float2(tx.y * unfold, ty.y * unfold);
+  float2 q[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) q[i] = div2(v[i], nd, yy);
+  uint32_t wx0, wx1, wy0, wy1;
+  if constexpr (SR) {
+    const uint64_t lin0 = (uint64_t)(m0 + 16 * g) * (uint64_t)a.K + (uint64_t)(k0 + 2 * cp);
+    wx0 = wx1 = wy0 = wy1 = 0;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const uint64_t lin = lin0 + (uint64_t)i * (uint64_t)a.K;
+      const uint32_t cx = sr_code(q[i].x, sr_bits(key, lin));
+      const uint32_t cy = sr_code(q[i].y, sr_bits(key, lin + 1));
+      if (i < 8) {
+        wx0 |= cx << (4 * i);
+        wy0 |= cy << (4 * i);
+      } else {
+        wx1 |= cx << (4 * (i - 8));
+        wy1 |= cy << (4 * (i - 8));
+      }
+    }
+  } else {
+    wx0 = e2m1x8(q[0].x, q[1].x, q[2].x, q[3].x, q[4].x, q[5].x, q[6].x, q[7].x);
+    wx1 = e2m1x8(q[8].x, q[9].x, q[10].x, q[11].x, q[12].x, q[13].x, q[14].x, q[15].x);
+    wy0 = e2m1x8(q[0].y, q[1].y, q[2].y, q[3].y, q[4].y, q[5].y, q[6].y, q[7].y);
+    wy1 = e2m1x8(q[8].y, q[9].y, q[10].y, q[11].y, q[12].y, q[13].y, q[14].y, q[15].y);
+  }
+  // Smallest non-zero |v|: 2^-133 for bf16 inputs and sums of them, 2^-149 otherwise.
+  const float risk = (F32IN || (HAD && !hdr->had_fast)) ? 1.0f : 65536.0f;
+  if (dx >= risk) {
+    wx0 &= underflow_mask8(&v[0].x, 2, dx);
+    wx1 &= underflow_mask8(&v[8].x, 2, dx);
+  }
+  if (dyv >= risk) {
+    wy0 &= underflow_mask8(&v[0].y, 2, dyv);
+    wy1 &= underflow_mask8(&v[8].y, 2, dyv);
+  }
+  const int64_t kx = k0 + 2 * cp;
+  const int64_t half_m = a.M >> 1;
+  uint8_t* dst = a.col_packed + kx * half_m + ((m0 + 16 * g) >> 1);
+  st_global_v2(dst, wx0, wx1);
+  st_global_v2(dst + half_m, wy0, wy1);
+  const int64_t nct = a.M >> 6;  // 4-column scale tiles per 128-row tile (M/16 scale columns)
+  const int64_t mb = (m0 >> 4) + g;
+  a.col_scale[blocked_offset(kx, mb, nct)] = (uint8_t)bx;
+  a.col_scale[blocked_offset(kx + 1, mb, nct)] = (uint8_t)by;
+}
+
+// ---------------------------------------------------------------------------------------------
+// The kernel
+// ---------------------------------------------------------------------------------------------
+template <bool F32IN, bool DO_ROW, bool DO_COL, bool HAD, bool SR>
+__global__ void __launch_bounds__(kQThreads, 1)
+    nvfp4_quantize_kernel(const __grid_constant__ CUtensorMap tmap, const QuantArgs a) {
+  using Cfg = QCfg<F32IN>;
+  constexpr int S = Cfg::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  QHeader* hdr = reinterpret_cast<QHeader*>(smem + (size_t)Cfg::kTileBytes * S);
+  const int tid = threadIdx.x;
+
+  if ((int)blockIdx.x >= a.n_tiles) return;
+  const int n_my = (a.n_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+
+  if (tid == 0) {
+    for (int s = 0; s < S; ++s) mbar_init(&hdr->full[s], 1);
+    fence_mbar_init();
+    prefetch_tensormap(&tmap);
+  }
+  const float gs = *a.gs;
+  const float denom = __fmul_rn(6.0f, gs);
+  if (tid < 127) {
+    const float d = __fmul_rn(e4m3_value(tid), gs);
+    hdr->table[tid] = make_float2(d, __frcp_rn(d));
+  }
+  if constexpr (HAD) {
+    hdr->had[tid] = a.hadamard[tid];
+  }
+  uint32_t key = 0;
+  if constexpr (SR) key = sr_key(a.seed);
+  __syncthreads();
+  if constexpr (HAD) {
+    // Is R = (Sylvester / 4) with row signs?  Then take the add-only fast path.
+    if (tid < 32) {
+      bool ok = true;
+      for (int e = tid; e < 256; e += 32) {
+        const int j = e >> 4, i = e & 15;
+        const float rj = hdr->had[j * 16];
+        const float want = (__popc(i & j) & 1) ? -rj : rj;
+        ok = ok && (hdr->had[e] == want) && (fabsf(rj) == 0.25f);
+      }
+      ok = __all_sync(0xFFFFFFFFu, ok);
+      if (tid < 16) hdr->sign_mask[tid] = (hdr->had[tid * 16] < 0.0f) ? 0xFFFFFFFFu : 0u;
+      if (tid == 0) hdr->had_fast = ok ? 1 : 0;
+    }
+    __syncthreads();
+  }
+
+  auto issue = [&](int it) {
+    const int s = it % S;
+    const int t = (int)blockIdx.x + it * (int)gridDim.x;
+    const int mt = t / a.tiles_k, kt = t - mt * a.tiles_k;
+    uint8_t* dst = smem + (size_t)s * Cfg::kTileBytes;
+    mbar_arrive_expect_tx(&hdr->full[s], Cfg::kTileBytes);
+    if constexpr (!F32IN) {
+      tma_load_2d(dst, &tmap, &hdr->full[s], kt * kQCols, mt * kQRows);
+    } else {
+      tma_load_2d(dst, &tmap, &hdr->full[s], kt * kQCols, mt * kQRows);
+      tma_load_2d(dst + 16384, &tmap, &hdr->full[s], kt * kQCols + 32, mt * kQRows);
+    }
+  };
+  if (tid == 0) {
+    for (int it = 0; it < S && it < n_my; ++it) issue(it);
+  }
+
+  for (int it = 0; it < n_my; ++it) {
+    const int s = it % S;
+    const bool ok = mbar_wait(&hdr->full[s], (uint32_t)((it / S) & 1));
+    // Every thread has finished tile it-1 once past this barrier, so its stage may be refilled.
+    if (__syncthreads_or(!ok)) {
+      if (tid == 0) record_status(&g_quant_status, kStatusTimeoutTma);
+      return;
+    }
+    if (tid == 0 && it >= 1 && it - 1 + S < n_my) issue(it - 1 + S);
+
+    const int t = (int)blockIdx.x + it * (int)gridDim.x;
+    const int mt = t / a.tiles_k, kt = t - mt * a.tiles_k;
+    const int64_t m0 = (int64_t)mt * kQRows, k0 = (int64_t)kt * kQCols;
+    const uint32_t tile = smem_u32(smem + (size_t)s * Cfg::kTileBytes);
+    if constexpr (DO_COL) {
+      col_unit<F32IN, HAD, SR>(tile, hdr, a, m0, k0, denom, key);
+      // The last 64-column tile of a K that is not a multiple of 128 owns the zero padding of
+      // the colblock scale tiles (rows K..K+63 of the last 128-row scale tile).
+      if ((a.K & 127) != 0 && kt == a.tiles_k - 1 && tid < 64) {
+        const int64_t atom = (k0 >> 7) * (a.M >> 6) + 2 * mt + (tid >> 5);
+        st_global_v2(a.col_scale + atom * 512 + (tid & 31) * 16 + 8, 0u, 0u);
+      }
+    }
+    if constexpr (DO_ROW) row_blocks<F32IN, SR>(tile, hdr, a, m0, k0, mt, kt, denom, key);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// amax -> global scale
+// ---------------------------------------------------------------------------------------------
+template <bool F32IN>
+__global__ void __launch_bounds__(512) global_scale_kernel(const void* x, int64_t rows, int64_t cols, int64_t ld,
+                                                           uint32_t* ws, float* gs_out) {
+  uint32_t m = 0;  // max of |x| bit patterns (non-negative floats order like their bits)
+  const int64_t gtid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const bool flat = (ld == cols) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
+  if (flat) {
+    const int64_t n = rows * cols;
+    constexpr int kPer = F32IN ? 4 : 8;
+    const int64_t nv = n / kPer;
+    const uint4* xv = reinterpret_cast<const uint4*>(x);
+    int64_t i = gtid;
+    for (; i + 3 * stride < nv; i += 4 * stride) {
+      uint4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[u] = __ldg(xv + i + u * stride);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if constexpr (F32IN) {
+          m = max(m, max(max(v[u].x & 0x7FFFFFFFu, v[u].y & 0x7FFFFFFFu), max(v[u].z & 0x7FFFFFFFu, v[u].w & 0x7FFFFFFFu)));
+        } else {
+          m = __vmaxu2(m, __vmaxu2(__vmaxu2(v[u].x & 0x7FFF7FFFu, v[u].y & 0x7FFF7FFFu),
+                                   __vmaxu2(v[u].z & 0x7FFF7FFFu, v[u].w & 0x7FFF7FFFu)));
+        }
+      }
+    }
+    for (; i < nv; i += stride) {
+      const uint4 v = __ldg(xv + i);
+      if constexpr (F32IN) {
+        m = max(m, max(max(v.x & 0x7FFFFFFFu, v.y & 0x7FFFFFFFu), max(v.z & 0x7FFFFFFFu, v.w & 0x7FFFFFFFu)));
+      } else {
+        m = __vmaxu2(m, __vmaxu2(__vmaxu2(v.x & 0x7FFF7FFFu, v.y & 0x7FFF7FFFu), __vmaxu2(v.z & 0x7FFF7FFFu, v.w & 0x7FFF7FFFu)));
+      }
+    }
+    for (int64_t e = nv * kPer + gtid; e < n; e += stride) {
+      if constexpr (F32IN) m = max(m, reinterpret_cast<const uint32_t*>(x)[e] & 0x7FFFFFFFu);
+      else m = max(m, (uint32_t)(reinterpret_cast<const uint16_t*>(x)[e] & 0x7FFFu));
+    }
+  } else {
+    for (int64_t e = gtid; e < rows * cols; e += stride) {
+      const int64_t r = e / cols, c = e - r * cols;
+      if constexpr (F32IN) m = max(m, reinterpret_cast<const uint32_t*>(x)[r * ld + c] & 0x7FFFFFFFu);
+      else m = max(m, (uint32_t)(reinterpret_cast<const uint16_t*>(x)[r * ld + c] & 0x7FFFu));
+    }
+  }
+  if constexpr (!F32IN) m = max(m & 0xFFFFu, m >> 16) << 16;  // bf16 bits -> fp32 bits
+  m = __reduce_max_sync(0xFFFFFFFFu, m);
+  __shared__ uint32_t red[16];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = m;
+  __syncthreads();
+  if (warp == 0) {
+    m = lane < (int)(blockDim.x >> 5) ? red[lane] : 0u;
+    m = __reduce_max_sync(0xFFFFFFFFu, m);
+    if (lane == 0) {
+      atomicMax(&ws[0], m);
+      __threadfence();
+      const uint32_t ticket = atomicAdd(&ws[1], 1u);
+      if (ticket == gridDim.x - 1) {
+        __threadfence();
+        const uint32_t mb = atomicExch(&ws[0], 0u);
+        atomicExch(&ws[1], 0u);
+        float gs = __fdiv_rn(__uint_as_float(mb), 2688.0f);
+        gs = (gs < 1e-12f) ? 1e-12f : gs;  // clamp(min=1e-12); NaN passes through as in torch
+        *gs_out = gs;
+      }
+    }
+  }
+}
+
+__global__ void fill_float_kernel(float* p, float v) { *p = v; }
+
+__global__ void selftest_division_kernel(const float* x, const float* d, int64_t n, uint32_t* mismatches) {
+  uint32_t bad = 0;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const float dv = d[i];
+    const float y = __frcp_rn(dv);
+    const float2 q = div2(make_float2(x[i], x[i]), make_float2(-dv, -dv), make_float2(y, y));
+    const float ref = __fdiv_rn(x[i], dv);
+    bad += (__float_as_uint(q.x) != __float_as_uint(ref)) ? 1u : 0u;
+  }
+  bad = __reduce_add_sync(0xFFFFFFFFu, bad);
+  if ((threadIdx.x & 31) == 0 && bad) atomicAdd(mismatches, bad);
+}
+
+}  // namespace rb
+
+// =============================================================================================
+// Host entry points
+// =============================================================================================
+using namespace rb;
+
+static bool device_is_sm100() {
+  static int cache[64] = {0};  // 0 unknown, 1 yes, 2 no
+  const int dev = rb_host::current_device();
+  if (dev < 0 || dev >= 64) return false;
+  if (cache[dev] == 0) {
+    int major = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    cache[dev] = (major == 10) ? 1 : 2;
+  }
+  return cache[dev] == 1;
+}
+
+template <bool F32IN, bool DO_ROW, bool DO_COL, bool HAD, bool SR>
+static int launch_quant(const CUtensorMap& tmap, const QuantArgs& a, cudaStream_t stream) {
+  auto kern = nvfp4_quantize_kernel<F32IN, DO_ROW, DO_COL, HAD, SR>;
+  constexpr size_t smem = quant_smem_bytes<F32IN>();
+  static bool configured[64] = {false};
+  const int dev = rb_host::current_device();
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
+      rb_host::set_error("cudaFuncSetAttribute failed: %s", cudaGetErrorString(cudaGetLastError()));
+      return RB_ERR_CUDA;
+    }
+    configured[dev] = true;
+  }
+  static int per_sm[64] = {0};
+  if (dev >= 0 && dev < 64 && per_sm[dev] == 0) {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kQThreads, smem) != cudaSuccess || n < 1) n = 1;
+    per_sm[dev] = n;
+  }
+  const int sms = rb_host::num_sms(dev);
+  const int slots = sms * ((dev >= 0 && dev < 64) ? per_sm[dev] : 1);
+  const int grid = a.n_tiles < slots ? a.n_tiles : slots;
+  kern<<<grid, kQThreads, smem, stream>>>(tmap, a);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    rb_host::set_error("nvfp4 quantize launch failed: %s", cudaGetErrorString(e));
+    return RB_ERR_CUDA;
+  }
+  return RB_OK;
+}
+
+template <bool F32IN, bool DO_ROW, bool DO_COL>
+static int dispatch_had_sr(const CUtensorMap& tmap, const QuantArgs& a, bool had, bool sr, cudaStream_t s) {
+  if (had) {
+    return sr ? launch_quant<F32IN, DO_ROW, DO_COL, DO_COL, true>(tmap, a, s)
+              : launch_quant<F32IN, DO_ROW, DO_COL, DO_COL, false>(tmap, a, s);
+  }
+  return sr ? launch_quant<F32IN, DO_ROW, DO_COL, false, true>(tmap, a, s)
+            : launch_quant<F32IN, DO_ROW, DO_COL, false, false>(tmap, a, s);
+}
+
+template <bool F32IN>
+static int dispatch_forms(const CUtensorMap& tmap, const QuantArgs& a, bool row, bool col, bool had, bool sr,
+                          cudaStream_t s) {
+  if (row && col) return dispatch_had_sr<F32IN, true, true>(tmap, a, had, sr, s);
+  if (row) return dispatch_had_sr<F32IN, true, false>(tmap, a, false, sr, s);
+  return dispatch_had_sr<F32IN, false, true>(tmap, a, had, sr, s);
+}
+
+extern "C" {
+
+uint32_t rb_internal_quant_status(int clear) {
+  uint32_t v = 0;
+  cudaDeviceSynchronize();
+  cudaMemcpyFromSymbol(&v, rb::g_quant_status, sizeof(v));
+  if (clear) {
+    const uint32_t z = 0;
+    cudaMemcpyToSymbol(rb::g_quant_status, &z, sizeof(z));
+  }
+  return v;
+}
+
+int rb_nvfp4_global_scale(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld, float* gs_out,
+                          void* workspace, void* stream) {
+  if (gs_out == nullptr || workspace == nullptr || (x == nullptr && rows * cols > 0)) {
+    rb_host::set_error("nvfp4 global_scale: null pointer argument");
+    return RB_ERR_ARG;
+  }
+  if (dtype != RB_DTYPE_BF16 && dtype != RB_DTYPE_F32) {
+    rb_host::set_error("nvfp4 global_scale: unsupported dtype %d", dtype);
+    return RB_ERR_ARG;
+  }
+  if (rows < 0 || cols < 0 || ld < cols) {
+    rb_host::set_error("nvfp4 global_scale: bad shape rows=%lld cols=%lld ld=%lld", (long long)rows,
+                       (long long)cols, (long long)ld);
+    return RB_ERR_SHAPE;
+  }
+  if (!device_is_sm100()) {
+    rb_host::set_error("nvfp4 global_scale: the current device is not an sm_100 GPU");
+    return RB_ERR_DEVICE;
+  }
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (rows * cols == 0) {
+    rb::fill_float_kernel<<<1, 1, 0, s>>>(gs_out, 1e-12f);
+  } else {
+    const int sms = rb_host::num_sms(rb_host::current_device());
+    const int64_t per = (dtype == RB_DTYPE_BF16 ? 8 : 4) * 512 * 4;
+    int64_t grid = (rows * cols + per - 1) / per;
+    if (grid > 4 * sms) grid = 4 * sms;
+    if (grid < 1) grid = 1;
+    uint32_t* ws = reinterpret_cast<uint32_t*>(workspace);
+    if (dtype == RB_DTYPE_BF16)
+      rb::global_scale_kernel<false><<<(int)grid, 512, 0, s>>>(x, rows, cols, ld, ws, gs_out);
+    else
+      rb::global_scale_kernel<true><<<(int)grid, 512, 0, s>>>(x, rows, cols, ld, ws, gs_out);
+  }
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    rb_host::set_error("nvfp4 global_scale launch failed: %s", cudaGetErrorString(e));
+    return RB_ERR_CUDA;
+  }
+  return RB_OK;
+}
+
+int rb_nvfp4_quantize(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld, const float* gs,
+                      const float* hadamard, const int64_t* seed, void* row_packed, void* row_scale,
+                      void* col_packed, void* col_scale, void* stream) {
+  const bool row = row_packed != nullptr || row_scale != nullptr;
+  const bool col = col_packed != nullptr || col_scale != nullptr;
+  if (!row && !col) {
+    rb_host::set_error("nvfp4 quantize: no output form requested");
+    return RB_ERR_ARG;
+  }
+  if ((row && (row_packed == nullptr || row_scale == nullptr)) ||
+      (col && (col_packed == nullptr || col_scale == nullptr)) || x == nullptr || gs == nullptr) {
+    rb_host::set_error("nvfp4 quantize: null pointer argument");
+    return RB_ERR_ARG;
+  }
+  if (dtype != RB_DTYPE_BF16 && dtype != RB_DTYPE_F32) {
+    rb_host::set_error("nvfp4 quantize: unsupported dtype %d", dtype);
+    return RB_ERR_ARG;
+  }
+  if (rows <= 0 || cols <= 0 || rows % 128 != 0 || cols % 64 != 0) {
+    rb_host::set_error("nvfp4 quantize needs rows %% 128 == 0 and cols %% 64 == 0, got (%lld, %lld)",
+                       (long long)rows, (long long)cols);
+    return RB_ERR_SHAPE;
+  }
+  const int esize = dtype == RB_DTYPE_BF16 ? 2 : 4;
+  if (ld < cols || ((uint64_t)ld * esize) % 16 != 0 || (reinterpret_cast<uintptr_t>(x) & 15) != 0) {
+    rb_host::set_error("nvfp4 quantize: input must be 16-byte aligned with a 16-byte row stride (ld=%lld)",
+                       (long long)ld);
+    return RB_ERR_ARG;
+  }
+  if ((row && ((reinterpret_cast<uintptr_t>(row_packed) & 7) || (reinterpret_cast<uintptr_t>(row_scale) & 3))) ||
+      (col && (reinterpret_cast<uintptr_t>(col_packed) & 7 || (reinterpret_cast<uintptr_t>(col_scale) & 7)))) {
+    rb_host::set_error("nvfp4 quantize: output buffers must be 8-byte aligned");
+    return RB_ERR_ARG;
+  }
+  if ((rows / 128) * (cols / 64) > (int64_t)0x7FFFFFFF) {
+    rb_host::set_error("nvfp4 quantize: tensor too large");
+    return RB_ERR_SHAPE;
+  }
+  if (!device_is_sm100()) {
+    rb_host::set_error("nvfp4 quantize: the current device is not an sm_100 GPU");
+    return RB_ERR_DEVICE;
+  }
+  CUtensorMap tmap;
+  const bool f32 = dtype == RB_DTYPE_F32;
+  if (!rb_host::make_tmap_2d(&tmap, x, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                             (uint64_t)cols, (uint64_t)rows, (uint64_t)ld * esize, f32 ? 32 : 64, 128,
+                             CU_TENSOR_MAP_SWIZZLE_128B))
+    return RB_ERR_CUDA;
+  QuantArgs a;
+  a.M = rows;
+  a.K = cols;
+  a.gs = gs;
+  a.hadamard = hadamard;
+  a.seed = seed;
+  a.row_packed = reinterpret_cast<uint8_t*>(row_packed);
+  a.row_scale = reinterpret_cast<uint8_t*>(row_scale);
+  a.col_packed = reinterpret_cast<uint8_t*>(col_packed);
+  a.col_scale = reinterpret_cast<uint8_t*>(col_scale);
+  a.tiles_k = (int)(cols / 64);
+  a.n_tiles = (int)((rows / 128) * (cols / 64));
+  const bool had = col && hadamard != nullptr;
+  const bool sr = seed != nullptr;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  return f32 ? dispatch_forms<true>(tmap, a, row, col, had, sr, s) : dispatch_forms<false>(tmap, a, row, col, had, sr, s);
+}
+
+int rb_nvfp4_selftest_division(const float* x, const float* d, int64_t n, uint32_t* mismatches, void* stream) {
+  if (x == nullptr || d == nullptr || mismatches == nullptr || n < 0) {
+    rb_host::set_error("nvfp4 selftest_division: bad arguments");
+    return RB_ERR_ARG;
+  }
+  if (!device_is_sm100()) {
+    rb_host::set_error("nvfp4 selftest_division: the current device is not an sm_100 GPU");
+    return RB_ERR_DEVICE;
+  }
+  const int sms = rb_host::num_sms(rb_host::current_device());
+  rb::selftest_division_kernel<<<4 * sms, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(x, d, n, mismatches);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    rb_host::set_error("selftest launch failed: %s", cudaGetErrorString(e));
+    return RB_ERR_CUDA;
+  }
+  return RB_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,68 @@
+"""The C ABI without a GPU: the library loads, exports every function ``include/*.h`` declares,
+and rejects bad arguments on the host with the reference's error text."""
+
+import ctypes
+import glob
+import os
+import re
+
+import pytest
+
+from radiance_b200 import _lib
+from tests.conftest import ROOT
+
+
+def _declared():
+    names = set()
+    for h in glob.glob(os.path.join(ROOT, "include", "*.h")):
+        text = open(h).read()
+        text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+        names |= set(re.findall(r"\b(rb_\w+)\s*\(", text))
+    return sorted(names)
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    lib = _lib.load()
+    declared = _declared()
+    assert "rb_nvfp4_quantize" in declared and "rb_nvfp4_gemm" in declared
+    for name in declared:
+        assert hasattr(lib, name), name
+        assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
+    assert lib.rb_nvfp4_abi_version() == _lib.ABI_VERSION
+
+
+def test_shape_contract_is_checked_on_the_host():
+    lib = _lib.load()
+    buf = ctypes.c_void_p(16)  # never dereferenced: validation fails first
+    rc = lib.rb_nvfp4_quantize(buf, 0, 100, 128, 128, buf, None, None, buf, buf, None, None, None)
+    assert rc == 1
+    assert "rows % 128" in lib.rb_nvfp4_last_error().decode()
+    with pytest.raises(ValueError, match="rows % 128"):
+        _lib.check(rc, "nvfp4.quantize")
+    rc = lib.rb_nvfp4_quantize(buf, 0, 128, 128, 128, buf, None, None, None, None, None, None, None)
+    assert rc == 2 and "no output form" in lib.rb_nvfp4_last_error().decode()
+    rc = lib.rb_nvfp4_quantize(buf, 7, 128, 128, 128, buf, None, None, buf, buf, None, None, None)
+    assert rc == 2 and "dtype" in lib.rb_nvfp4_last_error().decode()
+    rc = lib.rb_nvfp4_global_scale(buf, 0, 4, 4, 2, buf, buf, None)
+    assert rc == 1
+
+
+def test_gemm_shape_contract_is_checked_on_the_host():
+    lib = _lib.load()
+    buf = ctypes.c_void_p(256)
+    rc = lib.rb_nvfp4_gemm(buf, buf, buf, buf, 100, 128, 128, None, None, None, 0, buf, 0, 128, None)
+    assert rc in (1, 2)
+    assert lib.rb_nvfp4_last_error().decode()
+
+
+def test_ops_refuse_cpu_tensors():
+    import torch
+
+    import radiance_b200.nvfp4 as nv
+
+    x = torch.randn(128, 64)
+    with pytest.raises(RuntimeError, match="no CPU"):
+        nv.quantize(x, -1)
+    with pytest.raises(RuntimeError, match="no CPU"):
+        nv.global_scale_of(x)
+    assert not nv.nvfp4_supported("cpu")
