@@ -1,0 +1,449 @@
+"""Benchmark of the NVFP4 linear path (BASELINE metric: NVFP4 linear fwd+bwd TFLOPS).
+
+Workload: one dense transformer block's linears -- QKV 2048->6144,
+O 2048->2048, gate/up 2048->11264, down 5632->2048 -- forward + dgrad + wgrad through
+``radiance_b200.nvfp4.FP4Linear`` with the default recipe (stochastic rounding and Hadamard on,
+packed activation saving on), 16384 tokens per GPU, weights ~N(0, 0.02), activations ~N(0, 1),
+upstream gradients ~N(0, 1e-3).  A step = one micro-batch forward + backward of the four linears.
+Token rows shard across ranks with no data-path collective (weak scaling: every rank runs its own
+16384-token micro-batch; the data-parallel gradient all-reduce belongs to the optimizer, not to
+this path).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints one JSON line (rank 0).  ``--impl reference`` times the reference's CPU implementation of
+the path (the NumPy restatement of radiance's pure-torch NVFP4 emulation in ``oracle/``) on the
+host cores, on a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+D_MODEL = 2048
+TOKENS_PER_GPU = 16384
+LAYERS = [("qkv", 2048, 6144), ("o", 2048, 2048), ("gate_up", 2048, 11264), ("down", 5632, 2048)]
+STEP_FLOPS = 6.0 * TOKENS_PER_GPU * sum(k * n for _, k, n in LAYERS)  # 5.051e12
+METRIC = "NVFP4 linear fwd+bwd TFLOPS (BASELINE config 3 block linears, 16384 tokens/GPU)"
+
+# Average DRAM bytes per GEMM launch of this workload, from `ncu` (profiles/gemm_block_step.txt);
+# None until captured.
+GEMM_DRAM_BYTES_PER_LAUNCH = None
+
+
+def _peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return p, "measured"
+    except (OSError, ValueError):
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+# --------------------------------------------------------------------------------------------------
+# nvidia-smi clock sampling during the timed region
+# --------------------------------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: str):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.gpu)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True,
+            )
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=2)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {
+            "sm_mhz": statistics.median(sm) if sm else None,
+            "sm_max_mhz": max(smax) if smax else None,
+            "reasons": sorted(reasons),
+            "samples": len(sm),
+        }
+
+
+# --------------------------------------------------------------------------------------------------
+# The GPU arm
+# --------------------------------------------------------------------------------------------------
+def _dist_setup(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        from datetime import timedelta
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def _make_layers(device, seed):
+    import torch
+
+    from radiance_b200 import nvfp4 as nv
+
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    layers, xs, dys = [], [], []
+    for name, k, n in LAYERS:
+        lin = nv.FP4Linear(k, n, bias=False, recipe=nv.FP4Recipe())
+        with torch.no_grad():
+            lin.weight.copy_(torch.randn(n, k, generator=g) * 0.02)
+        lin = lin.to(device)
+        lin.refresh_fp4_cache()
+        layers.append(lin)
+        xs.append((torch.randn(TOKENS_PER_GPU, k, generator=g)).to(torch.bfloat16))
+        dys.append((torch.randn(TOKENS_PER_GPU, n, generator=g) * 1e-3).to(torch.bfloat16))
+    return layers, xs, dys
+
+
+def _step(layers, xs, dys, outs=None):
+    import torch
+
+    for i, lin in enumerate(layers):
+        x = xs[i].detach().requires_grad_(True)
+        y = lin(x)
+        gx, gw = torch.autograd.grad(y, (x, lin.weight), dys[i])
+        if outs is not None:
+            outs.append((gx, gw))
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    from radiance_b200.nvfp4 import _trace
+
+    rank, world, local = _dist_setup(args)
+    device = torch.device("cuda", local if world > 1 else 0)
+    layers, xs_host, dys_host = _make_layers(device, seed=1234 + rank)
+    xs = [x.to(device) for x in xs_host]
+    dys = [d.to(device) for d in dys_host]
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-resident timing (value) ------------------------------------------------------
+    for _ in range(args.warmup):
+        _step(layers, xs, dys)
+    torch.cuda.synchronize()
+    visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+    phys = visible.split(",")[torch.cuda.current_device()] if visible else str(torch.cuda.current_device())
+    clocks = ClockSampler(phys)
+    barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    for _ in range(20):  # keep the GPU loaded while the sampler starts up (untimed)
+        _step(layers, xs, dys)
+    with _trace.kernel_timer() as kt:
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        torch.cuda.synchronize()
+        start.record()
+        for _ in range(args.steps):
+            _step(layers, xs, dys)
+        stop.record()
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = start.elapsed_time(stop)
+    ms_max = max_over_ranks(ms)
+    per_kind = kt.summary()
+    launches = kt.launches
+
+    # ---- end-to-end through the public API with host buffers (e2e) --------------------------
+    pinned_x = [x.pin_memory() for x in xs_host]
+    pinned_dy = [d.pin_memory() for d in dys_host]
+    dev_x = [torch.empty_like(x, device=device) for x in xs_host]
+    dev_dy = [torch.empty_like(d, device=device) for d in dys_host]
+    result_host = torch.empty(D_MODEL, dtype=torch.float32).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in pinned_x + pinned_dy)
+    d2h = result_host.numel() * result_host.element_size()
+
+    def e2e_step():
+        for i in range(len(layers)):
+            dev_x[i].copy_(pinned_x[i], non_blocking=True)
+            dev_dy[i].copy_(pinned_dy[i], non_blocking=True)
+        outs = []
+        _step(layers, dev_x, dev_dy, outs)
+        result_host.copy_(outs[0][1][0], non_blocking=True)  # first row of dW(qkv)
+
+    e2e_steps = max(3, min(args.steps, 20))
+    for _ in range(max(3, args.warmup)):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    es.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    ee.record()
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(es.elapsed_time(ee)) / e2e_steps
+
+    if rank == 0:
+        peaks, peak_kind = _peaks()
+        ms_step = ms_max / args.steps
+        value = world * STEP_FLOPS / (ms_step * 1e-3) / 1e12
+        gemm = per_kind.get("gemm", {"launches": 0, "ms": 0.0, "work": 0.0})
+        quant = per_kind.get("quantize", {"launches": 0, "ms": 0.0, "work": 0.0})
+        amax = per_kind.get("amax", {"launches": 0, "ms": 0.0, "work": 0.0})
+        fp4_peak = 4.0 * peaks["bf16_tflops"]
+        gemm_ms_launch = gemm["ms"] / max(gemm["launches"], 1)
+        gemm_tflops = gemm["work"] / (gemm["ms"] * 1e-3) / 1e12 if gemm["ms"] else None
+        traffic = GEMM_DRAM_BYTES_PER_LAUNCH
+        line = {
+            "metric": METRIC,
+            "value": round(value, 2),
+            "unit": "TFLOPS",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_step, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "nvfp4 (e2m1 x e4m3 block scales, fp32 accumulate; bf16 in/out, fp32 dW)",
+            "data": "synthetic (seeded; W~N(0,0.02), X~N(0,1), dY~N(0,1e-3))",
+            "config": {
+                "workload": "config3: dense block linears fwd+dgrad+wgrad via FP4Linear",
+                "d_model": D_MODEL,
+                "layers": {n: [k, o] for n, k, o in LAYERS},
+                "tokens_per_gpu": TOKENS_PER_GPU,
+                "global_batch_tokens": TOKENS_PER_GPU * world,
+                "recipe": "grad_gemms, stochastic_rounding, hadamard, save_activations",
+                "parallelism": f"token-sharded dp{world} (no data-path collective)",
+                "l2": "inputs larger than L2 (about 1 GB of activations and gradients per step)",
+            },
+            "tokens_per_s": round(world * TOKENS_PER_GPU / (ms_step * 1e-3), 1),
+            "gpu_launches": launches,
+            "kernels": {
+                "gemm": {"launches": gemm["launches"], "ms": round(gemm["ms"], 3),
+                         "TFLOPS": None if gemm_tflops is None else round(gemm_tflops, 1)},
+                "quantize": {"launches": quant["launches"], "ms": round(quant["ms"], 3),
+                             "GBps": round(quant["work"] / (quant["ms"] * 1e-3) / 1e9, 1) if quant["ms"] else None},
+                "amax": {"launches": amax["launches"], "ms": round(amax["ms"], 3),
+                         "GBps": round(amax["work"] / (amax["ms"] * 1e-3) / 1e9, 1) if amax["ms"] else None},
+            },
+            "roofline": {
+                "kernel": "nvfp4_gemm_kernel (tcgen05 block-scaled GEMM)",
+                "bound": "tensor",
+                "achieved": None if gemm_tflops is None else round(gemm_tflops, 1),
+                "peak": round(fp4_peak, 1),
+                "peak_basis": f"4 x {peak_kind} dense bf16 ({peaks['bf16_tflops']} TF/s): B200 NVFP4 dense rate is 4x bf16; nominal 9000",
+                "unit": "TFLOP/s",
+                "frac": None if gemm_tflops is None else round(gemm_tflops / fp4_peak, 4),
+                "traffic": traffic,
+                "flops_per_launch": round(gemm["work"] / max(gemm["launches"], 1)),
+                "ms_per_launch": round(gemm_ms_launch, 4),
+            },
+            "e2e": {
+                "value": round(world * STEP_FLOPS / (e2e_ms * 1e-3) / 1e12, 2),
+                "unit": "TFLOPS",
+                "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h,
+                "ms_per_step": round(e2e_ms, 3),
+                "path": "FP4Linear forward/backward (public API), inputs copied from pinned host memory each step",
+            },
+            "clocks": clk,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(budget_s=args.cpu_budget)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# --------------------------------------------------------------------------------------------------
+# The CPU arm (the reference's algorithm: quantize -> dequantize -> fp32 matmul emulation)
+# --------------------------------------------------------------------------------------------------
+def _cpu_linear_step(O, np, w_row, w_col, tokens, rng):
+    """One FP4 linear forward + dgrad + wgrad on the CPU oracle (O-projection shape 2048 -> 2048),
+    following radiance's _FP4LinearFn (linear.py:63-155) with the default recipe."""
+    k = n = D_MODEL
+    x = O.bf16_to_f32(O.f32_to_bf16_bits(rng.standard_normal((tokens, k), dtype=np.float32)))
+    dy = O.bf16_to_f32(O.f32_to_bf16_bits(rng.standard_normal((tokens, n), dtype=np.float32) * 1e-3))
+    had = O.hadamard_matrix()
+    gx = O.global_scale_of(x)
+    xp, xs = O.quantize_rowblock(x, gx)
+    xtp, xts = O.quantize_colblock(x, gx, hadamard=had)
+    (wp, ws, gw) = w_row
+    y = O.dequantize(xp, xs, gx) @ O.dequantize(wp, ws, gw).T
+    gg = O.global_scale_of(dy)
+    u = rng.random(dy.shape, dtype=np.float32)
+    gp, gsc = O.quantize_rowblock(dy, gg, u=u)
+    gtp, gts = O.quantize_colblock(dy, gg, hadamard=had, u=u)
+    (wcp, wcs, gwc) = w_col
+    dx = O.dequantize(gp, gsc, gg) @ O.dequantize(wcp, wcs, gwc).T
+    dw = O.dequantize(gtp, gts, gg) @ O.dequantize(xtp, xts, gx).T
+    return y, dx, dw
+
+
+def _cpu_setup():
+    import numpy as np
+
+    from oracle import nvfp4_oracle as O
+
+    rng = np.random.default_rng(0)
+    w = O.bf16_to_f32(O.f32_to_bf16_bits(rng.standard_normal((D_MODEL, D_MODEL), dtype=np.float32) * 0.02))
+    gw = O.global_scale_of(w)
+    wp, ws = O.quantize_rowblock(w, gw)
+    wcp, wcs = O.quantize_colblock(w, gw)
+    return O, np, (wp, ws, gw), (wcp, wcs, gw), rng
+
+
+def cpu_baseline(budget_s: float = 15.0) -> dict:
+    O, np, w_row, w_col, rng = _cpu_setup()
+    tokens = 512
+    t0 = time.perf_counter()
+    done = 0
+    while time.perf_counter() - t0 < budget_s or done == 0:
+        _cpu_linear_step(O, np, w_row, w_col, tokens, rng)
+        done += 1
+    dt = (time.perf_counter() - t0) / done
+    flops = 6.0 * tokens * D_MODEL * D_MODEL
+    return {
+        "value": round(flops / dt / 1e12, 6),
+        "unit": "TFLOPS",
+        "cores": os.cpu_count(),
+        "kind": "port",
+        "sample": f"{done} x one 2048->2048 linear fwd+dgrad+wgrad on {tokens} tokens (oracle restatement of "
+                  f"radiance's CPU emulation; numpy, BLAS matmuls on all cores), {dt:.2f} s each",
+    }
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    O, np, w_row, w_col, rng = _cpu_setup()
+    # Size one step so warmup + steps fit in about two minutes.
+    t0 = time.perf_counter()
+    _cpu_linear_step(O, np, w_row, w_col, 16, rng)
+    per16 = time.perf_counter() - t0
+    budget = 120.0 / max(args.steps + args.warmup, 1)
+    tokens = int(max(16, min(2048, (budget / max(per16, 1e-3)) * 16)) // 16 * 16)
+    for _ in range(args.warmup):
+        _cpu_linear_step(O, np, w_row, w_col, tokens, rng)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        _cpu_linear_step(O, np, w_row, w_col, tokens, rng)
+    dt = (time.perf_counter() - t0) / args.steps
+    flops = 6.0 * tokens * D_MODEL * D_MODEL
+    value = flops / dt / 1e12
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(value, 6),
+        "unit": "TFLOPS",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(dt * 1e3, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "nvfp4 emulated in fp32 (quantize -> dequantize -> matmul)",
+        "data": "synthetic (seeded)",
+        "config": {"workload": "config3 block linears, sampled: one 2048->2048 linear fwd+dgrad+wgrad",
+                   "tokens_per_step": tokens, "parallelism": "host CPU, rank 0 only"},
+        "cpu_baseline": {
+            "value": round(value, 6),
+            "unit": "TFLOPS",
+            "cores": os.cpu_count(),
+            "kind": "port",
+            "sample": f"one 2048->2048 FP4 linear fwd+dgrad+wgrad on {tokens} tokens per step (recipe: SR + Hadamard)",
+        },
+        "e2e": {"value": round(value, 6), "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-budget", type=float, default=15.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -19,6 +19,7 @@ from dataclasses import dataclass
 import torch
 
 from .. import _lib
+from . import _trace
 
 # Format constants -- quantize.py:16-32.
 FP4_VALUES: tuple[float, ...] = (0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0)
@@ -224,6 +225,7 @@ def global_scale_of(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.T
     if out is None:
         out = torch.empty((), dtype=torch.float32, device=x.device)
     rows, cols = x2.shape
+    tok = _trace.begin("amax", rows * cols * x2.element_size())
     _lib.check(
         lib.rb_nvfp4_global_scale(
             x2.data_ptr(), _dtype_code(x2), rows, cols, x2.stride(0), out.data_ptr(),
@@ -231,6 +233,7 @@ def global_scale_of(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.T
         ),
         "nvfp4.global_scale_of",
     )
+    _trace.end(tok)
     return out
 
 
@@ -259,6 +262,8 @@ def _quantize_into(
     gs = global_scale
     if gs.dtype != torch.float32 or not gs.is_cuda:
         gs = gs.to(device=x.device, dtype=torch.float32)
+    forms = (row is not None) + (col is not None)
+    tok = _trace.begin("quantize", m * k * (x.element_size() + 0.5625 * forms))
     _lib.check(
         lib.rb_nvfp4_quantize(
             x.data_ptr(), _dtype_code(x), m, k, x.stride(0), gs.data_ptr(),
@@ -269,6 +274,7 @@ def _quantize_into(
         ),
         "nvfp4.quantize",
     )
+    _trace.end(tok)
 
 
 def _check_shape(x: torch.Tensor, form: str) -> None:
@@ -419,6 +425,7 @@ def _gemm(
             bias = bias.to(torch.float32)
         bias = bias.contiguous()
         bias_code = _lib.RB_DTYPE_BF16 if bias.dtype == torch.bfloat16 else _lib.RB_DTYPE_F32
+    tok = _trace.begin("gemm", 2.0 * m * n * k)
     _lib.check(
         lib.rb_nvfp4_gemm(
             a_packed.data_ptr(), a_scale.data_ptr(), b_packed.data_ptr(), b_scale.data_ptr(), m, n, k,
@@ -428,6 +435,7 @@ def _gemm(
         ),
         "nvfp4.mm",
     )
+    _trace.end(tok)
     return out if native == out_dtype else out.to(out_dtype)
 
 
