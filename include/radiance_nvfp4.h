@@ -71,6 +71,23 @@ int rb_nvfp4_global_scale(const void* x, int dtype, int64_t rows, int64_t cols, 
                           void* workspace, void* stream);
 
 /*
+ * The same global scale as rb_nvfp4_global_scale, for callers that cannot allocate device memory
+ * on the call path -- code that runs where device allocation is not allowed (a host callback),
+ * plugin hosts whose execute step only receives pre-planned buffers, or a plain C/FFI caller that
+ * has device pointers but no allocator.  It takes no workspace and allocates nothing; the caller
+ * passes only the input and the output.  No counterpart in the reference (radiance's
+ * global_scale_of allocates through torch).
+ *   Scratch: a fixed 64 KiB device array inside this library (held by every GPU that loads it
+ *   until exit), shared by all calls on a device.  One call covers at most 2^31 elements
+ *   (rows * cols); larger inputs return RB_ERR_SHAPE.  Calls whose kernels overlap on the GPU race
+ *   on the scratch: order them (for example, issue them on one stream).
+ *   The first call on each device looks up the scratch's device address; make that first call
+ *   before any stream capture.
+ */
+int rb_nvfp4_global_scale_noalloc(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld, float* gs_out,
+                                  void* stream);
+
+/*
  * NVFP4 quantizer: one pass over x writes the rowblock form, the colblock form, or both.
  * Replaces `quantize` (quantize.py:672-736) and its two Triton kernels (quantize.py:538-644);
  * bit-identical to `quantize_reference` / `ref_quantize_rowblock` / `ref_quantize_colblock`

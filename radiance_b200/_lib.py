@@ -24,6 +24,7 @@ SIGNATURES: dict[str, tuple] = {
     "rb_nvfp4_abi_version": (_int, []),
     "rb_nvfp4_device_status": (_int, [_int]),
     "rb_nvfp4_global_scale": (_int, [_c_void_p, _int, _i64, _i64, _i64, _c_void_p, _c_void_p, _c_void_p]),
+    "rb_nvfp4_global_scale_noalloc": (_int, [_c_void_p, _int, _i64, _i64, _i64, _c_void_p, _c_void_p]),
     "rb_nvfp4_quantize": (
         _int,
         [_c_void_p, _int, _i64, _i64, _i64, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
