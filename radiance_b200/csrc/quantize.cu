@@ -8,11 +8,14 @@
 //   colblock + R  y_i   = sum_j R[j][i] * x_j, j = 0..15 left to right in fp32 (:261-262)
 // and the codes/scale bytes are bit-identical to the reference for round-to-nearest.
 //
-// Design (one persistent CTA pair per SM, 256 threads each):
-//   * A 128 x 64 input tile is brought into shared memory by TMA (128-byte swizzle, so both the
-//     row-major and the column-major walks below are bank-conflict free), S tiles in flight.
+// Design (persistent CTAs, two per SM, 256 threads each):
+//   * A 128-row x 128-byte-wide input tile (128 x 128 bf16 or 128 x 64 fp32) is brought into
+//     shared memory by TMA as two 128-byte-swizzled boxes, three tiles in flight per CTA.  The
+//     swizzle makes both walks below bank-conflict free.
 //   * The rowblock form reads each 16-element run along a row; the colblock form reads 16 rows of
-//     two adjacent columns and works on float2 pairs with Blackwell's packed f32x2 FMA path.
+//     two adjacent columns and works on float2 pairs with Blackwell's packed f32x2 FMA path.  Its
+//     output (a transpose) is staged in shared memory and written as whole 64-byte rows and whole
+//     512-byte scale atoms.
 //   * x / D is never computed with a divide instruction.  Each block looks up D and
 //     Y = RN(1/D) in a 127-entry table (one entry per e4m3 byte, built per CTA with the IEEE
 //     reciprocal) and refines q0 = x*Y with two residual corrections r = x - q*D, q += r*Y, each a
@@ -23,8 +26,9 @@
 //     the correctly rounded quotient after the second.  It holds while the residual x - q*d is a
 //     normal number, i.e. for every quotient above ~1e-20 -- far below 0.25, the smallest quotient
 //     with a non-zero e2m1 code.  Smaller quotients only decide the sign bit of a zero code, and
-//     that sign is fixed up exactly (see underflow_mask8).
-//     rb_nvfp4_selftest_division checks the identity against the IEEE divide on the GPU.
+//     that sign is fixed up exactly (see underflow_mask8).  The block scale amax / (6 gs) uses the
+//     same method with a per-CTA reciprocal of 6 gs.  rb_nvfp4_selftest_division checks the
+//     identity against the IEEE divide on the GPU.
 //   * Codes come from the hardware round-to-nearest-even convert cvt.rn.satfinite.e2m1x2.f32,
 //     which rounds exactly like the reference's comparison ladder (ties to the even code).
 //   * The Hadamard fast path: radiance's rotation is a Sylvester matrix with row signs, scaled by
@@ -43,7 +47,15 @@ __device__ uint32_t g_quant_status;
 
 constexpr int kQThreads = 256;
 constexpr int kQRows = 128;
-constexpr int kQCols = 64;
+constexpr int kQStages = 3;
+constexpr int kQBoxBytes = 16384;        // one 128-row x 128-byte TMA box
+constexpr int kQTileBytes = 2 * kQBoxBytes;
+
+template <bool F32IN>
+struct QTile {
+  static constexpr int kCols = F32IN ? 64 : 128;     // tile width in elements (two boxes)
+  static constexpr int kBoxCols = F32IN ? 32 : 64;   // box width in elements
+};
 
 struct QuantArgs {
   int64_t M, K;
@@ -58,24 +70,17 @@ struct QuantArgs {
   int n_tiles;
 };
 
-template <bool F32IN>
-struct QCfg {
-  static constexpr int kTileBytes = F32IN ? 32768 : 16384;
-  static constexpr int kStages = F32IN ? 3 : 4;
-};
-
 struct QHeader {
-  uint64_t full[4];
+  uint64_t full[kQStages];
   float2 table[128];  // (D, RN(1/D)) for each e4m3 byte; entry 127 unused
   float had[256];
   uint32_t sign_mask[16];
   int had_fast;
+  alignas(16) uint8_t stage_pk[8 * 1024];  // colblock codes: 8 warps x 128 rows x 8 bytes
+  alignas(16) uint8_t stage_sc[2 * 512];   // colblock scales: the tile's two SWIZZLE_32_4_4 atoms
 };
 
-template <bool F32IN>
-constexpr size_t quant_smem_bytes() {
-  return 1024 + (size_t)QCfg<F32IN>::kTileBytes * QCfg<F32IN>::kStages + sizeof(QHeader);
-}
+constexpr size_t quant_smem_bytes() { return 1024 + (size_t)kQTileBytes * kQStages + sizeof(QHeader); }
 
 // ---------------------------------------------------------------------------------------------
 // Scalar helpers
@@ -86,19 +91,26 @@ __device__ __forceinline__ float e4m3_value(uint32_t b) {
   return __uint_as_float(((e + 120u) << 23) | (m << 20));
 }
 
-// Smallest e4m3 byte whose value is >= s, for s in [1e-12, 448] (quantize.py:180-184).
+// Smallest e4m3 byte whose value is >= s, for s in [1e-12, 448] (quantize.py:180-184): round the
+// fp32 mantissa up to 3 bits in the normal range, ceil(s * 2^9) in the subnormal range.
 __device__ __forceinline__ uint32_t e4m3_ceil_byte(float s) {
-  if (s >= 0.015625f) {
-    const uint32_t b = (__float_as_uint(s) + 0xFFFFFu) & 0xFFF00000u;
-    return (b >> 20) - 960u;
-  }
-  return (uint32_t)ceilf(s * 512.0f);
+  const uint32_t nb = ((__float_as_uint(s) + 0xFFFFFu) >> 20) - 960u;
+  const uint32_t sb = __float2uint_ru(s * 512.0f);
+  return s >= 0.015625f ? nb : sb;
 }
 
-__device__ __forceinline__ uint32_t block_scale_byte(float amax, float denom) {
-  float s = __fdiv_rn(amax, denom);
-  s = fminf(fmaxf(s, 1e-12f), 448.0f);
-  return e4m3_ceil_byte(s);
+// Block-scale byte for a block amax: smallest e4m3 >= clamp(RN(amax / denom), 1e-12, 448).  The
+// quotient is Markstein's (rd = RN(1/denom), nd = -denom); a quotient above 512 saturates to 448
+// directly, since the corrections would overflow there.
+__device__ __forceinline__ uint32_t block_scale_byte(float amax, float nd, float rd) {
+  const float q0 = amax * rd;
+  float q = q0;
+  float r = fmaf(q, nd, amax);
+  q = fmaf(r, rd, q);
+  r = fmaf(q, nd, amax);
+  q = fmaf(r, rd, q);
+  q = (q0 > 512.0f) ? 448.0f : fminf(fmaxf(q, 1e-12f), 448.0f);
+  return e4m3_ceil_byte(q);
 }
 
 // q = RN(x / d) for a float2, given nd = -d and y = RN(1/d) (Markstein, two corrections).
@@ -110,8 +122,7 @@ __device__ __forceinline__ float2 div2(float2 x, float2 nd, float2 y) {
   return __ffma2_rn(r, y, q);
 }
 
-// Eight quotients (element order a.x, a.y, b.x, ...) -> one 32-bit word of packed e2m1 codes,
-// element 0 in the low nibble.
+// Eight quotients -> one 32-bit word of packed e2m1 codes, e0 in the low nibble.
 __device__ __forceinline__ uint32_t e2m1x8(float e0, float e1, float e2, float e3, float e4, float e5, float e6,
                                            float e7) {
   uint32_t out;
@@ -126,41 +137,43 @@ __device__ __forceinline__ uint32_t e2m1x8(float e0, float e1, float e2, float e
   return out;
 }
 
-// Counter-based random bits: the PCG output permutation applied to one LCG step of the input
-// (M. O'Neill, "PCG: a family of simple fast space-efficient statistically good algorithms for
-// random number generation", 2014; used as a hash in Jarzynski & Olano, "Hash Functions for GPU
-// Rendering", JCGT 9(3), 2020).
-__device__ __forceinline__ uint32_t pcg_hash(uint32_t v) {
-  const uint32_t s = v * 747796405u + 2891336453u;
-  const uint32_t w = ((s >> ((s >> 28u) + 4u)) ^ s) * 277803737u;
-  return (w >> 22u) ^ w;
+// Random bits for stochastic rounding: a two-round xor-shift / multiply mixer applied to
+// (element index ^ key) -- the "lowbias32" finalizer from C. Wellons' hash-prospector search
+// (public domain constants), a bijection on 32-bit words with full avalanche.
+__device__ __forceinline__ uint32_t mix32(uint32_t x) {
+  x ^= x >> 16;
+  x *= 0x7FEB352Du;
+  x ^= x >> 15;
+  x *= 0x846CA68Bu;
+  x ^= x >> 16;
+  return x;
 }
 
-// Stochastic rounding of a quotient q (already RN(x/D)) to a signed e2m1 code (quantize.py:122-138):
-// lo = the grid level at or below min(|q|, 6), round up with probability (a - lo) / (hi - lo).
-// The fraction is read straight from the fp32 bits: on [1, 8) the e2m1 grid keeps one mantissa
-// bit, so the 22 bits below it are the fraction in units of 2^-22; [0, 1) is shifted to [1, 2),
-// where the grid spacing (0.5) is the same.  The draw uses 22 random bits.
-__device__ __forceinline__ uint32_t sr_code(float q, uint32_t rnd) {
+// Per-launch key from the 64-bit seed (read on the device through a pointer).
+__device__ __forceinline__ uint32_t sr_key(const int64_t* seed) {
+  const uint64_t s = (uint64_t)(*seed);
+  return mix32((uint32_t)s ^ 0x9E3779B9u) ^ mix32((uint32_t)(s >> 32) + 0x7F4A7C15u);
+}
+
+// Key for a run of element indices sharing the same upper 32 bits.
+__device__ __forceinline__ uint32_t sr_key_hi(uint32_t key, uint64_t lin) {
+  const uint32_t hi = (uint32_t)(lin >> 32);
+  return hi ? key ^ mix32(hi + 0x632BE5ABu) : key;
+}
+
+// Stochastic rounding of a quotient q (= RN(x / D)) to a signed e2m1 code, with 32 random bits r
+// (rule of quantize.py:122-138: lo = the grid level at or below a = min(|q|, 6), round up with
+// probability (a - lo) / (hi - lo)).  On [1, 8) the e2m1 grid keeps one fp32 mantissa bit, so the
+// 22 bits below it hold the fraction (a - lo) / (hi - lo) in units of 2^-22: adding 22 uniform
+// random bits carries into the kept bit exactly with that probability, and the carry moves the
+// value to the next level (into the exponent where the level is a power of two).  [0, 1) is
+// shifted to [1, 2), where the grid step (0.5) is the same, and the code shifted back by 2.
+__device__ __forceinline__ uint32_t sr_code(float q, uint32_t r) {
   const float a = fminf(fabsf(q), 6.0f);
   const bool sub = a < 1.0f;
   const float t = sub ? __fadd_rn(a, 1.0f) : a;
-  const uint32_t bits = __float_as_uint(t);
-  uint32_t code = (bits >> 22) - (sub ? 254u : 252u);
-  code += ((rnd >> 10) < (bits & 0x3FFFFFu)) ? 1u : 0u;
-  return code | (q < 0.0f ? 8u : 0u);
-}
-
-__device__ __forceinline__ uint32_t sr_key(const int64_t* seed) {
-  const uint64_t s = (uint64_t)(*seed);
-  return pcg_hash((uint32_t)s ^ 0x9E3779B9u) ^ pcg_hash((uint32_t)(s >> 32) + 0x7F4A7C15u);
-}
-
-// Random bits for element index `lin` (row * cols + col of the original tensor, the same index
-// for both layouts, as in quantize.py:564-567 and :620-623).
-__device__ __forceinline__ uint32_t sr_bits(uint32_t key, uint64_t lin) {
-  const uint32_t hi = (uint32_t)(lin >> 32);
-  return pcg_hash((uint32_t)lin ^ key ^ (hi ? pcg_hash(hi) : 0u));
+  const uint32_t b = __float_as_uint(t) + (r >> 10);
+  return (b >> 22) - (sub ? 254u : 252u) + (q < 0.0f ? 8u : 0u);
 }
 
 // A quotient that rounds to +-0 must produce nibble 0 (the reference's sign is `q < 0`, false for
@@ -177,7 +190,7 @@ __device__ __forceinline__ uint32_t underflow_mask8(const float* v, int stride, 
 }
 
 // ---------------------------------------------------------------------------------------------
-// Shared-memory reads of the swizzled tile
+// Shared-memory access
 // ---------------------------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t lds32(uint32_t addr) {
   uint32_t v;
@@ -194,6 +207,12 @@ __device__ __forceinline__ uint4 lds128(uint32_t addr) {
   asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
   return v;
 }
+__device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+__device__ __forceinline__ void sts8(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared.b8 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
 
 __device__ __forceinline__ float2 bf16x2_to_float2(uint32_t w) {
   return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
@@ -202,95 +221,121 @@ __device__ __forceinline__ float2 bf16x2_to_float2(uint32_t w) {
 __device__ __forceinline__ void st_global_v2(void* p, uint32_t a, uint32_t b) {
   asm volatile("st.global.v2.b32 [%0], {%1, %2};" ::"l"(p), "r"(a), "r"(b) : "memory");
 }
-
-// Byte offset of scale (r, c) in the SWIZZLE_32_4_4 layout with `nct` 4-column tiles per 128-row
-// tile (quantize.py:293-305).
-__device__ __forceinline__ int64_t blocked_offset(int64_t r, int64_t c, int64_t nct) {
-  return ((r >> 7) * nct + (c >> 2)) * 512 + (r & 31) * 16 + ((r & 127) >> 5) * 4 + (c & 3);
+__device__ __forceinline__ void st_global_v4(void* p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.global.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
 
+struct QCtx {
+  const QHeader* hdr;
+  float nden, rden;  // -(6 gs) and RN(1/(6 gs))
+  uint32_t key;
+};
+
 // ---------------------------------------------------------------------------------------------
-// The rowblock form: thread (warp w, lane l) handles rows 16w + 8p + l/4 (p = 0, 1), block l % 4.
+// The rowblock form of one 16-element block: returns its two packed words and its scale byte.
 // ---------------------------------------------------------------------------------------------
-template <bool F32IN, bool SR>
-__device__ __forceinline__ void row_blocks(uint32_t tile, const QHeader* hdr, const QuantArgs& a, int64_t m0,
-                                           int64_t k0, int mt, int kt, float denom, uint32_t key) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int b = lane & 3;
+template <bool SR>
+__device__ __forceinline__ uint32_t row_block(const float2 (&v)[8], const QCtx& c, const QuantArgs& a, uint64_t lin0,
+                                              uint32_t& w0, uint32_t& w1, bool f32in) {
+  float amax = 0.0f;
 #pragma unroll
-  for (int p = 0; p < 2; ++p) {
-    const int r = 16 * warp + 8 * p + (lane >> 2);
-    float2 v[8];
-    if constexpr (!F32IN) {
-      const uint32_t row = tile + r * 128;
-      const uint4 c0 = lds128(row + (((2 * b) ^ (r & 7)) << 4));
-      const uint4 c1 = lds128(row + (((2 * b + 1) ^ (r & 7)) << 4));
-      v[0] = bf16x2_to_float2(c0.x); v[1] = bf16x2_to_float2(c0.y);
-      v[2] = bf16x2_to_float2(c0.z); v[3] = bf16x2_to_float2(c0.w);
-      v[4] = bf16x2_to_float2(c1.x); v[5] = bf16x2_to_float2(c1.y);
-      v[6] = bf16x2_to_float2(c1.z); v[7] = bf16x2_to_float2(c1.w);
-    } else {
-      const uint32_t row = tile + (b >> 1) * 16384 + r * 128;
+  for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fmaxf(fabsf(v[e].x), fabsf(v[e].y)));
+  const uint32_t sbyte = block_scale_byte(amax, c.nden, c.rden);
+  const float2 dy = c.hdr->table[sbyte];
+  const float2 nd = make_float2(-dy.x, -dy.x), yy = make_float2(dy.y, dy.y);
+  if constexpr (SR) {
+    const uint32_t kk = sr_key_hi(c.key, lin0), l0 = (uint32_t)lin0;
+    w0 = w1 = 0;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const uint4 w = lds128(row + ((((b & 1) * 4 + c) ^ (r & 7)) << 4));
-        v[2 * c] = make_float2(__uint_as_float(w.x), __uint_as_float(w.y));
-        v[2 * c + 1] = make_float2(__uint_as_float(w.z), __uint_as_float(w.w));
-      }
+    for (int e = 0; e < 8; ++e) {
+      const float2 q = div2(v[e], nd, yy);
+      const uint32_t pair = sr_code(q.x, mix32((l0 + 2 * e) ^ kk)) | (sr_code(q.y, mix32((l0 + 2 * e + 1) ^ kk)) << 4);
+      if (e < 4) w0 |= pair << (8 * e);
+      else w1 |= pair << (8 * (e - 4));
     }
-    float amax = 0.0f;
-#pragma unroll
-    for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fmaxf(fabsf(v[e].x), fabsf(v[e].y)));
-    const uint32_t sbyte = block_scale_byte(amax, denom);
-    const float2 dy = hdr->table[sbyte];
-    const float2 nd = make_float2(-dy.x, -dy.x), yy = make_float2(dy.y, dy.y);
+  } else {
     float2 q[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) q[e] = div2(v[e], nd, yy);
-    uint32_t w0, w1;
-    if constexpr (SR) {
+    w0 = e2m1x8(q[0].x, q[0].y, q[1].x, q[1].y, q[2].x, q[2].y, q[3].x, q[3].y);
+    w1 = e2m1x8(q[4].x, q[4].y, q[5].x, q[5].y, q[6].x, q[6].y, q[7].x, q[7].y);
+  }
+  if (dy.x >= (f32in ? 1.0f : 65536.0f)) {
+    w0 &= underflow_mask8(&v[0].x, 1, dy.x);
+    w1 &= underflow_mask8(&v[4].x, 1, dy.x);
+  }
+  return sbyte;
+}
+
+// Rowblock form of a tile.  bf16: thread (warp w, lane l) takes block l % 8 of rows
+// 16w + 4p + l/8 (p = 0..3); fp32: block l % 4 of rows 16w + 8p + l/4 (p = 0, 1).  Two blocks are
+// processed together for instruction-level parallelism.
+template <bool F32IN, bool SR>
+__device__ __forceinline__ void row_tile(uint32_t tile, const QCtx& c, const QuantArgs& a, int64_t m0, int64_t k0,
+                                         int mt, int kt, int valid_cols) {
+  constexpr int kBlocksPerRow = F32IN ? 4 : 8;
+  constexpr int kRowsPerPass = 32 / kBlocksPerRow;
+  constexpr int kPasses = 16 / kRowsPerPass;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = lane % kBlocksPerRow;
+  const bool valid = 16 * b < valid_cols;
+#pragma unroll 1
+  for (int pp = 0; pp < kPasses; pp += 2) {
+    float2 v[2][8];
+    int rr[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int r = 16 * warp + kRowsPerPass * (pp + u) + lane / kBlocksPerRow;
+      rr[u] = r;
+      if constexpr (!F32IN) {
+        const uint32_t row = tile + (b >> 2) * kQBoxBytes + r * 128;
+        const uint4 c0 = lds128(row + (((2 * (b & 3)) ^ (r & 7)) << 4));
+        const uint4 c1 = lds128(row + (((2 * (b & 3) + 1) ^ (r & 7)) << 4));
+        v[u][0] = bf16x2_to_float2(c0.x); v[u][1] = bf16x2_to_float2(c0.y);
+        v[u][2] = bf16x2_to_float2(c0.z); v[u][3] = bf16x2_to_float2(c0.w);
+        v[u][4] = bf16x2_to_float2(c1.x); v[u][5] = bf16x2_to_float2(c1.y);
+        v[u][6] = bf16x2_to_float2(c1.z); v[u][7] = bf16x2_to_float2(c1.w);
+      } else {
+        const uint32_t row = tile + (b >> 1) * kQBoxBytes + r * 128;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint4 w = lds128(row + ((((b & 1) * 4 + q) ^ (r & 7)) << 4));
+          v[u][2 * q] = make_float2(__uint_as_float(w.x), __uint_as_float(w.y));
+          v[u][2 * q + 1] = make_float2(__uint_as_float(w.z), __uint_as_float(w.w));
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int r = rr[u];
       const uint64_t lin0 = (uint64_t)(m0 + r) * (uint64_t)a.K + (uint64_t)(k0 + 16 * b);
-      uint32_t c[16];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        c[2 * e] = sr_code(q[e].x, sr_bits(key, lin0 + 2 * e));
-        c[2 * e + 1] = sr_code(q[e].y, sr_bits(key, lin0 + 2 * e + 1));
+      uint32_t w0, w1;
+      const uint32_t sbyte = row_block<SR>(v[u], c, a, lin0, w0, w1, F32IN);
+      if (valid) st_global_v2(a.row_packed + (m0 + r) * (a.K >> 1) + (k0 >> 1) + 8 * b, w0, w1);
+      // Gather the four scale bytes of an atom column group (lanes l..l+3) into one store.
+      uint32_t s4 = sbyte;
+      s4 |= __shfl_down_sync(0xFFFFFFFFu, sbyte, 1) << 8;
+      s4 |= __shfl_down_sync(0xFFFFFFFFu, sbyte, 2) << 16;
+      s4 |= __shfl_down_sync(0xFFFFFFFFu, sbyte, 3) << 24;
+      if ((b & 3) == 0 && valid) {
+        uint8_t* atom = a.row_scale + ((int64_t)mt * (a.K >> 6) + (k0 >> 6) + (b >> 2)) * 512;
+        *reinterpret_cast<uint32_t*>(atom + (r & 31) * 16 + (r >> 5) * 4) = s4;
       }
-      w0 = w1 = 0;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        w0 |= c[e] << (4 * e);
-        w1 |= c[8 + e] << (4 * e);
-      }
-    } else {
-      w0 = e2m1x8(q[0].x, q[0].y, q[1].x, q[1].y, q[2].x, q[2].y, q[3].x, q[3].y);
-      w1 = e2m1x8(q[4].x, q[4].y, q[5].x, q[5].y, q[6].x, q[6].y, q[7].x, q[7].y);
-    }
-    const float risk = F32IN ? 1.0f : 65536.0f;
-    if (dy.x >= risk) {
-      w0 &= underflow_mask8(&v[0].x, 1, dy.x);
-      w1 &= underflow_mask8(&v[4].x, 1, dy.x);
-    }
-    st_global_v2(a.row_packed + (m0 + r) * (a.K >> 1) + (k0 >> 1) + 8 * b, w0, w1);
-    // Gather the four block scales of this row (lanes l..l+3) into one 32-bit store.
-    uint32_t s4 = sbyte;
-    s4 |= __shfl_down_sync(0xFFFFFFFFu, sbyte, 1) << 8;
-    s4 |= __shfl_down_sync(0xFFFFFFFFu, sbyte, 2) << 16;
-    s4 |= __shfl_down_sync(0xFFFFFFFFu, sbyte, 3) << 24;
-    if (b == 0) {
-      uint8_t* atom = a.row_scale + ((int64_t)mt * a.tiles_k + kt) * 512;
-      *reinterpret_cast<uint32_t*>(atom + (r & 31) * 16 + (r >> 5) * 4) = s4;
     }
   }
 }
 
 // ---------------------------------------------------------------------------------------------
-// The colblock form: thread (warp g, lane cp) handles rows 16g..16g+15 of columns 2cp, 2cp+1.
+// The colblock form: warp g handles rows 16g..16g+15; each unit is two adjacent columns.  Its two
+// 8-byte packed runs go to warp g's staging region (rows permuted by `row ^ 4g`, so both the
+// write and the row-wise read-back are conflict-free) and its two scale bytes into the staged
+// SWIZZLE_32_4_4 atoms.
 // ---------------------------------------------------------------------------------------------
 template <bool F32IN, bool HAD, bool SR>
-__device__ __forceinline__ void col_unit(uint32_t tile, const QHeader* hdr, const QuantArgs& a, int64_t m0,
-                                         int64_t k0, float denom, uint32_t key) {
-  const int g = threadIdx.x >> 5, cp = threadIdx.x & 31;
+__device__ __forceinline__ void col_unit(uint32_t tile, const QCtx& c, const QuantArgs& a, int64_t m0, int64_t k0,
+                                         int cp, bool valid, uint32_t stage_pk, uint32_t stage_sc) {
+  const QHeader* hdr = c.hdr;
+  const int g = threadIdx.x >> 5;
   float2 v[16];
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
@@ -298,11 +343,13 @@ __device__ __forceinline__ void col_unit(uint32_t tile, const QHeader* hdr, cons
     uint32_t sm = 0;
     if constexpr (HAD) sm = hdr->had_fast ? hdr->sign_mask[j] : 0u;
     if constexpr (!F32IN) {
-      uint32_t w = lds32(tile + r * 128 + ((((cp >> 2) ^ (j & 7)) << 4) | ((cp & 3) << 2)));
+      const int cpl = cp & 31;  // pair within its 64-column box
+      const uint32_t w = lds32(tile + (cp >> 5) * kQBoxBytes + r * 128 + ((((cpl >> 2) ^ (j & 7)) << 4) | ((cpl & 3) << 2)));
       v[j] = bf16x2_to_float2(w ^ (sm & 0x80008000u));
     } else {
-      const int cpp = cp & 15;
-      uint2 w = lds64(tile + (cp >> 4) * 16384 + r * 128 + ((((cpp >> 1) ^ (j & 7)) << 4) | ((cpp & 1) << 3)));
+      const int cpp = cp & 15;  // pair within its 32-column box
+      const uint2 w =
+          lds64(tile + (cp >> 4) * kQBoxBytes + r * 128 + ((((cpp >> 1) ^ (j & 7)) << 4) | ((cpp & 1) << 3)));
       v[j] = make_float2(__uint_as_float(w.x ^ (sm & 0x80000000u)), __uint_as_float(w.y ^ (sm & 0x80000000u)));
     }
   }
@@ -343,23 +390,24 @@ __device__ __forceinline__ void col_unit(uint32_t tile, const QHeader* hdr, cons
     ay = fmaxf(ay, fabsf(v[i].y));
   }
   const float unfold = 1.0f / scale_fold;  // exact (1 or 1/4)
-  const uint32_t bx = block_scale_byte(ax * unfold, denom);
-  const uint32_t by = block_scale_byte(ay * unfold, denom);
+  const uint32_t bx = block_scale_byte(ax * unfold, c.nden, c.rden);
+  const uint32_t by = block_scale_byte(ay * unfold, c.nden, c.rden);
   const float2 tx = hdr->table[bx], ty = hdr->table[by];
   const float dx = tx.x * scale_fold, dyv = ty.x * scale_fold;
   const float2 nd = make_float2(-dx, -dyv), yy = make_float2(tx.y * unfold, ty.y * unfold);
-  float2 q[16];
-#pragma unroll
-  for (int i = 0; i < 16; ++i) q[i] = div2(v[i], nd, yy);
   uint32_t wx0, wx1, wy0, wy1;
   if constexpr (SR) {
     const uint64_t lin0 = (uint64_t)(m0 + 16 * g) * (uint64_t)a.K + (uint64_t)(k0 + 2 * cp);
+    const uint32_t kk = sr_key_hi(c.key, lin0);
+    uint32_t l = (uint32_t)lin0;
+    const uint32_t kstride = (uint32_t)a.K;
     wx0 = wx1 = wy0 = wy1 = 0;
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
-      const uint64_t lin = lin0 + (uint64_t)i * (uint64_t)a.K;
-      const uint32_t cx = sr_code(q[i].x, sr_bits(key, lin));
-      const uint32_t cy = sr_code(q[i].y, sr_bits(key, lin + 1));
+      const float2 q = div2(v[i], nd, yy);
+      const uint32_t cx = sr_code(q.x, mix32(l ^ kk));
+      const uint32_t cy = sr_code(q.y, mix32((l + 1) ^ kk));
+      l += kstride;
       if (i < 8) {
         wx0 |= cx << (4 * i);
         wy0 |= cy << (4 * i);
@@ -369,6 +417,9 @@ __device__ __forceinline__ void col_unit(uint32_t tile, const QHeader* hdr, cons
       }
     }
   } else {
+    float2 q[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) q[i] = div2(v[i], nd, yy);
     wx0 = e2m1x8(q[0].x, q[1].x, q[2].x, q[3].x, q[4].x, q[5].x, q[6].x, q[7].x);
     wx1 = e2m1x8(q[8].x, q[9].x, q[10].x, q[11].x, q[12].x, q[13].x, q[14].x, q[15].x);
     wy0 = e2m1x8(q[0].y, q[1].y, q[2].y, q[3].y, q[4].y, q[5].y, q[6].y, q[7].y);
@@ -384,28 +435,68 @@ __device__ __forceinline__ void col_unit(uint32_t tile, const QHeader* hdr, cons
     wy0 &= underflow_mask8(&v[0].y, 2, dyv);
     wy1 &= underflow_mask8(&v[8].y, 2, dyv);
   }
-  const int64_t kx = k0 + 2 * cp;
-  const int64_t half_m = a.M >> 1;
-  uint8_t* dst = a.col_packed + kx * half_m + ((m0 + 16 * g) >> 1);
-  st_global_v2(dst, wx0, wx1);
-  st_global_v2(dst + half_m, wy0, wy1);
-  const int64_t nct = a.M >> 6;  // 4-column scale tiles per 128-row tile (M/16 scale columns)
-  const int64_t mb = (m0 >> 4) + g;
-  a.col_scale[blocked_offset(kx, mb, nct)] = (uint8_t)bx;
-  a.col_scale[blocked_offset(kx + 1, mb, nct)] = (uint8_t)by;
+  // Columns past K (the zero-filled half of a K % 128 == 64 tile) stage zeros: their scale bytes
+  // are the contract's zero padding, and their packed rows are never stored.
+  const uint32_t sbx = valid ? bx : 0u, sby = valid ? by : 0u;
+  // Packed runs of columns 2cp and 2cp+1 -> rows (2cp ^ 4g), (2cp ^ 4g) + 1 of region g.
+  sts128(stage_pk + g * 1024 + (((2 * cp) ^ (4 * g)) << 3), wx0, wx1, wy0, wy1);
+  // Scale bytes: atom g/4; 16-byte row (kk % 32); 4-byte group (k0 % 128 + kk) / 32; byte g % 4.
+  const int kk0 = (int)(k0 & 127) + 2 * cp;
+  const uint32_t sc = stage_sc + (g >> 2) * 512 + (kk0 & 31) * 16 + (kk0 >> 5) * 4 + (g & 3);
+  sts8(sc, sbx);
+  sts8(sc + 16, sby);
+}
+
+// Writes the staged colblock outputs of one tile: `valid_cols` output rows of 64 bytes, and the
+// tile's scale atoms (whole atoms for a 128-column tile, the tile's half for a 64-column one).
+template <bool F32IN>
+__device__ __forceinline__ void col_store(const QuantArgs& a, int64_t m0, int64_t k0, int mt, int valid_cols,
+                                          uint32_t stage_pk, uint32_t stage_sc) {
+  constexpr int kCols = QTile<F32IN>::kCols;
+  const int t = threadIdx.x;
+#pragma unroll
+  for (int item = t; item < kCols * 4; item += kQThreads) {
+    const int kk = item >> 2, p = item & 3;  // output row k0 + kk, bytes 16p .. 16p+15
+    if (kk < valid_cols) {
+      const uint2 lo = lds64(stage_pk + (2 * p) * 1024 + ((kk ^ (8 * p)) << 3));
+      const uint2 hi = lds64(stage_pk + (2 * p + 1) * 1024 + ((kk ^ (8 * p + 4)) << 3));
+      st_global_v4(a.col_packed + (k0 + kk) * (a.M >> 1) + (m0 >> 1) + 16 * p, lo.x, lo.y, hi.x, hi.y);
+    }
+  }
+  const int64_t atom0 = (k0 >> 7) * (a.M >> 6) + 2 * mt;
+  if constexpr (!F32IN) {
+    if (t < 64) {  // two whole 512-byte atoms, 16 bytes per thread
+      const int at = t >> 5, off = (t & 31) * 16;
+      const uint4 s = lds128(stage_sc + at * 512 + off);
+      st_global_v4(a.col_scale + (atom0 + at) * 512 + off, s.x, s.y, s.z, s.w);
+    }
+  } else {
+    if (t < 64) {  // the tile's 8-byte half of each 16-byte atom row
+      const int at = t >> 5, r = t & 31, half = (k0 & 64) ? 8 : 0;
+      const uint2 s = lds64(stage_sc + at * 512 + r * 16 + half);
+      st_global_v2(a.col_scale + (atom0 + at) * 512 + r * 16 + half, s.x, s.y);
+    }
+    // A K that is not a multiple of 128 ends on a 64-column tile whose atoms' other halves are
+    // padding rows: they must read as zero.
+    if ((a.K & 127) != 0 && (k0 >> 6) == (a.K >> 6) - 1 && t >= 64 && t < 128) {
+      const int u = t - 64;
+      st_global_v2(a.col_scale + (atom0 + (u >> 5)) * 512 + (u & 31) * 16 + 8, 0u, 0u);
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------------------------
 // The kernel
 // ---------------------------------------------------------------------------------------------
 template <bool F32IN, bool DO_ROW, bool DO_COL, bool HAD, bool SR>
-__global__ void __launch_bounds__(kQThreads, 1)
+__global__ void __launch_bounds__(kQThreads, 2)
     nvfp4_quantize_kernel(const __grid_constant__ CUtensorMap tmap, const QuantArgs a) {
-  using Cfg = QCfg<F32IN>;
-  constexpr int S = Cfg::kStages;
+  constexpr int S = kQStages;
+  constexpr int kCols = QTile<F32IN>::kCols;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  QHeader* hdr = reinterpret_cast<QHeader*>(smem + (size_t)Cfg::kTileBytes * S);
+  QHeader* hdr = reinterpret_cast<QHeader*>(smem + (size_t)kQTileBytes * S);
+  const uint32_t stage_pk = smem_u32(hdr->stage_pk), stage_sc = smem_u32(hdr->stage_sc);
   const int tid = threadIdx.x;
 
   if ((int)blockIdx.x >= a.n_tiles) return;
@@ -416,8 +507,13 @@ __global__ void __launch_bounds__(kQThreads, 1)
     fence_mbar_init();
     prefetch_tensormap(&tmap);
   }
+  QCtx c;
+  c.hdr = hdr;
   const float gs = *a.gs;
   const float denom = __fmul_rn(6.0f, gs);
+  c.nden = -denom;
+  c.rden = __frcp_rn(denom);
+  c.key = 0;
   if (tid < 127) {
     const float d = __fmul_rn(e4m3_value(tid), gs);
     hdr->table[tid] = make_float2(d, __frcp_rn(d));
@@ -425,8 +521,7 @@ __global__ void __launch_bounds__(kQThreads, 1)
   if constexpr (HAD) {
     hdr->had[tid] = a.hadamard[tid];
   }
-  uint32_t key = 0;
-  if constexpr (SR) key = sr_key(a.seed);
+  if constexpr (SR) c.key = sr_key(a.seed);
   __syncthreads();
   if constexpr (HAD) {
     // Is R = (Sylvester / 4) with row signs?  Then take the add-only fast path.
@@ -449,14 +544,10 @@ __global__ void __launch_bounds__(kQThreads, 1)
     const int s = it % S;
     const int t = (int)blockIdx.x + it * (int)gridDim.x;
     const int mt = t / a.tiles_k, kt = t - mt * a.tiles_k;
-    uint8_t* dst = smem + (size_t)s * Cfg::kTileBytes;
-    mbar_arrive_expect_tx(&hdr->full[s], Cfg::kTileBytes);
-    if constexpr (!F32IN) {
-      tma_load_2d(dst, &tmap, &hdr->full[s], kt * kQCols, mt * kQRows);
-    } else {
-      tma_load_2d(dst, &tmap, &hdr->full[s], kt * kQCols, mt * kQRows);
-      tma_load_2d(dst + 16384, &tmap, &hdr->full[s], kt * kQCols + 32, mt * kQRows);
-    }
+    uint8_t* dst = smem + (size_t)s * kQTileBytes;
+    mbar_arrive_expect_tx(&hdr->full[s], kQTileBytes);
+    tma_load_2d(dst, &tmap, &hdr->full[s], kt * kCols, mt * kQRows);
+    tma_load_2d(dst + kQBoxBytes, &tmap, &hdr->full[s], kt * kCols + QTile<F32IN>::kBoxCols, mt * kQRows);
   };
   if (tid == 0) {
     for (int it = 0; it < S && it < n_my; ++it) issue(it);
@@ -465,7 +556,8 @@ __global__ void __launch_bounds__(kQThreads, 1)
   for (int it = 0; it < n_my; ++it) {
     const int s = it % S;
     const bool ok = mbar_wait(&hdr->full[s], (uint32_t)((it / S) & 1));
-    // Every thread has finished tile it-1 once past this barrier, so its stage may be refilled.
+    // Every thread has finished tile it-1 once past this barrier, so its stage may be refilled
+    // and the colblock staging area reused.
     if (__syncthreads_or(!ok)) {
       if (tid == 0) record_status(&g_quant_status, kStatusTimeoutTma);
       return;
@@ -474,18 +566,20 @@ __global__ void __launch_bounds__(kQThreads, 1)
 
     const int t = (int)blockIdx.x + it * (int)gridDim.x;
     const int mt = t / a.tiles_k, kt = t - mt * a.tiles_k;
-    const int64_t m0 = (int64_t)mt * kQRows, k0 = (int64_t)kt * kQCols;
-    const uint32_t tile = smem_u32(smem + (size_t)s * Cfg::kTileBytes);
+    const int64_t m0 = (int64_t)mt * kQRows, k0 = (int64_t)kt * kCols;
+    const int valid_cols = (int)min((int64_t)kCols, a.K - k0);
+    const uint32_t tile = smem_u32(smem + (size_t)s * kQTileBytes);
     if constexpr (DO_COL) {
-      col_unit<F32IN, HAD, SR>(tile, hdr, a, m0, k0, denom, key);
-      // The last 64-column tile of a K that is not a multiple of 128 owns the zero padding of
-      // the colblock scale tiles (rows K..K+63 of the last 128-row scale tile).
-      if ((a.K & 127) != 0 && kt == a.tiles_k - 1 && tid < 64) {
-        const int64_t atom = (k0 >> 7) * (a.M >> 6) + 2 * mt + (tid >> 5);
-        st_global_v2(a.col_scale + atom * 512 + (tid & 31) * 16 + 8, 0u, 0u);
-      }
+      const int lane = tid & 31;
+      col_unit<F32IN, HAD, SR>(tile, c, a, m0, k0, lane, 2 * lane < valid_cols, stage_pk, stage_sc);
+      if constexpr (!F32IN)
+        col_unit<F32IN, HAD, SR>(tile, c, a, m0, k0, lane + 32, 2 * (lane + 32) < valid_cols, stage_pk, stage_sc);
     }
-    if constexpr (DO_ROW) row_blocks<F32IN, SR>(tile, hdr, a, m0, k0, mt, kt, denom, key);
+    if constexpr (DO_ROW) row_tile<F32IN, SR>(tile, c, a, m0, k0, mt, kt, valid_cols);
+    if constexpr (DO_COL) {
+      __syncthreads();
+      col_store<F32IN>(a, m0, k0, mt, valid_cols, stage_pk, stage_sc);
+    }
   }
 }
 
@@ -600,7 +694,7 @@ static bool device_is_sm100() {
 template <bool F32IN, bool DO_ROW, bool DO_COL, bool HAD, bool SR>
 static int launch_quant(const CUtensorMap& tmap, const QuantArgs& a, cudaStream_t stream) {
   auto kern = nvfp4_quantize_kernel<F32IN, DO_ROW, DO_COL, HAD, SR>;
-  constexpr size_t smem = quant_smem_bytes<F32IN>();
+  constexpr size_t smem = quant_smem_bytes();
   static bool configured[64] = {false};
   const int dev = rb_host::current_device();
   if (dev >= 0 && dev < 64 && !configured[dev]) {
@@ -759,8 +853,9 @@ int rb_nvfp4_quantize(const void* x, int dtype, int64_t rows, int64_t cols, int6
   a.row_scale = reinterpret_cast<uint8_t*>(row_scale);
   a.col_packed = reinterpret_cast<uint8_t*>(col_packed);
   a.col_scale = reinterpret_cast<uint8_t*>(col_scale);
-  a.tiles_k = (int)(cols / 64);
-  a.n_tiles = (int)((rows / 128) * (cols / 64));
+  const int tile_cols = f32 ? QTile<true>::kCols : QTile<false>::kCols;
+  a.tiles_k = (int)((cols + tile_cols - 1) / tile_cols);
+  a.n_tiles = (int)((rows / 128) * a.tiles_k);
   const bool had = col && hadamard != nullptr;
   const bool sr = seed != nullptr;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
