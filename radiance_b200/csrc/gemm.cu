@@ -145,6 +145,11 @@ __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int
   nt = r / gm;
 }
 
+// Waits with the whole warp and returns a warp-uniform result (false after the ~1 s limit).
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity) {
+  return __all_sync(0xFFFFFFFFu, mbar_wait(bar, parity));
+}
+
 __device__ __forceinline__ void st_global_v4(void* p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   asm volatile("st.global.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
@@ -188,7 +193,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------------ producer
-    if (lane == 0) {
+    // The whole warp runs the loop (warp-uniform operands); one elected lane issues the copies.
+    {
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -197,22 +203,27 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tile_coords((int)blockIdx.x + i * (int)gridDim.x, g.tiles_m, g.tiles_n, mt, nt);
         const bool two_halves = (int64_t)nt * kBN + 128 < g.N;
         for (int ks = 0; ks < g.k_steps; ++ks) {
-          if (!mbar_wait(&sm.empty[stage], phase ^ 1u)) {
-            record_status(&g_gemm_status, kStatusTimeoutProducer);
+          if (!mbar_wait_warp(&sm.empty[stage], phase ^ 1u)) {
+            if (lane == 0) record_status(&g_gemm_status, kStatusTimeoutProducer);
             ok = false;
             break;
           }
           const int nkb = min(4, g.k_blocks - 4 * ks);
           const uint32_t sf_bytes = (uint32_t)nkb * 512u;
-          mbar_arrive_expect_tx(&sm.full[stage], kBM * kStepBytes + kBN * kStepBytes + sf_bytes * (two_halves ? 3u : 2u));
-          tma_load_2d(sm.a[stage], &tmA, &sm.full[stage], ks * kStepBytes, mt * kBM);
-          tma_load_2d(sm.b[stage], &tmB, &sm.full[stage], ks * kStepBytes, nt * kBN);
-          bulk_load(sm.sfa[stage], g.a_scale + ((int64_t)mt * g.k_blocks + 4 * ks) * 512, sf_bytes, &sm.full[stage]);
-          bulk_load(sm.sfb[stage], g.b_scale + ((int64_t)(2 * nt) * g.k_blocks + 4 * ks) * 512, sf_bytes,
-                    &sm.full[stage]);
-          if (two_halves)
-            bulk_load(sm.sfb[stage] + 4 * 512, g.b_scale + ((int64_t)(2 * nt + 1) * g.k_blocks + 4 * ks) * 512,
-                      sf_bytes, &sm.full[stage]);
+          if (elect_one()) {
+            mbar_arrive_expect_tx(&sm.full[stage],
+                                  kBM * kStepBytes + kBN * kStepBytes + sf_bytes * (two_halves ? 3u : 2u));
+            tma_load_2d(sm.a[stage], &tmA, &sm.full[stage], ks * kStepBytes, mt * kBM);
+            tma_load_2d(sm.b[stage], &tmB, &sm.full[stage], ks * kStepBytes, nt * kBN);
+            bulk_load(sm.sfa[stage], g.a_scale + ((int64_t)mt * g.k_blocks + 4 * ks) * 512, sf_bytes,
+                      &sm.full[stage]);
+            bulk_load(sm.sfb[stage], g.b_scale + ((int64_t)(2 * nt) * g.k_blocks + 4 * ks) * 512, sf_bytes,
+                      &sm.full[stage]);
+            if (two_halves)
+              bulk_load(sm.sfb[stage] + 4 * 512, g.b_scale + ((int64_t)(2 * nt + 1) * g.k_blocks + 4 * ks) * 512,
+                        sf_bytes, &sm.full[stage]);
+          }
+          __syncwarp();
           if (++stage == kStages) {
             stage = 0;
             phase ^= 1u;
@@ -222,7 +233,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // The whole warp runs the loop so descriptors stay warp-uniform; one elected lane issues the
+    // tcgen05 instructions (issuing them from a one-lane branch costs ~75 cycles each).
+    {
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -232,41 +245,47 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int width = (int)min((int64_t)kBN, g.N - (int64_t)nt * kBN);
         const uint32_t idesc = idesc_nvf4(width);
         const uint32_t acc = tmem + ((i & 1) ? kAcc1Col : 0);
-        if (i >= 1 && !mbar_wait(&sm.acc_empty, (uint32_t)((i - 1) & 1))) {
-          record_status(&g_gemm_status, kStatusTimeoutEpilogue);
+        if (i >= 1 && !mbar_wait_warp(&sm.acc_empty, (uint32_t)((i - 1) & 1))) {
+          if (lane == 0) record_status(&g_gemm_status, kStatusTimeoutEpilogue);
           break;
         }
         tc_fence_after();
         for (int ks = 0; ks < g.k_steps; ++ks) {
-          if (!mbar_wait(&sm.full[stage], phase)) {
-            record_status(&g_gemm_status, kStatusTimeoutTma);
+          // The TMA bytes are visible to the tensor core once the barrier completes (both are
+          // async-proxy accesses ordered by the mbarrier); no tcgen05 fence is needed here.
+          if (!mbar_wait_warp(&sm.full[stage], phase)) {
+            if (lane == 0) record_status(&g_gemm_status, kStatusTimeoutTma);
             ok = false;
             break;
           }
-          tc_fence_after();
           const int nkb = min(4, g.k_blocks - 4 * ks);
           const uint32_t sfa_s = smem_u32(sm.sfa[stage]), sfb_s = smem_u32(sm.sfb[stage]);
-          for (int kb = 0; kb < nkb; ++kb) {
-            tc_cp_scale(tmem + kSfaCol + 4 * kb, sdesc_scale(sfa_s + kb * 512));
-            tc_cp_scale(tmem + kSfbCol + 8 * kb, sdesc_scale(sfb_s + kb * 512));
-            if (width > 128) tc_cp_scale(tmem + kSfbCol + 8 * kb + 4, sdesc_scale(sfb_s + (4 + kb) * 512));
-          }
           const uint32_t a_s = smem_u32(sm.a[stage]), b_s = smem_u32(sm.b[stage]);
-          for (int kb = 0; kb < nkb; ++kb) {
-            tc_mma_nvf4(acc, sdesc_sw128(a_s + 32 * kb), sdesc_sw128(b_s + 32 * kb), idesc, tmem + kSfaCol + 4 * kb,
-                        tmem + kSfbCol + 8 * kb, (ks > 0 || kb > 0) ? 1u : 0u);
+          if (elect_one()) {
+            for (int kb = 0; kb < nkb; ++kb) {
+              tc_cp_scale(tmem + kSfaCol + 4 * kb, sdesc_scale(sfa_s + kb * 512));
+              tc_cp_scale(tmem + kSfbCol + 8 * kb, sdesc_scale(sfb_s + kb * 512));
+              if (width > 128) tc_cp_scale(tmem + kSfbCol + 8 * kb + 4, sdesc_scale(sfb_s + (4 + kb) * 512));
+            }
+            for (int kb = 0; kb < nkb; ++kb) {
+              tc_mma_nvf4(acc, sdesc_sw128(a_s + 32 * kb), sdesc_sw128(b_s + 32 * kb), idesc, tmem + kSfaCol + 4 * kb,
+                          tmem + kSfbCol + 8 * kb, (ks > 0 || kb > 0) ? 1u : 0u);
+            }
+            tc_commit(&sm.empty[stage]);
           }
-          tc_commit(&sm.empty[stage]);
+          __syncwarp();
           if (++stage == kStages) {
             stage = 0;
             phase ^= 1u;
           }
         }
-        if (ok) tc_commit(&sm.acc_full);
+        if (ok && elect_one()) tc_commit(&sm.acc_full);
+        __syncwarp();
       }
-      // Every MMA this thread issued has finished once `drain` completes.
-      tc_commit(&sm.drain);
-      mbar_wait(&sm.drain, 0);
+      // Every MMA this CTA issued has finished once `drain` completes.
+      if (elect_one()) tc_commit(&sm.drain);
+      __syncwarp();
+      mbar_wait_warp(&sm.drain, 0);
     }
   } else {
     // ------------------------------------------------------------------ epilogue (warps 2..5)
@@ -340,6 +359,310 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 1) tmem_dealloc(tmem, 512);
 }
 
+
+// =============================================================================================
+// Two-SM variant: a cluster of two CTAs computes a 256 x 256 tile with tcgen05 cta_group::2.
+//
+// CTA r of the pair loads A rows [256 mt + 128 r, +128) and B rows [256 nt + 128 r, +128) with
+// their scale atoms, plus the scale atoms of all 256 B rows (each CTA's tensor core multiplies
+// its 128 rows by the whole B tile).  All loads of both CTAs complete on the leader's (rank 0)
+// barrier; the leader alone issues tcgen05.cp / tcgen05.mma with cta_group::2, which read the
+// same shared-memory offsets in both CTAs and write the same TMEM columns in both.  The leader's
+// commits arrive on both CTAs' barriers (multicast commit), and the peer's epilogue warps release
+// the shared accumulator columns on the leader's barrier.  One 256x256x64 MMA and three scale
+// copies serve two SMs, half the per-FLOP issue and copy work of the one-SM kernel.
+// =============================================================================================
+constexpr int kStages2 = 5;
+constexpr int kSfStep = 2048;  // one K step's scale atoms for 128 rows (4 x 512 B)
+
+struct Gemm2Smem {
+  uint8_t a[kStages2][kBM * kStepBytes];  // this CTA's 128 A rows (16 KB)
+  uint8_t b[kStages2][kBM * kStepBytes];  // this CTA's 128 of the tile's 256 B rows (16 KB)
+  uint8_t sfa[kStages2][kSfStep];         // scale atoms of this CTA's A rows
+  uint8_t sfb[kStages2][2 * kSfStep];     // scale atoms of all 256 B rows: [half][k block]
+  uint64_t full[kStages2];                // leader: both CTAs' loads of a stage
+  uint64_t empty[kStages2];               // each CTA: the leader's MMAs finished with a stage
+  uint64_t acc_full;                      // each CTA: the accumulator of a tile is complete
+  uint64_t acc_empty;                     // leader: the pair's 8 epilogue warps drained the shared columns
+  uint64_t drain;
+  uint32_t tmem_base;
+};
+
+constexpr uint32_t kStageBytes2 = 2 * kBM * kStepBytes + 3 * kSfStep;  // per CTA
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_id() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_count() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_alloc2(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish2() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc2(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// Arrives on the barrier at the same shared-memory offset in each CTA of `mask`.
+__device__ __forceinline__ void tc_commit2(uint64_t* bar, uint16_t mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"(mask)
+      : "memory");
+}
+__device__ __forceinline__ void tc_cp_scale2(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+__device__ __forceinline__ void tc_mma_nvf4_2sm(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                                uint32_t sfa_tmem, uint32_t sfb_tmem, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.scale_vec::4X [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(
+          d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+// TMA tile load into this CTA's shared memory that completes on the leader CTA's barrier.
+__device__ __forceinline__ void tma_load_2d_to_leader(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int x,
+                                                      int y) {
+  const uint32_t leader_bar = smem_u32(bar) & 0xFEFFFFFFu;
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
+      "%4}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(map), "r"(leader_bar), "r"(x), "r"(y)
+      : "memory");
+}
+// Arrive on the barrier at the same offset in the leader CTA.
+__device__ __forceinline__ void mbar_arrive_leader(uint64_t* bar) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(remote) : "r"(smem_u32(bar)));
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote) : "memory");
+}
+
+__host__ __device__ constexpr uint32_t idesc_nvf4_m256(int n) {
+  return (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
+}
+
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    nvfp4_gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                       const __grid_constant__ CUtensorMap tmSA, const __grid_constant__ CUtensorMap tmSB,
+                       const GemmArgs g) {
+  extern __shared__ uint8_t smem_raw[];
+  Gemm2Smem& sm = *reinterpret_cast<Gemm2Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const int cid = (int)cluster_id(), ncl = (int)cluster_count();
+  const int n_my = (cid < g.n_tiles) ? (g.n_tiles - cid + ncl - 1) / ncl : 0;  // n_tiles counts 256x256 tiles
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages2; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], 1);
+    }
+    mbar_init(&sm.acc_full, 1);
+    mbar_init(&sm.acc_empty, 8);
+    mbar_init(&sm.drain, 1);
+    fence_mbar_init();
+    prefetch_tensormap(&tmA);
+    prefetch_tensormap(&tmB);
+    prefetch_tensormap(&tmSA);
+    prefetch_tensormap(&tmSB);
+  }
+  if (warp == 1) {
+    tmem_alloc2(&sm.tmem_base, 512);
+    tmem_relinquish2();
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ producer (both CTAs)
+    {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int i = 0; i < n_my && ok; ++i) {
+        int mt, nt;
+        tile_coords(cid + i * ncl, g.tiles_m, g.tiles_n, mt, nt);
+        const int arow = 2 * mt + (int)rank;  // this CTA's 128-row tile of A
+        // Each CTA supplies half of the tile's B rows: 128 for a 256-wide tile, 64 for a 128-wide
+        // tail (rows loaded past that half are never read by the MMA).
+        const int width = (int)min((int64_t)kBN, g.N - (int64_t)nt * kBN);
+        const int brow = nt * kBN + (int)rank * (width / 2);
+        for (int ks = 0; ks < g.k_steps; ++ks) {
+          if (!mbar_wait_warp(&sm.empty[stage], phase ^ 1u)) {
+            if (lane == 0) record_status(&g_gemm_status, kStatusTimeoutProducer);
+            ok = false;
+            break;
+          }
+          if (elect_one()) {
+            if (rank == 0) mbar_arrive_expect_tx(&sm.full[stage], 2 * kStageBytes2);
+            tma_load_2d_to_leader(sm.a[stage], &tmA, &sm.full[stage], ks * kStepBytes, arow * kBM);
+            tma_load_2d_to_leader(sm.b[stage], &tmB, &sm.full[stage], ks * kStepBytes, brow);
+            tma_load_2d_to_leader(sm.sfa[stage], &tmSA, &sm.full[stage], 0, (arow * g.k_blocks + 4 * ks) * 2);
+            tma_load_2d_to_leader(sm.sfb[stage], &tmSB, &sm.full[stage], 0, ((2 * nt) * g.k_blocks + 4 * ks) * 2);
+            tma_load_2d_to_leader(sm.sfb[stage] + kSfStep, &tmSB, &sm.full[stage], 0,
+                                  ((2 * nt + 1) * g.k_blocks + 4 * ks) * 2);
+          }
+          __syncwarp();
+          if (++stage == kStages2) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer (leader only)
+    if (rank == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int i = 0; i < n_my && ok; ++i) {
+        int mt, nt;
+        tile_coords(cid + i * ncl, g.tiles_m, g.tiles_n, mt, nt);
+        const int width = (int)min((int64_t)kBN, g.N - (int64_t)nt * kBN);
+        const uint32_t idesc = idesc_nvf4_m256(width);
+        const uint32_t acc = tmem + ((i & 1) ? kAcc1Col : 0);
+        if (i >= 1 && !mbar_wait_warp(&sm.acc_empty, (uint32_t)((i - 1) & 1))) {
+          if (lane == 0) record_status(&g_gemm_status, kStatusTimeoutEpilogue);
+          break;
+        }
+        tc_fence_after();
+        for (int ks = 0; ks < g.k_steps; ++ks) {
+          if (!mbar_wait_warp(&sm.full[stage], phase)) {
+            if (lane == 0) record_status(&g_gemm_status, kStatusTimeoutTma);
+            ok = false;
+            break;
+          }
+          const int nkb = min(4, g.k_blocks - 4 * ks);
+          const uint32_t sfa_s = smem_u32(sm.sfa[stage]), sfb_s = smem_u32(sm.sfb[stage]);
+          const uint32_t a_s = smem_u32(sm.a[stage]), b_s = smem_u32(sm.b[stage]);
+          if (elect_one()) {
+            for (int kb = 0; kb < nkb; ++kb) {
+              tc_cp_scale2(tmem + kSfaCol + 4 * kb, sdesc_scale(sfa_s + kb * 512));
+              tc_cp_scale2(tmem + kSfbCol + 8 * kb, sdesc_scale(sfb_s + kb * 512));
+              if (width > 128) tc_cp_scale2(tmem + kSfbCol + 8 * kb + 4, sdesc_scale(sfb_s + kSfStep + kb * 512));
+            }
+            for (int kb = 0; kb < nkb; ++kb) {
+              tc_mma_nvf4_2sm(acc, sdesc_sw128(a_s + 32 * kb), sdesc_sw128(b_s + 32 * kb), idesc,
+                              tmem + kSfaCol + 4 * kb, tmem + kSfbCol + 8 * kb, (ks > 0 || kb > 0) ? 1u : 0u);
+            }
+            tc_commit2(&sm.empty[stage], 0x3);
+          }
+          __syncwarp();
+          if (++stage == kStages2) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (ok && elect_one()) tc_commit2(&sm.acc_full, 0x3);
+        __syncwarp();
+      }
+      // Every MMA of the pair has finished once `drain` completes.
+      if (elect_one()) tc_commit2(&sm.drain, 0x1);
+      __syncwarp();
+      mbar_wait_warp(&sm.drain, 0);
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue (warps 2..5, both CTAs)
+    const int q = warp & 3;  // TMEM lanes 32q .. 32q+31
+    float alpha = 1.0f;
+    if (g.alpha_a != nullptr) alpha = *g.alpha_a;
+    if (g.alpha_b != nullptr) alpha = __fmul_rn(alpha, *g.alpha_b);
+    for (int i = 0; i < n_my; ++i) {
+      int mt, nt;
+      tile_coords(cid + i * ncl, g.tiles_m, g.tiles_n, mt, nt);
+      const int width = (int)min((int64_t)kBN, g.N - (int64_t)nt * kBN);
+      const int buf = i & 1;
+      const int base_col = buf ? kAcc1Col : 0;
+      if (!mbar_wait(&sm.acc_full, (uint32_t)(i & 1))) {
+        record_status(&g_gemm_status, kStatusTimeoutMma);
+        break;
+      }
+      tc_fence_after();
+      const int nch = width / kEpiChunk;
+      const int first = (buf == 0) ? ((width == kBN) ? nch - 1 : -1) : 0;
+      auto release = [&]() {
+        if (rank == 0) mbar_arrive(&sm.acc_empty);
+        else mbar_arrive_leader(&sm.acc_empty);
+      };
+      if (first < 0 && lane == 0) release();
+      const int64_t row = (int64_t)mt * 256 + (int64_t)rank * kBM + 32 * q + lane;
+      const bool row_ok = row < g.M;
+      for (int step = 0; step < nch; ++step) {
+        const int c = (first < 0) ? step : (step == 0 ? first : (buf == 0 ? step - 1 : step));
+        uint32_t r[kEpiChunk];
+        const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(base_col + c * kEpiChunk);
+        RB_TMEM_LD_X32(taddr, r);
+        RB_TMEM_LD_X32(taddr + 32, (r + 32));
+        tmem_ld_wait();
+        if (step == 0 && first >= 0) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) release();
+        }
+        if (!row_ok) continue;
+        const int64_t col0 = (int64_t)nt * kBN + c * kEpiChunk;
+        float v[kEpiChunk];
+#pragma unroll
+        for (int j = 0; j < kEpiChunk; ++j) v[j] = __fmul_rn(__uint_as_float(r[j]), alpha);
+        if (g.bias != nullptr) {
+          if (g.bias_f32) {
+            const float* bp = reinterpret_cast<const float*>(g.bias) + col0;
+#pragma unroll
+            for (int j = 0; j < kEpiChunk; ++j) v[j] = __fadd_rn(v[j], __ldg(bp + j));
+          } else {
+            const __nv_bfloat16* bp = reinterpret_cast<const __nv_bfloat16*>(g.bias) + col0;
+#pragma unroll
+            for (int j = 0; j < kEpiChunk; ++j) v[j] = __fadd_rn(v[j], __bfloat162float(bp[j]));
+          }
+        }
+        if (g.out_f32) {
+          float* op = reinterpret_cast<float*>(g.out) + row * g.ldo + col0;
+#pragma unroll
+          for (int j = 0; j < kEpiChunk; j += 4)
+            st_global_v4(op + j, __float_as_uint(v[j]), __float_as_uint(v[j + 1]), __float_as_uint(v[j + 2]),
+                         __float_as_uint(v[j + 3]));
+        } else {
+          __nv_bfloat16* op = reinterpret_cast<__nv_bfloat16*>(g.out) + row * g.ldo + col0;
+#pragma unroll
+          for (int j = 0; j < kEpiChunk; j += 8)
+            st_global_v4(op + j, pack_bf16x2(v[j], v[j + 1]), pack_bf16x2(v[j + 2], v[j + 3]),
+                         pack_bf16x2(v[j + 4], v[j + 5]), pack_bf16x2(v[j + 6], v[j + 7]));
+        }
+      }
+    }
+  }
+
+  // Both CTAs stay until every MMA of the pair is done (the leader drained them above), then free
+  // the pair's tensor memory together.
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc2(tmem, 512);
+}
+
 }  // namespace rb
 
 // =============================================================================================
@@ -394,12 +717,6 @@ int rb_nvfp4_gemm(const void* a_packed, const void* a_scale, const void* b_packe
     rb_host::set_error("nvfp4 gemm: the current device is not an sm_100 GPU");
     return RB_ERR_DEVICE;
   }
-  CUtensorMap tmA, tmB;
-  if (!rb_host::make_tmap_2d(&tmA, a_packed, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)(k / 2), (uint64_t)m,
-                             (uint64_t)(k / 2), kStepBytes, kBM, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !rb_host::make_tmap_2d(&tmB, b_packed, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)(k / 2), (uint64_t)n,
-                             (uint64_t)(k / 2), kStepBytes, kBN, CU_TENSOR_MAP_SWIZZLE_128B))
-    return RB_ERR_CUDA;
   GemmArgs g;
   g.M = m;
   g.N = n;
@@ -413,25 +730,78 @@ int rb_nvfp4_gemm(const void* a_packed, const void* a_scale, const void* b_packe
   g.out = out;
   g.out_f32 = out_dtype == RB_OUT_F32;
   g.ldo = ldo;
-  g.tiles_m = (int)(m / kBM);
-  g.tiles_n = (int)((n + kBN - 1) / kBN);
-  g.n_tiles = g.tiles_m * g.tiles_n;
   g.k_blocks = (int)(k / 64);
   g.k_steps = (g.k_blocks + 3) / 4;
-  const size_t smem = sizeof(GemmSmem) + 1024;
-  static bool configured[64] = {false};
-  if (dev >= 0 && dev < 64 && !configured[dev]) {
-    if (cudaFuncSetAttribute(nvfp4_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-        cudaSuccess) {
-      rb_host::set_error("cudaFuncSetAttribute(gemm) failed: %s", cudaGetErrorString(cudaGetLastError()));
-      return RB_ERR_CUDA;
-    }
-    configured[dev] = true;
-  }
+  g.tiles_n = (int)((n + kBN - 1) / kBN);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const int sms = rb_host::num_sms(dev);
-  const int grid = g.n_tiles < sms ? g.n_tiles : sms;
-  nvfp4_gemm_kernel<<<grid, kGemmThreads, smem, reinterpret_cast<cudaStream_t>(stream)>>>(tmA, tmB, g);
-  const cudaError_t e = cudaGetLastError();
+  const bool two_sm = m >= 256;
+  CUtensorMap tmA, tmB;
+  if (!rb_host::make_tmap_2d(&tmA, a_packed, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)(k / 2), (uint64_t)m,
+                             (uint64_t)(k / 2), kStepBytes, kBM, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !rb_host::make_tmap_2d(&tmB, b_packed, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)(k / 2), (uint64_t)n,
+                             (uint64_t)(k / 2), kStepBytes, two_sm ? kBM : kBN, CU_TENSOR_MAP_SWIZZLE_128B))
+    return RB_ERR_CUDA;
+  cudaError_t e = cudaSuccess;
+  if (two_sm) {
+    // Scale buffers viewed as rows of 256 bytes (half a 512-byte atom): one K step of one 128-row
+    // tile is 8 consecutive rows.
+    CUtensorMap tmSA, tmSB;
+    if (!rb_host::make_tmap_2d(&tmSA, a_scale, CU_TENSOR_MAP_DATA_TYPE_UINT8, 256, (uint64_t)(m / 128) * (k / 64) * 2,
+                               256, 256, 8, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !rb_host::make_tmap_2d(&tmSB, b_scale, CU_TENSOR_MAP_DATA_TYPE_UINT8, 256, (uint64_t)(n / 128) * (k / 64) * 2,
+                               256, 256, 8, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return RB_ERR_CUDA;
+    g.tiles_m = (int)((m + 255) / 256);
+    g.n_tiles = g.tiles_m * g.tiles_n;
+    const size_t smem = sizeof(Gemm2Smem) + 1024;
+    static int max_clusters[64] = {0};
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(kGemmThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (dev >= 0 && dev < 64 && max_clusters[dev] == 0) {
+      if (cudaFuncSetAttribute(nvfp4_gemm2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+          cudaSuccess) {
+        rb_host::set_error("cudaFuncSetAttribute(gemm2) failed: %s", cudaGetErrorString(cudaGetLastError()));
+        return RB_ERR_CUDA;
+      }
+      cfg.gridDim = dim3(2 * (sms / 2), 1, 1);
+      int nc = 0;
+      if (cudaOccupancyMaxActiveClusters(&nc, nvfp4_gemm2_kernel, &cfg) != cudaSuccess || nc < 1) {
+        cudaGetLastError();
+        nc = sms / 2;
+      }
+      max_clusters[dev] = nc;
+    }
+    const int cap = (dev >= 0 && dev < 64) ? max_clusters[dev] : sms / 2;
+    const int clusters = g.n_tiles < cap ? g.n_tiles : cap;
+    cfg.gridDim = dim3(2 * clusters, 1, 1);
+    e = cudaLaunchKernelEx(&cfg, nvfp4_gemm2_kernel, tmA, tmB, tmSA, tmSB, g);
+  } else {
+    g.tiles_m = (int)(m / kBM);
+    g.n_tiles = g.tiles_m * g.tiles_n;
+    const size_t smem = sizeof(GemmSmem) + 1024;
+    static bool configured[64] = {false};
+    if (dev >= 0 && dev < 64 && !configured[dev]) {
+      if (cudaFuncSetAttribute(nvfp4_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+          cudaSuccess) {
+        rb_host::set_error("cudaFuncSetAttribute(gemm) failed: %s", cudaGetErrorString(cudaGetLastError()));
+        return RB_ERR_CUDA;
+      }
+      configured[dev] = true;
+    }
+    const int grid = g.n_tiles < sms ? g.n_tiles : sms;
+    nvfp4_gemm_kernel<<<grid, kGemmThreads, smem, st>>>(tmA, tmB, g);
+  }
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) {
     rb_host::set_error("nvfp4 gemm launch failed: %s", cudaGetErrorString(e));
     return RB_ERR_CUDA;
