@@ -13,12 +13,12 @@
 //                        the quantizer (SWIZZLE_32_4_4: one 512-byte atom per 128 rows x 4 scale
 //                        columns) is exactly what tcgen05.cp.32x128b.warpx4 moves into tensor
 //                        memory, so scales go global -> shared -> TMEM untouched.
-//   warp 1 (one lane)  : MMA issuer.  tcgen05.cp for the scales, then four
-//                        tcgen05.mma.kind::mxf4nvf4.block_scale.scale_vec::4X (128 x 256 x 64) per
-//                        K step into a TMEM accumulator; tcgen05.commit frees the smem stage.
+//   warp 1 (one lane)  : MMA issuer.  Per 64-wide K block, tcgen05.cp of its scale atoms and one
+//                        tcgen05.mma.kind::mxf4nvf4.block_scale.scale_vec::4X (128 x 256 x 64) into
+//                        a TMEM accumulator; tcgen05.commit frees the smem stage.
 //   warps 2-5          : epilogue.  tcgen05.ld the accumulator (each warp owns 32 TMEM lanes =
 //                        32 output rows), alpha = ga * gb and bias applied in fp32, one rounding to
-//                        bf16 or fp32, stored straight to global memory.
+//                        bf16 or fp32, staged in swizzled shared memory and written by TMA stores.
 // The two accumulator buffers share TMEM columns: buffer 0 is columns [0, 256), buffer 1 is
 // [192, 448), and the scale factors live in [448, 512).  The epilogue drains the shared 64
 // columns first and releases them, so the next tile's MMAs start while the rest drains.
@@ -33,7 +33,7 @@ __device__ uint32_t g_gemm_status;
 constexpr int kBM = 128;            // tile rows (M) = TMEM lanes
 constexpr int kBN = 256;            // tile cols (N)
 constexpr int kStepBytes = 128;     // packed bytes of one K step (256 e2m1 values)
-constexpr int kStages = 4;
+constexpr int kStages = 3;
 constexpr int kOverlap = 64;        // TMEM columns shared by the two accumulator buffers
 constexpr int kAcc1Col = kBN - kOverlap;   // 192
 constexpr int kSfaCol = 512 - kOverlap;    // 448: 4 columns per 64-wide K block (16 total)
@@ -47,6 +47,7 @@ struct GemmSmem {
   uint8_t b[kStages][kBN * kStepBytes];   // 32 KB per stage
   uint8_t sfa[kStages][4 * 512];          // 4 K-blocks x one 128-row atom
   uint8_t sfb[kStages][8 * 512];          // [row half h][K-block kb] at (4h + kb) * 512
+  uint8_t out[4][2][4096];                // per epilogue warp: two staged output boxes
   uint64_t full[kStages];
   uint64_t empty[kStages];
   uint64_t acc_full;
@@ -150,13 +151,108 @@ __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity) {
   return __all_sync(0xFFFFFFFFu, mbar_wait(bar, parity));
 }
 
-__device__ __forceinline__ void st_global_v4(void* p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-  asm volatile("st.global.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
-}
-
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+// Orders this thread's generic-proxy shared-memory writes before later async-proxy (TMA) reads.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t smem_src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(map),
+               "r"(smem_src), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Waits until at most N committed bulk groups of this thread still read their shared-memory source.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+constexpr int kOutBox = 4096;  // one staged output box: 32 rows x 128 B
+
+// One 32-row x 64-column piece of the output: this warp's 32 accumulator lanes (one output row per
+// lane), times alpha, plus bias, rounded once to the output type.  The rows are staged in shared
+// memory in the 128-byte-swizzled layout of the output tensor map (16-byte chunk c of row r at
+// r * 128 + (c ^ (r % 8)) * 16, which also makes the 32 lanes' writes bank-conflict free) and
+// written by one TMA store, so the global write is a few full-line bursts instead of 32 rows of
+// scattered 16-byte stores.  `slots` is the warp's two staged boxes (8 KB, 1024-byte aligned):
+// bf16 pieces alternate between them, fp32 pieces (two boxes of 32 columns) use both.  Rows at or
+// past M (the upper half of a 256-row tile when M % 256 == 128) are not stored.
+__device__ __forceinline__ void epilogue_piece(const uint32_t (&r)[kEpiChunk], float alpha, const GemmArgs& g,
+                                               const CUtensorMap* tmO, uint32_t slots, int& slot, int col0,
+                                               int64_t row0, int lane) {
+  float v[kEpiChunk];
+#pragma unroll
+  for (int j = 0; j < kEpiChunk; ++j) v[j] = __fmul_rn(__uint_as_float(r[j]), alpha);
+  if (g.bias != nullptr) {
+    if (g.bias_f32) {
+      const float4* bp = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(g.bias) + col0);
+#pragma unroll
+      for (int j = 0; j < kEpiChunk / 4; ++j) {
+        const float4 b = __ldg(bp + j);
+        v[4 * j] = __fadd_rn(v[4 * j], b.x);
+        v[4 * j + 1] = __fadd_rn(v[4 * j + 1], b.y);
+        v[4 * j + 2] = __fadd_rn(v[4 * j + 2], b.z);
+        v[4 * j + 3] = __fadd_rn(v[4 * j + 3], b.w);
+      }
+    } else {
+      const uint4* bp = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(g.bias) + col0);
+#pragma unroll
+      for (int j = 0; j < kEpiChunk / 8; ++j) {
+        const uint4 b = __ldg(bp + j);
+        const uint32_t w[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          v[8 * j + 2 * h] = __fadd_rn(v[8 * j + 2 * h], __uint_as_float(w[h] << 16));
+          v[8 * j + 2 * h + 1] = __fadd_rn(v[8 * j + 2 * h + 1], __uint_as_float(w[h] & 0xFFFF0000u));
+        }
+      }
+    }
+  }
+  const bool store = row0 < g.M;
+  const uint32_t row_off = (uint32_t)lane * 128u, sw = (uint32_t)(lane & 7);
+  if (g.out_f32) {
+    if (lane == 0) bulk_wait_read<0>();
+    __syncwarp();
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int c = 0; c < 8; ++c)
+        st_shared_v4(slots + h * kOutBox + row_off + ((c ^ sw) << 4), __float_as_uint(v[32 * h + 4 * c]),
+                     __float_as_uint(v[32 * h + 4 * c + 1]), __float_as_uint(v[32 * h + 4 * c + 2]),
+                     __float_as_uint(v[32 * h + 4 * c + 3]));
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0 && store) {
+      tma_store_2d(tmO, slots, col0, (int)row0);
+      tma_store_2d(tmO, slots + kOutBox, col0 + 32, (int)row0);
+      bulk_commit_group();
+    }
+  } else {
+    if (lane == 0) bulk_wait_read<1>();
+    __syncwarp();
+    const uint32_t box = slots + (uint32_t)slot * kOutBox;
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+      st_shared_v4(box + row_off + ((c ^ sw) << 4), pack_bf16x2(v[8 * c], v[8 * c + 1]),
+                   pack_bf16x2(v[8 * c + 2], v[8 * c + 3]), pack_bf16x2(v[8 * c + 4], v[8 * c + 5]),
+                   pack_bf16x2(v[8 * c + 6], v[8 * c + 7]));
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0 && store) {
+      tma_store_2d(tmO, box, col0, (int)row0);
+      bulk_commit_group();
+    }
+    slot ^= 1;
+  }
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -164,7 +260,7 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 // ---------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(kGemmThreads, 1)
     nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                      const GemmArgs g) {
+                      const __grid_constant__ CUtensorMap tmO, const GemmArgs g) {
   extern __shared__ uint8_t smem_raw[];
   GemmSmem& sm = *reinterpret_cast<GemmSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -181,6 +277,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     fence_mbar_init();
     prefetch_tensormap(&tmA);
     prefetch_tensormap(&tmB);
+    prefetch_tensormap(&tmO);
   }
   if (warp == 1) {
     tmem_alloc(&sm.tmem_base, 512);
@@ -245,11 +342,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int width = (int)min((int64_t)kBN, g.N - (int64_t)nt * kBN);
         const uint32_t idesc = idesc_nvf4(width);
         const uint32_t acc = tmem + ((i & 1) ? kAcc1Col : 0);
-        if (i >= 1 && !mbar_wait_warp(&sm.acc_empty, (uint32_t)((i - 1) & 1))) {
-          if (lane == 0) record_status(&g_gemm_status, kStatusTimeoutEpilogue);
-          break;
-        }
-        tc_fence_after();
         for (int ks = 0; ks < g.k_steps; ++ks) {
           // The TMA bytes are visible to the tensor core once the barrier completes (both are
           // async-proxy accesses ordered by the mbarrier); no tcgen05 fence is needed here.
@@ -261,13 +353,25 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const int nkb = min(4, g.k_blocks - 4 * ks);
           const uint32_t sfa_s = smem_u32(sm.sfa[stage]), sfb_s = smem_u32(sm.sfb[stage]);
           const uint32_t a_s = smem_u32(sm.a[stage]), b_s = smem_u32(sm.b[stage]);
-          if (elect_one()) {
-            for (int kb = 0; kb < nkb; ++kb) {
-              tc_cp_scale(tmem + kSfaCol + 4 * kb, sdesc_scale(sfa_s + kb * 512));
-              tc_cp_scale(tmem + kSfbCol + 8 * kb, sdesc_scale(sfb_s + kb * 512));
-              if (width > 128) tc_cp_scale(tmem + kSfbCol + 8 * kb + 4, sdesc_scale(sfb_s + (4 + kb) * 512));
+          auto copy_scales = [&](int kb) {
+            tc_cp_scale(tmem + kSfaCol + 4 * kb, sdesc_scale(sfa_s + kb * 512));
+            tc_cp_scale(tmem + kSfbCol + 8 * kb, sdesc_scale(sfb_s + kb * 512));
+            if (width > 128) tc_cp_scale(tmem + kSfbCol + 8 * kb + 4, sdesc_scale(sfb_s + (4 + kb) * 512));
+          };
+          if (ks == 0 && i >= 1) {
+            if (!mbar_wait_warp(&sm.acc_empty, (uint32_t)((i - 1) & 1))) {
+              if (lane == 0) record_status(&g_gemm_status, kStatusTimeoutEpilogue);
+              ok = false;
+              break;
             }
+            tc_fence_after();
+          }
+          if (elect_one()) {
+            // An MMA starts only after every scale copy issued before it has landed, so each K
+            // block's copies go directly before its own MMA (all copies of a step first costs ~20%,
+            // copies one block ahead cost more, not less).
             for (int kb = 0; kb < nkb; ++kb) {
+              copy_scales(kb);
               tc_mma_nvf4(acc, sdesc_sw128(a_s + 32 * kb), sdesc_sw128(b_s + 32 * kb), idesc, tmem + kSfaCol + 4 * kb,
                           tmem + kSfbCol + 8 * kb, (ks > 0 || kb > 0) ? 1u : 0u);
             }
@@ -290,6 +394,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else {
     // ------------------------------------------------------------------ epilogue (warps 2..5)
     const int q = warp & 3;  // TMEM lanes 32q .. 32q+31
+    const uint32_t slots = smem_u32(sm.out[q]);
+    int slot = 0;
     float alpha = 1.0f;
     if (g.alpha_a != nullptr) alpha = *g.alpha_a;
     if (g.alpha_b != nullptr) alpha = __fmul_rn(alpha, *g.alpha_b);
@@ -308,7 +414,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       // Chunks of this buffer that lie in the shared columns [192, 256) go first.
       const int first = (buf == 0) ? ((width == kBN) ? nch - 1 : -1) : 0;
       if (first < 0 && lane == 0) mbar_arrive(&sm.acc_empty);
-      const int64_t row = (int64_t)mt * kBM + 32 * q + lane;
+      const int64_t row0 = (int64_t)mt * kBM + 32 * q;
       for (int step = 0; step < nch; ++step) {
         const int c = (first < 0) ? step : (step == 0 ? first : (buf == 0 ? step - 1 : step));
         uint32_t r[kEpiChunk];
@@ -321,36 +427,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(&sm.acc_empty);
         }
-        const int64_t col0 = (int64_t)nt * kBN + c * kEpiChunk;
-        float v[kEpiChunk];
-#pragma unroll
-        for (int j = 0; j < kEpiChunk; ++j) v[j] = __fmul_rn(__uint_as_float(r[j]), alpha);
-        if (g.bias != nullptr) {
-          if (g.bias_f32) {
-            const float* bp = reinterpret_cast<const float*>(g.bias) + col0;
-#pragma unroll
-            for (int j = 0; j < kEpiChunk; ++j) v[j] = __fadd_rn(v[j], __ldg(bp + j));
-          } else {
-            const __nv_bfloat16* bp = reinterpret_cast<const __nv_bfloat16*>(g.bias) + col0;
-#pragma unroll
-            for (int j = 0; j < kEpiChunk; ++j) v[j] = __fadd_rn(v[j], __bfloat162float(bp[j]));
-          }
-        }
-        if (g.out_f32) {
-          float* op = reinterpret_cast<float*>(g.out) + row * g.ldo + col0;
-#pragma unroll
-          for (int j = 0; j < kEpiChunk; j += 4)
-            st_global_v4(op + j, __float_as_uint(v[j]), __float_as_uint(v[j + 1]), __float_as_uint(v[j + 2]),
-                         __float_as_uint(v[j + 3]));
-        } else {
-          __nv_bfloat16* op = reinterpret_cast<__nv_bfloat16*>(g.out) + row * g.ldo + col0;
-#pragma unroll
-          for (int j = 0; j < kEpiChunk; j += 8)
-            st_global_v4(op + j, pack_bf16x2(v[j], v[j + 1]), pack_bf16x2(v[j + 2], v[j + 3]),
-                         pack_bf16x2(v[j + 4], v[j + 5]), pack_bf16x2(v[j + 6], v[j + 7]));
-        }
+        epilogue_piece(r, alpha, g, &tmO, slots, slot, nt * kBN + c * kEpiChunk, row0, lane);
       }
     }
+    // The staged boxes must not be overwritten or freed while a TMA store still reads them.
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -380,6 +462,7 @@ struct Gemm2Smem {
   uint8_t b[kStages2][kBM * kStepBytes];  // this CTA's 128 of the tile's 256 B rows (16 KB)
   uint8_t sfa[kStages2][kSfStep];         // scale atoms of this CTA's A rows
   uint8_t sfb[kStages2][2 * kSfStep];     // scale atoms of all 256 B rows: [half][k block]
+  uint8_t out[4][2][4096];                // per epilogue warp: two staged output boxes
   uint64_t full[kStages2];                // leader: both CTAs' loads of a stage
   uint64_t empty[kStages2];               // each CTA: the leader's MMAs finished with a stage
   uint64_t acc_full;                      // each CTA: the accumulator of a tile is complete
@@ -464,7 +547,7 @@ __host__ __device__ constexpr uint32_t idesc_nvf4_m256(int n) {
 __global__ void __launch_bounds__(kGemmThreads, 1)
     nvfp4_gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                        const __grid_constant__ CUtensorMap tmSA, const __grid_constant__ CUtensorMap tmSB,
-                       const GemmArgs g) {
+                       const __grid_constant__ CUtensorMap tmO, const GemmArgs g) {
   extern __shared__ uint8_t smem_raw[];
   Gemm2Smem& sm = *reinterpret_cast<Gemm2Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -485,6 +568,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     prefetch_tensormap(&tmB);
     prefetch_tensormap(&tmSA);
     prefetch_tensormap(&tmSB);
+    prefetch_tensormap(&tmO);
   }
   if (warp == 1) {
     tmem_alloc2(&sm.tmem_base, 512);
@@ -544,11 +628,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int width = (int)min((int64_t)kBN, g.N - (int64_t)nt * kBN);
         const uint32_t idesc = idesc_nvf4_m256(width);
         const uint32_t acc = tmem + ((i & 1) ? kAcc1Col : 0);
-        if (i >= 1 && !mbar_wait_warp(&sm.acc_empty, (uint32_t)((i - 1) & 1))) {
-          if (lane == 0) record_status(&g_gemm_status, kStatusTimeoutEpilogue);
-          break;
-        }
-        tc_fence_after();
         for (int ks = 0; ks < g.k_steps; ++ks) {
           if (!mbar_wait_warp(&sm.full[stage], phase)) {
             if (lane == 0) record_status(&g_gemm_status, kStatusTimeoutTma);
@@ -558,13 +637,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const int nkb = min(4, g.k_blocks - 4 * ks);
           const uint32_t sfa_s = smem_u32(sm.sfa[stage]), sfb_s = smem_u32(sm.sfb[stage]);
           const uint32_t a_s = smem_u32(sm.a[stage]), b_s = smem_u32(sm.b[stage]);
-          if (elect_one()) {
-            for (int kb = 0; kb < nkb; ++kb) {
-              tc_cp_scale2(tmem + kSfaCol + 4 * kb, sdesc_scale(sfa_s + kb * 512));
-              tc_cp_scale2(tmem + kSfbCol + 8 * kb, sdesc_scale(sfb_s + kb * 512));
-              if (width > 128) tc_cp_scale2(tmem + kSfbCol + 8 * kb + 4, sdesc_scale(sfb_s + kSfStep + kb * 512));
+          auto copy_scales = [&](int kb) {
+            tc_cp_scale2(tmem + kSfaCol + 4 * kb, sdesc_scale(sfa_s + kb * 512));
+            tc_cp_scale2(tmem + kSfbCol + 8 * kb, sdesc_scale(sfb_s + kb * 512));
+            if (width > 128) tc_cp_scale2(tmem + kSfbCol + 8 * kb + 4, sdesc_scale(sfb_s + kSfStep + kb * 512));
+          };
+          if (ks == 0 && i >= 1) {
+            if (!mbar_wait_warp(&sm.acc_empty, (uint32_t)((i - 1) & 1))) {
+              if (lane == 0) record_status(&g_gemm_status, kStatusTimeoutEpilogue);
+              ok = false;
+              break;
             }
+            tc_fence_after();
+          }
+          if (elect_one()) {
+            // As in the one-SM kernel, each K block's scale copies directly precede its MMA.
             for (int kb = 0; kb < nkb; ++kb) {
+              copy_scales(kb);
               tc_mma_nvf4_2sm(acc, sdesc_sw128(a_s + 32 * kb), sdesc_sw128(b_s + 32 * kb), idesc,
                               tmem + kSfaCol + 4 * kb, tmem + kSfbCol + 8 * kb, (ks > 0 || kb > 0) ? 1u : 0u);
             }
@@ -587,6 +676,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else {
     // ------------------------------------------------------------------ epilogue (warps 2..5, both CTAs)
     const int q = warp & 3;  // TMEM lanes 32q .. 32q+31
+    const uint32_t slots = smem_u32(sm.out[q]);
+    int slot = 0;
     float alpha = 1.0f;
     if (g.alpha_a != nullptr) alpha = *g.alpha_a;
     if (g.alpha_b != nullptr) alpha = __fmul_rn(alpha, *g.alpha_b);
@@ -608,8 +699,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         else mbar_arrive_leader(&sm.acc_empty);
       };
       if (first < 0 && lane == 0) release();
-      const int64_t row = (int64_t)mt * 256 + (int64_t)rank * kBM + 32 * q + lane;
-      const bool row_ok = row < g.M;
+      const int64_t row0 = (int64_t)mt * 256 + (int64_t)rank * kBM + 32 * q;
       for (int step = 0; step < nch; ++step) {
         const int c = (first < 0) ? step : (step == 0 ? first : (buf == 0 ? step - 1 : step));
         uint32_t r[kEpiChunk];
@@ -622,37 +712,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           __syncwarp();
           if (lane == 0) release();
         }
-        if (!row_ok) continue;
-        const int64_t col0 = (int64_t)nt * kBN + c * kEpiChunk;
-        float v[kEpiChunk];
-#pragma unroll
-        for (int j = 0; j < kEpiChunk; ++j) v[j] = __fmul_rn(__uint_as_float(r[j]), alpha);
-        if (g.bias != nullptr) {
-          if (g.bias_f32) {
-            const float* bp = reinterpret_cast<const float*>(g.bias) + col0;
-#pragma unroll
-            for (int j = 0; j < kEpiChunk; ++j) v[j] = __fadd_rn(v[j], __ldg(bp + j));
-          } else {
-            const __nv_bfloat16* bp = reinterpret_cast<const __nv_bfloat16*>(g.bias) + col0;
-#pragma unroll
-            for (int j = 0; j < kEpiChunk; ++j) v[j] = __fadd_rn(v[j], __bfloat162float(bp[j]));
-          }
-        }
-        if (g.out_f32) {
-          float* op = reinterpret_cast<float*>(g.out) + row * g.ldo + col0;
-#pragma unroll
-          for (int j = 0; j < kEpiChunk; j += 4)
-            st_global_v4(op + j, __float_as_uint(v[j]), __float_as_uint(v[j + 1]), __float_as_uint(v[j + 2]),
-                         __float_as_uint(v[j + 3]));
-        } else {
-          __nv_bfloat16* op = reinterpret_cast<__nv_bfloat16*>(g.out) + row * g.ldo + col0;
-#pragma unroll
-          for (int j = 0; j < kEpiChunk; j += 8)
-            st_global_v4(op + j, pack_bf16x2(v[j], v[j + 1]), pack_bf16x2(v[j + 2], v[j + 3]),
-                         pack_bf16x2(v[j + 4], v[j + 5]), pack_bf16x2(v[j + 6], v[j + 7]));
-        }
+        epilogue_piece(r, alpha, g, &tmO, slots, slot, nt * kBN + c * kEpiChunk, row0, lane);
       }
     }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
   }
 
   // Both CTAs stay until every MMA of the pair is done (the leader drained them above), then free
@@ -706,8 +770,8 @@ int rb_nvfp4_gemm(const void* a_packed, const void* a_scale, const void* b_packe
   const int oesize = out_dtype == RB_OUT_F32 ? 4 : 2;
   const auto misaligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) != 0; };
   if (misaligned(a_packed) || misaligned(b_packed) || misaligned(a_scale) || misaligned(b_scale) || misaligned(out) ||
-      ldo < n || ((uint64_t)ldo * oesize) % 16 != 0) {
-    rb_host::set_error("nvfp4 gemm: operands and output must be 16-byte aligned with 16-byte row strides");
+      (bias != nullptr && misaligned(bias)) || ldo < n || ((uint64_t)ldo * oesize) % 16 != 0) {
+    rb_host::set_error("nvfp4 gemm: operands, bias and output must be 16-byte aligned with 16-byte row strides");
     return RB_ERR_ARG;
   }
   int dev = rb_host::current_device();
@@ -736,11 +800,15 @@ int rb_nvfp4_gemm(const void* a_packed, const void* a_scale, const void* b_packe
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const int sms = rb_host::num_sms(dev);
   const bool two_sm = m >= 256;
-  CUtensorMap tmA, tmB;
+  CUtensorMap tmA, tmB, tmO;
+  // Output boxes are 32 rows x 128 bytes (64 bf16 or 32 fp32 columns), 128-byte swizzled.
   if (!rb_host::make_tmap_2d(&tmA, a_packed, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)(k / 2), (uint64_t)m,
                              (uint64_t)(k / 2), kStepBytes, kBM, CU_TENSOR_MAP_SWIZZLE_128B) ||
       !rb_host::make_tmap_2d(&tmB, b_packed, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)(k / 2), (uint64_t)n,
-                             (uint64_t)(k / 2), kStepBytes, two_sm ? kBM : kBN, CU_TENSOR_MAP_SWIZZLE_128B))
+                             (uint64_t)(k / 2), kStepBytes, two_sm ? kBM : kBN, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !rb_host::make_tmap_2d(&tmO, out, oesize == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                             (uint64_t)n, (uint64_t)m, (uint64_t)ldo * oesize, 128 / oesize, 32,
+                             CU_TENSOR_MAP_SWIZZLE_128B))
     return RB_ERR_CUDA;
   cudaError_t e = cudaSuccess;
   if (two_sm) {
@@ -784,7 +852,7 @@ int rb_nvfp4_gemm(const void* a_packed, const void* a_scale, const void* b_packe
     const int cap = (dev >= 0 && dev < 64) ? max_clusters[dev] : sms / 2;
     const int clusters = g.n_tiles < cap ? g.n_tiles : cap;
     cfg.gridDim = dim3(2 * clusters, 1, 1);
-    e = cudaLaunchKernelEx(&cfg, nvfp4_gemm2_kernel, tmA, tmB, tmSA, tmSB, g);
+    e = cudaLaunchKernelEx(&cfg, nvfp4_gemm2_kernel, tmA, tmB, tmSA, tmSB, tmO, g);
   } else {
     g.tiles_m = (int)(m / kBM);
     g.n_tiles = g.tiles_m * g.tiles_n;
@@ -799,7 +867,7 @@ int rb_nvfp4_gemm(const void* a_packed, const void* a_scale, const void* b_packe
       configured[dev] = true;
     }
     const int grid = g.n_tiles < sms ? g.n_tiles : sms;
-    nvfp4_gemm_kernel<<<grid, kGemmThreads, smem, st>>>(tmA, tmB, g);
+    nvfp4_gemm_kernel<<<grid, kGemmThreads, smem, st>>>(tmA, tmB, tmO, g);
   }
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) {

@@ -424,7 +424,9 @@ def _gemm(
         if bias.dtype not in (torch.bfloat16, torch.float32):
             bias = bias.to(torch.float32)
         bias = bias.contiguous()
-        bias_code = _lib.RB_DTYPE_BF16 if bias.dtype == torch.bfloat16 else _lib.RB_DTYPE_F32
+        if bias.data_ptr() % 16:  # the epilogue reads the bias in 16-byte vectors
+            bias = bias.clone()
+        bias_code =_lib.RB_DTYPE_BF16 if bias.dtype == torch.bfloat16 else _lib.RB_DTYPE_F32
     tok = _trace.begin("gemm", 2.0 * m * n * k)
     _lib.check(
         lib.rb_nvfp4_gemm(
