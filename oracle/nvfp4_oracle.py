@@ -120,6 +120,106 @@ def encode_e2m1(a: np.ndarray, sign: np.ndarray, u: np.ndarray | None = None) ->
     return (code | (sign.astype(np.uint8) << 3)).astype(np.uint8)
 
 
+# --- the device's stochastic-rounding stream -----------------------------------------------------
+# radiance draws u = tl.rand(seed, row * K + col) per element (quantize.py:566-567, :622-623) and
+# rounds up when u < (a - lo) / (hi - lo).  The B200 kernels keep that rule but use their own
+# counter-based generator, restated here so the device output can be checked bit for bit.  Each
+# 16-element quantization block draws from its own stream:
+#   s_0     = mix32(lo32(blk) ^ key(hi32(blk)))            (mix32: the lowbias32 finalizer)
+#   r_j     = A^j s_0 + C (A^(j-1) + ... + 1)  mod 2^32    (a full-period LCG, A = 747796405,
+#                                                           C = 2891336453: PCG's 32-bit constants)
+#   key(0)  = mix32(lo32(seed) ^ 0x9E3779B9) ^ mix32(hi32(seed) + 0x7F4A7C15) for the rowblock
+#             form, and mix32(that ^ 0x85EBCA6B) for the colblock form
+#   key(h)  = key(0) ^ mix32(h + 0x632BE5AB)                for h != 0
+# Rowblock blocks are numbered (row * K + col) / 16 and draw j goes to column offset j; colblock
+# blocks are numbered col * (M / 16) + row / 16 (their row in the transposed output) and draw j goes
+# to row offset j.  The rounding uses the top 22 bits of r as u = (2^22 - 1 - (r >> 10)) / 2^22
+# against the fraction measured on the fp32 grid (see ``sr_nibbles``).
+
+_M32 = np.uint64(0xFFFFFFFF)
+LCG_A, LCG_C = 747796405, 2891336453
+
+
+def mix32(x) -> np.ndarray:
+    """lowbias32 (C. Wellons' hash-prospector finalizer) on uint32 values."""
+    x = np.asarray(x, dtype=np.uint64) & _M32
+    x ^= x >> np.uint64(16)
+    x = (x * np.uint64(0x7FEB352D)) & _M32
+    x ^= x >> np.uint64(15)
+    x = (x * np.uint64(0x846CA68B)) & _M32
+    x ^= x >> np.uint64(16)
+    return x.astype(np.uint32)
+
+
+def sr_key(seed: int) -> np.uint32:
+    s = np.uint64(int(seed) & 0xFFFFFFFFFFFFFFFF)
+    lo, hi = s & _M32, s >> np.uint64(32)
+    return np.uint32(mix32(lo ^ np.uint64(0x9E3779B9)) ^ mix32((hi + np.uint64(0x7F4A7C15)) & _M32))
+
+
+def sr_key_col(seed: int) -> np.uint32:
+    return np.uint32(mix32(np.uint64(sr_key(seed)) ^ np.uint64(0x85EBCA6B)))
+
+
+def sr_block_seeds(blk: np.ndarray, key) -> np.ndarray:
+    """s_0 of blocks ``blk`` (uint64 block indices)."""
+    blk = np.asarray(blk, dtype=np.uint64)
+    key = np.uint64(key)
+    hi = blk >> np.uint64(32)
+    keyh = np.where(hi == 0, key, key ^ mix32((hi + np.uint64(0x632BE5AB)) & _M32).astype(np.uint64))
+    return mix32((blk & _M32) ^ keyh)
+
+
+def lcg_jump(s0: np.ndarray, j: np.ndarray) -> np.ndarray:
+    """r_j = A^j s_0 + C_j mod 2^32, elementwise."""
+    mul = np.ones(BLOCK, dtype=np.uint64)
+    add = np.zeros(BLOCK, dtype=np.uint64)
+    for i in range(1, BLOCK):
+        mul[i] = (mul[i - 1] * np.uint64(LCG_A)) & _M32
+        add[i] = (add[i - 1] * np.uint64(LCG_A) + np.uint64(LCG_C)) & _M32
+    j = np.asarray(j)
+    return ((np.asarray(s0, dtype=np.uint64) * mul[j] + add[j]) & _M32).astype(np.uint32)
+
+
+def sr_stream_row(rows: int, cols: int, seed: int) -> np.ndarray:
+    """(rows, cols) random words of the rowblock form, indexed by element position."""
+    lin = np.arange(rows, dtype=np.uint64)[:, None] * np.uint64(cols) + np.arange(cols, dtype=np.uint64)[None, :]
+    return lcg_jump(sr_block_seeds(lin >> np.uint64(4), sr_key(seed)), (lin & np.uint64(15)).astype(np.int64))
+
+
+def sr_stream_col(rows: int, cols: int, seed: int) -> np.ndarray:
+    """(rows, cols) random words of the colblock form, indexed by the element's (row, col) in x."""
+    r = np.arange(rows, dtype=np.uint64)[:, None]
+    c = np.arange(cols, dtype=np.uint64)[None, :]
+    blk = c * np.uint64(rows // BLOCK) + (r >> np.uint64(4))
+    j = np.broadcast_to((r & np.uint64(15)).astype(np.int64), (rows, cols))
+    return lcg_jump(sr_block_seeds(blk, sr_key_col(seed)), j)
+
+
+def sr_nibbles(q: np.ndarray, r: np.ndarray) -> np.ndarray:
+    """The device's stochastic rounding of quotients q (already clamped to +-6) with random words r.
+
+    Same rule as quantize.py:122-138 (up with probability (a - lo) / (hi - lo)), with the fraction
+    measured on the fp32 grid: on [1, 6] the e2m1 levels keep one fp32 mantissa bit and the 22
+    bits below it are the fraction; [0, 1) is first mapped to RN(a + 1) / 2 on [0.5, 1) (one
+    rounding), where the levels again keep one bit.  Adding r >> 10 carries into the kept bit
+    exactly when u < fraction for u = (2^22 - 1 - (r >> 10)) / 2^22.  Sign in bit 3 (q < 0).
+    """
+    q = np.asarray(q, dtype=np.float32)
+    m = np.abs(q)
+    half = (m * np.float32(0.5)).astype(np.float32) + np.float32(0.5)  # RN(m/2 + 1/2): m/2 is exact
+    t = np.minimum(np.maximum(m, half.astype(np.float32)), np.float32(6.0)).astype(np.float32)
+    k = np.where(q < 0, np.uint64(12 << 22), np.uint64(4 << 22))
+    b = (t.view(np.uint32).astype(np.uint64) + k + (np.asarray(r, dtype=np.uint64) >> np.uint64(10))) & _M32
+    return ((b >> np.uint64(22)) & np.uint64(15)).astype(np.uint8)
+
+
+def sr_uniform(r: np.ndarray) -> np.ndarray:
+    """The uniform u in [0, 1) that ``sr_nibbles`` compares against (a multiple of 2^-22)."""
+    r22 = np.asarray(r, dtype=np.uint32) >> np.uint32(10)
+    return ((np.uint32((1 << 22) - 1) - r22).astype(np.float64) / float(1 << 22)).astype(np.float32)
+
+
 def pack_nibbles(code: np.ndarray) -> np.ndarray:
     """quantize.py:142-149 -- element 2i in the low nibble of byte i, 2i+1 in the high nibble."""
     return (code[..., 0::2] | (code[..., 1::2] << 4)).astype(np.uint8)
@@ -132,24 +232,26 @@ def unpack_nibbles(packed: np.ndarray) -> np.ndarray:
     return np.stack([low, high], axis=-1).reshape(*packed.shape[:-1], packed.shape[-1] * 2)
 
 
-def _quantize_blocks(xb: np.ndarray, gs, axis: int, u: np.ndarray | None):
+def _quantize_blocks(xb: np.ndarray, gs, axis: int, u: np.ndarray | None, r: np.ndarray | None = None):
     """Shared body of the two quantizers: amax over ``axis`` (the 16-wide block axis), the block
-    scale, the IEEE divide by ``divisor * gs``, the +-6 clamp and the encode."""
+    scale, the IEEE divide by ``divisor * gs``, the +-6 clamp and the encode (``r``: the device's
+    stochastic rounding with these random words, see ``sr_nibbles``)."""
     gs = _F32(gs)
     amax = np.abs(xb).max(axis=axis, keepdims=True)
     byte, divisor = block_scale(amax, gs)
     with np.errstate(invalid="ignore", divide="ignore", over="ignore"):
         q = np.clip(xb / (divisor * gs), -FP4_MAX, FP4_MAX).astype(np.float32)
-    code = encode_e2m1(np.abs(q), q < 0, u)
+    code = sr_nibbles(q, r) if r is not None else encode_e2m1(np.abs(q), q < 0, u)
     return code, byte
 
 
-def quantize_rowblock(x: np.ndarray, gs, u: np.ndarray | None = None):
+def quantize_rowblock(x: np.ndarray, gs, u: np.ndarray | None = None, r: np.ndarray | None = None):
     """quantize.py:216-232 -- (M, K) -> packed (M, K/2) uint8, unswizzled scale bytes (M, K/16)."""
     m, k = x.shape
     xb = x.astype(np.float32).reshape(m, k // BLOCK, BLOCK)
     ub = None if u is None else u.reshape(m, k // BLOCK, BLOCK)
-    code, byte = _quantize_blocks(xb, gs, 2, ub)
+    rb = None if r is None else r.reshape(m, k // BLOCK, BLOCK)
+    code, byte = _quantize_blocks(xb, gs, 2, ub, rb)
     return pack_nibbles(code.reshape(m, k)), byte.reshape(m, k // BLOCK)
 
 
@@ -170,18 +272,20 @@ def rotate_blocks(xb: np.ndarray, hadamard: np.ndarray) -> np.ndarray:
     return out
 
 
-def quantize_colblock(x: np.ndarray, gs, hadamard: np.ndarray | None = None, u: np.ndarray | None = None):
+def quantize_colblock(x: np.ndarray, gs, hadamard: np.ndarray | None = None, u: np.ndarray | None = None,
+                      r: np.ndarray | None = None):
     """quantize.py:235-268 -- blocks along dim 0, output transposed.
 
-    (M, K) -> packed (K, M/2) uint8, unswizzled scale bytes (K, M/16).  ``u`` is indexed by the
-    original (M, K) position, as in the reference.
+    (M, K) -> packed (K, M/2) uint8, unswizzled scale bytes (K, M/16).  ``u`` (and ``r``) are
+    indexed by the original (M, K) position, as in the reference.
     """
     m, k = x.shape
     xb = x.astype(np.float32).reshape(m // BLOCK, BLOCK, k)
     if hadamard is not None:
         xb = rotate_blocks(xb, hadamard)
     ub = None if u is None else u.reshape(m // BLOCK, BLOCK, k)
-    code, byte = _quantize_blocks(xb, gs, 1, ub)
+    rb = None if r is None else r.reshape(m // BLOCK, BLOCK, k)
+    code, byte = _quantize_blocks(xb, gs, 1, ub, rb)
     code = code.reshape(m, k).T.copy()
     return pack_nibbles(code), byte.reshape(m // BLOCK, k).T.copy()
 
@@ -245,14 +349,16 @@ def quantize_supported_shape(rows: int, cols: int) -> bool:
     return rows % 128 == 0 and cols % 64 == 0
 
 
-def quantize(x: np.ndarray, axis: int, gs=None, hadamard=None, u=None):
-    """quantize.py:412-433 (``quantize_reference``) -> (packed, swizzled flat scale, gs)."""
+def quantize(x: np.ndarray, axis: int, gs=None, hadamard=None, u=None, r=None):
+    """quantize.py:412-433 (``quantize_reference``) -> (packed, swizzled flat scale, gs).  ``r``
+    selects the device's stochastic rounding with those random words (``sr_stream_row`` or
+    ``sr_stream_col``)."""
     if gs is None:
         gs = global_scale_of(x)
     if axis in (-1, x.ndim - 1):
-        packed, scale = quantize_rowblock(x, gs, u=u)
+        packed, scale = quantize_rowblock(x, gs, u=u, r=r)
     elif axis == 0:
-        packed, scale = quantize_colblock(x, gs, hadamard=hadamard, u=u)
+        packed, scale = quantize_colblock(x, gs, hadamard=hadamard, u=u, r=r)
     else:
         raise ValueError(f"nvfp4.quantize supports axis 0 or -1, got {axis}")
     return packed, to_blocked(scale), _F32(gs)

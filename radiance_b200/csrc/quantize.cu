@@ -68,6 +68,11 @@ struct QuantArgs {
   uint8_t* col_scale;
   int tiles_k;
   int n_tiles;
+  // Powers of two handed to the kernel at run time (the host sets p2 = 2, p22 = 2^22,
+  // p25 = 2^25).  Part of the stochastic-rounding arithmetic is written as multiply-high /
+  // multiply-add by them (x >> s == umulhi(x, 2^(32-s))) so that it runs on the FMA pipe beside
+  // the integer/logic pipe; literal constants would be strength-reduced back into shifts.
+  uint32_t p2, p22, p25;
 };
 
 struct QHeader {
@@ -155,10 +160,31 @@ __device__ __forceinline__ uint32_t sr_key(const int64_t* seed) {
   return mix32((uint32_t)s ^ 0x9E3779B9u) ^ mix32((uint32_t)(s >> 32) + 0x7F4A7C15u);
 }
 
-// Key for a run of element indices sharing the same upper 32 bits.
-__device__ __forceinline__ uint32_t sr_key_hi(uint32_t key, uint64_t lin) {
-  const uint32_t hi = (uint32_t)(lin >> 32);
+// Key for indices sharing the same upper 32 bits.
+__device__ __forceinline__ uint32_t sr_key_hi(uint32_t key, uint64_t idx) {
+  const uint32_t hi = (uint32_t)(idx >> 32);
   return hi ? key ^ mix32(hi + 0x632BE5ABu) : key;
+}
+
+// Random words of one 16-element block: s_0 = mix32(block index ^ key), then the block's draws
+// follow a full-period 32-bit LCG (multiplier and increment of PCG's 32-bit generator),
+// r_j = A^j s_0 + C_j, each one multiply-add from s_0 (no dependency chain).  The rowblock form
+// numbers its blocks row-major, (row * K + col) / 16, with the launch key; the colblock form
+// numbers them by output row, col * (M / 16) + row / 16, with a second key.  Draw j goes to
+// element j of the block (column offset in the rowblock form, row offset in the colblock form).
+constexpr uint32_t kLcgA = 747796405u, kLcgC = 2891336453u;
+__host__ __device__ constexpr uint32_t lcg_mul(int j) {
+  uint32_t a = 1u;
+  for (int i = 0; i < j; ++i) a *= kLcgA;
+  return a;
+}
+__host__ __device__ constexpr uint32_t lcg_add(int j) {
+  uint32_t c = 0u;
+  for (int i = 0; i < j; ++i) c = c * kLcgA + kLcgC;
+  return c;
+}
+__device__ __forceinline__ uint32_t sr_block_seed(uint64_t blk, uint32_t key) {
+  return mix32((uint32_t)blk ^ sr_key_hi(key, blk));
 }
 
 // Stochastic rounding of a quotient q (= RN(x / D)) to a signed e2m1 code, with 32 random bits r
@@ -168,12 +194,26 @@ __device__ __forceinline__ uint32_t sr_key_hi(uint32_t key, uint64_t lin) {
 // random bits carries into the kept bit exactly with that probability, and the carry moves the
 // value to the next level (into the exponent where the level is a power of two).  [0, 1) is
 // shifted to [1, 2), where the grid step (0.5) is the same, and the code shifted back by 2.
-__device__ __forceinline__ uint32_t sr_code(float q, uint32_t r) {
-  const float a = fminf(fabsf(q), 6.0f);
-  const bool sub = a < 1.0f;
-  const float t = sub ? __fadd_rn(a, 1.0f) : a;
-  const uint32_t b = __float_as_uint(t) + (r >> 10);
-  return (b >> 22) - (sub ? 254u : 252u) + (q < 0.0f ? 8u : 0u);
+//
+// The kernels evaluate the same rule on q4 = 4q (their SR divisor is D / 4, an exact scaling of
+// the same quotient): t4 = min(max(m4, m4/2 + 2), 24) with m4 = |q4| is 4 max(a, (a+1)/2) -- the
+// [0, 1) range mapped onto [0.5, 1), one binade below a + 1, so every magnitude shares one offset
+// -- and bits(4t) = bits(t) + (4 << 22).  The code, sign included, is then bits 22..25 of
+// bits(t4) + (r >> 10) + sign(q) << 25: exponent-and-kept-bit 256..263 (t = 0.5 .. 6) is codes
+// 0..7 modulo 16, the carry never reaches bit 25 (t4 = 24 has no fraction bits), and bit 25 is
+// the sign.  The sign is the quotient's sign bit: the Markstein quotient of +-0 is +0, so it
+// equals the reference's q < 0 wherever the quotient is not an underflowed zero (those nibbles
+// are cleared by underflow_mask8).  Returns the nibble in place: bits 22..25 moved to 4e..4e+3
+// (e is a constant after unrolling, so the move is one shift).
+__device__ __forceinline__ uint32_t sr_nibble_at(float q4, uint32_t r, const QuantArgs& a, int e) {
+  const float m = fabsf(q4);
+  const float t = fminf(fmaxf(m, fmaf(m, 0.5f, 2.0f)), 24.0f);
+  const uint32_t sgn = __umulhi(__float_as_uint(q4), a.p2);         // sign bit
+  const uint32_t u = sgn * a.p25 + __float_as_uint(t);
+  const uint32_t b = __umulhi(r, a.p22) + u;                        // + (r >> 10)
+  const int sh = 22 - 4 * e;
+  const uint32_t moved = sh >= 0 ? (b >> sh) : (b << -sh);
+  return moved & (0xFu << (4 * e));
 }
 
 // A quotient that rounds to +-0 must produce nibble 0 (the reference's sign is `q < 0`, false for
@@ -228,7 +268,8 @@ __device__ __forceinline__ void st_global_v4(void* p, uint32_t a, uint32_t b, ui
 struct QCtx {
   const QHeader* hdr;
   float nden, rden;  // -(6 gs) and RN(1/(6 gs))
-  uint32_t key;
+  uint32_t key;      // stochastic rounding: rowblock-form key
+  uint32_t key_col;  // colblock-form key
 };
 
 // ---------------------------------------------------------------------------------------------
@@ -244,14 +285,19 @@ __device__ __forceinline__ uint32_t row_block(const float2 (&v)[8], const QCtx& 
   const float2 dy = c.hdr->table[sbyte];
   const float2 nd = make_float2(-dy.x, -dy.x), yy = make_float2(dy.y, dy.y);
   if constexpr (SR) {
-    const uint32_t kk = sr_key_hi(c.key, lin0), l0 = (uint32_t)lin0;
+    const uint32_t s0 = sr_block_seed(lin0 >> 4, c.key);
+    const float2 nd4 = make_float2(0.25f * nd.x, 0.25f * nd.y), y4 = make_float2(4.0f * yy.x, 4.0f * yy.y);
     w0 = w1 = 0;
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
-      const float2 q = div2(v[e], nd, yy);
-      const uint32_t pair = sr_code(q.x, mix32((l0 + 2 * e) ^ kk)) | (sr_code(q.y, mix32((l0 + 2 * e + 1) ^ kk)) << 4);
-      if (e < 4) w0 |= pair << (8 * e);
-      else w1 |= pair << (8 * (e - 4));
+      const float2 q = div2(v[e], nd4, y4);  // 4 * (x / D)
+      const uint32_t rx = s0 * lcg_mul(2 * e) + lcg_add(2 * e);
+      const uint32_t ry = s0 * lcg_mul(2 * e + 1) + lcg_add(2 * e + 1);
+      if (e < 4) {
+        w0 |= sr_nibble_at(q.x, rx, a, 2 * e) | sr_nibble_at(q.y, ry, a, 2 * e + 1);
+      } else {
+        w1 |= sr_nibble_at(q.x, rx, a, 2 * e - 8) | sr_nibble_at(q.y, ry, a, 2 * e - 7);
+      }
     }
   } else {
     float2 q[8];
@@ -397,23 +443,23 @@ __device__ __forceinline__ void col_unit(uint32_t tile, const QCtx& c, const Qua
   const float2 nd = make_float2(-dx, -dyv), yy = make_float2(tx.y * unfold, ty.y * unfold);
   uint32_t wx0, wx1, wy0, wy1;
   if constexpr (SR) {
-    const uint64_t lin0 = (uint64_t)(m0 + 16 * g) * (uint64_t)a.K + (uint64_t)(k0 + 2 * cp);
-    const uint32_t kk = sr_key_hi(c.key, lin0);
-    uint32_t l = (uint32_t)lin0;
-    const uint32_t kstride = (uint32_t)a.K;
+    // Blocks of output rows 2cp and 2cp + 1 (input columns k0 + 2cp, + 1), 16-row group m0/16 + g.
+    const uint64_t mb = (uint64_t)(a.M >> 4);
+    const uint64_t bx = (uint64_t)(k0 + 2 * cp) * mb + (uint64_t)(m0 >> 4) + (uint64_t)g;
+    const uint32_t sx = sr_block_seed(bx, c.key_col), sy = sr_block_seed(bx + mb, c.key_col);
+    const float2 nd4 = make_float2(0.25f * nd.x, 0.25f * nd.y), y4 = make_float2(4.0f * yy.x, 4.0f * yy.y);
     wx0 = wx1 = wy0 = wy1 = 0;
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
-      const float2 q = div2(v[i], nd, yy);
-      const uint32_t cx = sr_code(q.x, mix32(l ^ kk));
-      const uint32_t cy = sr_code(q.y, mix32((l + 1) ^ kk));
-      l += kstride;
+      const float2 q = div2(v[i], nd4, y4);
+      const uint32_t cx = sr_nibble_at(q.x, sx * lcg_mul(i) + lcg_add(i), a, i & 7);
+      const uint32_t cy = sr_nibble_at(q.y, sy * lcg_mul(i) + lcg_add(i), a, i & 7);
       if (i < 8) {
-        wx0 |= cx << (4 * i);
-        wy0 |= cy << (4 * i);
+        wx0 |= cx;
+        wy0 |= cy;
       } else {
-        wx1 |= cx << (4 * (i - 8));
-        wy1 |= cy << (4 * (i - 8));
+        wx1 |= cx;
+        wy1 |= cy;
       }
     }
   } else {
@@ -514,6 +560,7 @@ __global__ void __launch_bounds__(kQThreads, 2)
   c.nden = -denom;
   c.rden = __frcp_rn(denom);
   c.key = 0;
+  c.key_col = 0;
   if (tid < 127) {
     const float d = __fmul_rn(e4m3_value(tid), gs);
     hdr->table[tid] = make_float2(d, __frcp_rn(d));
@@ -521,7 +568,10 @@ __global__ void __launch_bounds__(kQThreads, 2)
   if constexpr (HAD) {
     hdr->had[tid] = a.hadamard[tid];
   }
-  if constexpr (SR) c.key = sr_key(a.seed);
+  if constexpr (SR) {
+    c.key = sr_key(a.seed);
+    c.key_col = mix32(c.key ^ 0x85EBCA6Bu);
+  }
   __syncthreads();
   if constexpr (HAD) {
     // Is R = (Sylvester / 4) with row signs?  Then take the add-only fast path.
@@ -855,6 +905,9 @@ int rb_nvfp4_quantize(const void* x, int dtype, int64_t rows, int64_t cols, int6
   a.col_scale = reinterpret_cast<uint8_t*>(col_scale);
   const int tile_cols = f32 ? QTile<true>::kCols : QTile<false>::kCols;
   a.tiles_k = (int)((cols + tile_cols - 1) / tile_cols);
+  a.p2 = 2u;
+  a.p22 = 1u << 22;
+  a.p25 = 1u << 25;
   a.n_tiles = (int)((rows / 128) * a.tiles_k);
   const bool had = col && hadamard != nullptr;
   const bool sr = seed != nullptr;

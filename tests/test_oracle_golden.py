@@ -57,6 +57,52 @@ def test_stochastic_rounding_bit_exact_for_a_given_draw(golden):
     np.testing.assert_array_equal(O.to_blocked(s), golden[f"{name}/sr_colh_scale"])
 
 
+def test_device_sr_rule_is_the_reference_rule():
+    """The device's stochastic rounding (``sr_nibbles``: a carry into the kept fp32 mantissa bit)
+    is the reference's ``u < (a - lo) / (hi - lo)`` (quantize.py:122-138) with
+    u = ``sr_uniform(r)``, for every quotient whose grid fraction is a multiple of 2^-22 -- all of
+    [1, 6], and [0, 1) down to 2^-21 on bf16-representable values."""
+    rng = np.random.default_rng(17)
+    n = 400_000
+    r = rng.integers(0, 2**32, size=n, dtype=np.uint64).astype(np.uint32)
+    # bf16-representable magnitudes in [2^-15, 6] and exact zeros, both signs, plus every level and
+    # the midpoints between levels.
+    mag = np.exp2(rng.uniform(-15, np.log2(6.0), size=n)).astype(np.float32)
+    mag = O.bf16_to_f32(O.f32_to_bf16_bits(mag))
+    levels = np.array(O.FP4_VALUES + (0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0), dtype=np.float32)
+    mag[: len(levels) * 100] = np.repeat(levels, 100)
+    mag[-1000:] = 0.0
+    q = np.minimum(mag, np.float32(6.0)) * np.where(rng.integers(0, 2, size=n) == 1, -1, 1).astype(np.float32)
+    dev = O.sr_nibbles(q, r)
+    ref = O.encode_e2m1(np.abs(q), q < 0, O.sr_uniform(r))
+    np.testing.assert_array_equal(dev, ref)
+
+
+def test_sr_streams_are_per_block():
+    """Each form's stream is a function of (seed, block index, offset in block) only: the same
+    block gets the same draws in any tensor shape that gives it the same index, the two forms and
+    two seeds differ, and block indices at or past 2^32 use the re-keyed upper half."""
+    a = O.sr_stream_row(8, 64, 5)
+    b = O.sr_stream_row(16, 32, 5)  # same row-major block indices, another shape
+    np.testing.assert_array_equal(a.reshape(-1), b.reshape(-1))
+    assert not np.array_equal(O.sr_stream_row(8, 64, 6), a)
+    assert not np.array_equal(O.sr_stream_col(32, 64, 5)[:8], O.sr_stream_row(32, 64, 5)[:8])
+    # Block j of the colblock form: column j // (rows/16), rows 16 * (j % (rows/16)) + 0..15.
+    col = O.sr_stream_col(64, 8, 5)
+    s0 = O.sr_block_seeds(np.array([3 * 4 + 2], dtype=np.uint64), O.sr_key_col(5))
+    np.testing.assert_array_equal(col[32:48, 3], O.lcg_jump(np.repeat(s0, 16), np.arange(16)))
+    key = np.uint64(O.sr_key(5))
+    seeds = O.sr_block_seeds(np.array([5, (1 << 32) + 5, (3 << 32) + 5], dtype=np.uint64), key)
+    assert seeds[0] == O.mix32(np.uint64(5) ^ key)
+    for i, h in ((1, 1), (2, 3)):
+        assert seeds[i] == O.mix32(np.uint64(5) ^ (key ^ np.uint64(O.mix32(np.uint64(h + 0x632BE5AB)))))
+    # The jump-ahead equals stepping the LCG.
+    st = int(seeds[0])
+    for jj in range(16):
+        assert int(O.lcg_jump(np.array([seeds[0]]), np.array([jj]))[0]) == st
+        st = (st * O.LCG_A + O.LCG_C) & 0xFFFFFFFF
+
+
 @pytest.mark.parametrize("shape", [(128, 4), (256, 8), (4096, 80), (100, 16), (64, 16)])
 def test_blocked_layout(golden, shape):
     rows, cols = shape

@@ -269,6 +269,34 @@ def test_stochastic_rounding_unbiased_over_many_seeds(nv, form):
     assert ((mean - t).norm() / t.norm()).item() < 0.25 * ((rn_deq - t).norm() / t.norm()).item()
 
 
+@pytest.mark.parametrize("shape", [(256, 512), (384, 320), (1024, 1408)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("form", ["row", "col", "colh"])
+def test_stochastic_rounding_matches_oracle_stream(nv, shape, dtype, form):
+    """Bit-exact against the oracle's restatement of the device streams and rounding
+    (``sr_stream_row`` / ``sr_stream_col`` / ``sr_nibbles``), both forms, fused and separate."""
+    torch.manual_seed(hash((shape, str(dtype), form)) % 2**31)
+    x = torch.randn(*shape, device="cuda", dtype=dtype) * 0.3
+    gs = nv.global_scale_of(x)
+    gs_np = np.float32(gs.item())
+    seed_value = 0x1234_5678_9ABC + len(form)
+    seed = torch.tensor(seed_value, device="cuda", dtype=torch.int64)
+    had = O.hadamard_matrix() if form == "colh" else None
+    h = None if had is None else torch.from_numpy(had).cuda()
+    axis = -1 if form == "row" else 0
+    r = (O.sr_stream_row if form == "row" else O.sr_stream_col)(*shape, seed_value)
+    p, s, _ = O.quantize(to_numpy_f32(x), axis, gs=gs_np, hadamard=had, r=r)
+    q = nv.quantize(x, axis, global_scale=gs, hadamard=h, stochastic=True, seed=seed)
+    np.testing.assert_array_equal(u8(q.packed), p)
+    np.testing.assert_array_equal(u8(q.scale), s)
+    if form != "row":
+        row, col = nv.quantize_both(x, global_scale=gs, hadamard=h, stochastic=True, seed=seed)
+        np.testing.assert_array_equal(u8(col.packed), p)
+        pr, sr_, _ = O.quantize(to_numpy_f32(x), -1, gs=gs_np, r=O.sr_stream_row(*shape, seed_value))
+        np.testing.assert_array_equal(u8(row.packed), pr)
+    _status_ok()
+
+
 def test_stochastic_both_forms(nv):
     x = torch.randn(1024, 512, device="cuda", dtype=torch.bfloat16) * 1e-3
     gs = nv.global_scale_of(x)
