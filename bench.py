@@ -217,6 +217,40 @@ def run_ours(args):
     per_kind = kt.summary()
     launches = kt.launches
 
+    # ---- with the data-parallel weight-gradient reduction (N > 1) -----------------------------
+    # Token sharding needs no collective on the fwd/dgrad path, but wgrad contracts over tokens:
+    # a data-parallel job sums each linear's fp32 dW across ranks.  Measured separately, the way
+    # DDP overlaps it (one async all-reduce per linear, issued as its dW is produced).
+    dp = None
+    if world > 1:
+        def step_allreduce():
+            works = []
+            for i, lin in enumerate(layers):
+                x = xs[i].detach().requires_grad_(True)
+                y = lin(x)
+                _gx, gw = torch.autograd.grad(y, (x, lin.weight), dys[i])
+                works.append(dist.all_reduce(gw, async_op=True))
+            for w in works:
+                w.wait()
+
+        dp_steps = max(3, min(args.steps, 50))
+        for _ in range(3):
+            step_allreduce()
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        ds, de = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ds.record()
+        for _ in range(dp_steps):
+            step_allreduce()
+        de.record()
+        torch.cuda.synchronize()
+        dp_ms = max_over_ranks(ds.elapsed_time(de)) / dp_steps
+        dp_bytes = sum(lin.weight.numel() * 4 for lin in layers)
+        dp = {"value": round(world * STEP_FLOPS / (dp_ms * 1e-3) / 1e12, 2), "unit": "TFLOPS",
+              "ms_per_step": round(dp_ms, 4), "allreduce_bytes_per_step": dp_bytes,
+              "what": "same step plus an async NCCL all-reduce of each linear's fp32 dW (overlapped)"}
+
     # ---- end-to-end through the public API with host buffers (e2e) --------------------------
     pinned_x = [x.pin_memory() for x in xs_host]
     pinned_dy = [d.pin_memory() for d in dys_host]
@@ -314,6 +348,8 @@ def run_ours(args):
             },
             "clocks": clk,
         }
+        if dp is not None:
+            line["with_dp_grad_allreduce"] = dp
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(budget_s=args.cpu_budget)
         print(json.dumps(line), flush=True)

@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define RB_NVFP4_ABI_VERSION 1
+#define RB_NVFP4_ABI_VERSION 2
 
 /* Input element types. */
 #define RB_DTYPE_BF16 0
@@ -98,8 +98,11 @@ int rb_nvfp4_global_scale_noalloc(const void* x, int dtype, int64_t rows, int64_
  *   hadamard   : NULL or a device 16x16 fp32 matrix R; the colblock form quantizes R^T applied to
  *                every 16-row group (quantize.py:261-262).  Not applied to the rowblock form.
  *   seed       : device int64 seed for stochastic rounding (read on the device); NULL = round to
- *                nearest even.  With a seed both forms use stochastic rounding, unbiased in
- *                distribution (quantize.py:122-138 defines the rounding rule).
+ *                nearest even.  With a seed both forms use stochastic rounding with the rule of
+ *                quantize.py:122-138 (up with probability (a - lo) / (hi - lo), resolved to
+ *                2^-22); each 16-element block draws from its own counter-based stream keyed by
+ *                the seed and the block's index, so results depend on (seed, element position)
+ *                only -- not on the launch shape -- and differ from radiance's tl.rand draws.
  *   row_packed : NULL or rows x cols/2 bytes;  row_scale: NULL or (rows/128)*(cols/64)*512 bytes.
  *   col_packed : NULL or cols x rows/2 bytes;  col_scale: NULL or ceil(cols/128)*(rows/64)*512 bytes
  *                (padding rows are written as zero).
@@ -118,13 +121,65 @@ int rb_nvfp4_quantize(const void* x, int dtype, int64_t rows, int64_t cols, int6
  *   a_packed/a_scale : rowblock-layout operand, m rows, k contraction (a "rows x contraction"
  *                      NVFP4Tensor, quantize.py:328-356).  b_packed/b_scale: likewise, n rows.
  *   alpha_a, alpha_b : device fp32 global scales of the two operands (NULL = 1).
- *   bias             : NULL or n elements of `bias_dtype` (RB_DTYPE_BF16 / RB_DTYPE_F32).
+ *   bias             : NULL or n elements of `bias_dtype` (RB_DTYPE_BF16 / RB_DTYPE_F32), 16-byte
+ *                      aligned.
  *   out              : m x n of `out_dtype`, row stride ldo elements.
  *   m % 128 == 0, n % 128 == 0, k % 64 == 0.
  */
 int rb_nvfp4_gemm(const void* a_packed, const void* a_scale, const void* b_packed, const void* b_scale, int64_t m,
                   int64_t n, int64_t k, const float* alpha_a, const float* alpha_b, const void* bias, int bias_dtype,
                   void* out, int out_dtype, int64_t ldo, void* stream);
+
+/*
+ * Grouped (mixture-of-experts) GEMMs, global scales and quantization.  radiance runs its experts
+ * as stacked bf16 batched matmuls (BatchedExperts.forward, src/radiance/model/ffn.py:148-153:
+ * torch.baddbmm over (experts, capacity, d)) and has no FP4 expert path (transformer.py:204-213
+ * rejects FP4 + MoE); these entries give that path NVFP4 operands.  A group is a contiguous row
+ * range of one stacked tensor: the tokens routed to one expert, or one expert's weight.
+ *
+ * Per-group global scales: gs_out[g] = max(amax(|x[offsets[g] : offsets[g+1]]|) / 2688, 1e-12)
+ * (global_scale_of, quantize.py:205-213, per group; an empty group gets 1e-12).
+ *   offsets   : device int64[num_groups + 1], non-decreasing, offsets[0] = 0, offsets[num_groups] <= rows.
+ *   workspace : device uint32[num_groups + 1], zero before the first call; left zero again.
+ *   cols * elemsize and ld * elemsize multiples of 16, x 16-byte aligned.
+ */
+int rb_nvfp4_global_scale_grouped(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld,
+                                  const int64_t* offsets, int num_groups, float* gs_out, void* workspace,
+                                  void* stream);
+
+/*
+ * rb_nvfp4_quantize with one global scale per group: every 128-row tile is quantized with
+ * group_gs[g] for the group g that holds its first row.  With group offsets that are multiples of
+ * 128 each group's rows of the outputs equal rb_nvfp4_quantize of that group alone (its packed
+ * rows and scale tiles sit at the group's row offset of the rowblock outputs, at its column
+ * offset of the colblock outputs).  Same shape contract and output sizes as rb_nvfp4_quantize.
+ */
+int rb_nvfp4_quantize_grouped(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld,
+                              const int64_t* offsets, int num_groups, const float* group_gs, const float* hadamard,
+                              const int64_t* seed, void* row_packed, void* row_scale, void* col_packed,
+                              void* col_scale, void* stream);
+
+/*
+ * Grouped block-scaled GEMM: for every group g with the device record
+ *   groups[6g .. 6g+5] = {a_row0, b_row0, out_row0, m, k0, k}
+ *   out[out_row0 + i, j] = alpha_a[g] * alpha_b[g] * sum_{k0 <= c < k0 + k} deq(a)[a_row0 + i, c] * deq(b)[b_row0 + j, c]
+ * for i < m, j < n.  One launch covers all groups; the records stay on the device (no host sync
+ * on routing counts).  a (a_rows rows) and b (b_rows rows) are rowblock-layout operands over one
+ * contraction axis of k_total elements (their scale grids are k_total/64 blocks wide); out has
+ * out_rows rows of n `out_dtype` elements, row stride ldo.  Forward and dgrad of an expert layer
+ * are groups over token rows (k0 = 0, k = k_total); its wgrad is groups over contraction ranges
+ * (the experts' token ranges of colblock-quantized operands).
+ *   Device-side contract per record: a_row0, b_row0, m multiples of 128; k0, k multiples of 64;
+ *   k0 + k <= k_total.  A record that breaks it is skipped and rb_nvfp4_device_status reports 5.
+ *   A group with k == 0 writes zeros.  Rows past a group's m (up to the next multiple of 256) are
+ *   computed but not stored.
+ *   alpha_a, alpha_b : NULL or device fp32[num_groups].
+ *   a_rows, b_rows, n multiples of 128; k_total multiple of 64; num_groups <= 256.
+ */
+int rb_nvfp4_gemm_grouped(const void* a_packed, const void* a_scale, int64_t a_rows, const void* b_packed,
+                          const void* b_scale, int64_t b_rows, int64_t n, int64_t k_total, const int64_t* groups,
+                          int num_groups, const float* alpha_a, const float* alpha_b, void* out, int out_dtype,
+                          int64_t out_rows, int64_t ldo, void* stream);
 
 /*
  * Self-test of the quantizer's division: for i < n, compares the library's correctly rounded

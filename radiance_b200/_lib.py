@@ -35,10 +35,23 @@ SIGNATURES: dict[str, tuple] = {
         [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _c_void_p, _c_void_p, _c_void_p, _int,
          _c_void_p, _int, _i64, _c_void_p],
     ),
+    "rb_nvfp4_global_scale_grouped": (
+        _int, [_c_void_p, _int, _i64, _i64, _i64, _c_void_p, _int, _c_void_p, _c_void_p, _c_void_p],
+    ),
+    "rb_nvfp4_quantize_grouped": (
+        _int,
+        [_c_void_p, _int, _i64, _i64, _i64, _c_void_p, _int, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
+         _c_void_p, _c_void_p, _c_void_p],
+    ),
+    "rb_nvfp4_gemm_grouped": (
+        _int,
+        [_c_void_p, _c_void_p, _i64, _c_void_p, _c_void_p, _i64, _i64, _i64, _c_void_p, _int, _c_void_p, _c_void_p,
+         _c_void_p, _int, _i64, _i64, _c_void_p],
+    ),
     "rb_nvfp4_selftest_division": (_int, [_c_void_p, _c_void_p, _i64, _c_void_p, _c_void_p]),
 }
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 RB_DTYPE_BF16 = 0
 RB_DTYPE_F32 = 1

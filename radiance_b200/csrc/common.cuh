@@ -26,6 +26,7 @@ enum : uint32_t {
   kStatusTimeoutMma = 2,       // an MMA commit never arrived
   kStatusTimeoutEpilogue = 3,  // the epilogue waited too long for the accumulator
   kStatusTimeoutProducer = 4,  // a producer waited too long for a free stage
+  kStatusBadGroup = 5,         // a grouped-GEMM group descriptor broke the contract (group skipped)
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

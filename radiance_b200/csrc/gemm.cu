@@ -69,7 +69,19 @@ struct GemmArgs {
   int64_t ldo;
   int tiles_m, tiles_n, n_tiles;
   int k_steps, k_blocks;   // K/256 rounded up, K/64
+  // Grouped mode (two-SM kernel only): `groups` holds num_groups device records
+  // {a_row0, b_row0, out_row0, m, k0, k}; group g computes
+  //   out[out_row0 + i, j] = alpha_a[g] alpha_b[g] sum_{k0 <= c < k0 + k} A[a_row0 + i, c] B[b_row0 + j, c]
+  // for i < m, j < N.  A and B share one contraction axis of kb_total 64-wide blocks (their scale
+  // grids are kb_total blocks wide); out has out_rows rows.
+  const int64_t* groups;
+  int num_groups;
+  int kb_total;
+  int64_t out_rows;
 };
+
+constexpr int kMaxGroups = 256;
+constexpr int kGroupFields = 6;
 
 // ---------------------------------------------------------------------------------------------
 // tcgen05 wrappers (inline PTX)
@@ -185,10 +197,11 @@ constexpr int kOutBox = 4096;  // one staged output box: 32 rows x 128 B
 // written by one TMA store, so the global write is a few full-line bursts instead of 32 rows of
 // scattered 16-byte stores.  `slots` is the warp's two staged boxes (8 KB, 1024-byte aligned):
 // bf16 pieces alternate between them, fp32 pieces (two boxes of 32 columns) use both.  Rows at or
-// past M (the upper half of a 256-row tile when M % 256 == 128) are not stored.
+// past row_end (the upper half of a 256-row tile when M % 256 == 128, or past a group's end) are
+// not stored.
 __device__ __forceinline__ void epilogue_piece(const uint32_t (&r)[kEpiChunk], float alpha, const GemmArgs& g,
                                                const CUtensorMap* tmO, uint32_t slots, int& slot, int col0,
-                                               int64_t row0, int lane) {
+                                               int64_t row0, int64_t row_end, int lane) {
   float v[kEpiChunk];
 #pragma unroll
   for (int j = 0; j < kEpiChunk; ++j) v[j] = __fmul_rn(__uint_as_float(r[j]), alpha);
@@ -217,7 +230,7 @@ __device__ __forceinline__ void epilogue_piece(const uint32_t (&r)[kEpiChunk], f
       }
     }
   }
-  const bool store = row0 < g.M;
+  const bool store = row0 < row_end;
   const uint32_t row_off = (uint32_t)lane * 128u, sw = (uint32_t)(lane & 7);
   if (g.out_f32) {
     if (lane == 0) bulk_wait_read<0>();
@@ -427,7 +440,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(&sm.acc_empty);
         }
-        epilogue_piece(r, alpha, g, &tmO, slots, slot, nt * kBN + c * kEpiChunk, row0, lane);
+        epilogue_piece(r, alpha, g, &tmO, slots, slot, nt * kBN + c * kEpiChunk, row0, g.M, lane);
       }
     }
     // The staged boxes must not be overwritten or freed while a TMA store still reads them.
@@ -463,6 +476,7 @@ struct Gemm2Smem {
   uint8_t sfa[kStages2][kSfStep];         // scale atoms of this CTA's A rows
   uint8_t sfb[kStages2][2 * kSfStep];     // scale atoms of all 256 B rows: [half][k block]
   uint8_t out[4][2][4096];                // per epilogue warp: two staged output boxes
+  int tile_prefix[kMaxGroups + 1];        // grouped mode: tiles of groups 0..g-1
   uint64_t full[kStages2];                // leader: both CTAs' loads of a stage
   uint64_t empty[kStages2];               // each CTA: the leader's MMAs finished with a stage
   uint64_t acc_full;                      // each CTA: the accumulator of a tile is complete
@@ -544,6 +558,56 @@ __host__ __device__ constexpr uint32_t idesc_nvf4_m256(int n) {
   return (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
 }
 
+// One 256 x 256 output tile of the two-SM kernel.
+struct Tile2 {
+  int64_t arow, brow, orow;  // first A row, B row and output row of the tile
+  int64_t row_end;           // output rows at or past this are not stored
+  int ncol0, width;          // first output column, columns in the tile (128 or 256)
+  int kb0, k_blocks;         // contraction: 64-wide blocks kb0 .. kb0 + k_blocks - 1
+  int group;                 // alpha index
+};
+
+__device__ __forceinline__ bool group_ok(int64_t a0, int64_t b0, int64_t o0, int64_t m, int64_t k0, int64_t k,
+                                         const GemmArgs& g) {
+  return a0 >= 0 && b0 >= 0 && o0 >= 0 && m >= 0 && k0 >= 0 && k >= 0 && (a0 & 127) == 0 && (b0 & 127) == 0 &&
+         (m & 127) == 0 && (k0 & 63) == 0 && (k & 63) == 0 && k0 + k <= 64 * (int64_t)g.kb_total;
+}
+
+__device__ __forceinline__ Tile2 tile2_at(int t, const GemmArgs& g, const int* prefix) {
+  Tile2 T;
+  int mt, nt;
+  if (g.groups == nullptr) {
+    tile_coords(t, g.tiles_m, g.tiles_n, mt, nt);
+    T.arow = T.orow = (int64_t)mt * 256;
+    T.brow = (int64_t)nt * kBN;
+    T.row_end = g.M;
+    T.kb0 = 0;
+    T.k_blocks = g.k_blocks;
+    T.group = 0;
+  } else {
+    int lo = 0, hi = g.num_groups - 1;  // the group whose tile range holds t
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (prefix[mid] <= t) lo = mid;
+      else hi = mid - 1;
+    }
+    const int64_t* d = g.groups + kGroupFields * lo;
+    const int64_t a0 = __ldg(d), b0 = __ldg(d + 1), o0 = __ldg(d + 2), m = __ldg(d + 3), k0 = __ldg(d + 4),
+                  k = __ldg(d + 5);
+    tile_coords(t - prefix[lo], (int)((m + 255) / 256), g.tiles_n, mt, nt);
+    T.arow = a0 + (int64_t)mt * 256;
+    T.brow = b0 + (int64_t)nt * kBN;
+    T.orow = o0 + (int64_t)mt * 256;
+    T.row_end = min(o0 + m, g.out_rows);
+    T.kb0 = (int)(k0 >> 6);
+    T.k_blocks = (int)(k >> 6);
+    T.group = lo;
+  }
+  T.ncol0 = nt * kBN;
+  T.width = (int)min((int64_t)kBN, g.N - (int64_t)T.ncol0);
+  return T;
+}
+
 __global__ void __launch_bounds__(kGemmThreads, 1)
     nvfp4_gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                        const __grid_constant__ CUtensorMap tmSA, const __grid_constant__ CUtensorMap tmSB,
@@ -553,7 +617,31 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_rank();
   const int cid = (int)cluster_id(), ncl = (int)cluster_count();
-  const int n_my = (cid < g.n_tiles) ? (g.n_tiles - cid + ncl - 1) / ncl : 0;  // n_tiles counts 256x256 tiles
+
+  if (g.groups != nullptr && warp == 2) {
+    // Tiles per group (ceil(m / 256) x tiles_n; 0 for a group that breaks the contract), scanned.
+    int run = 0;
+    for (int base = 0; base < g.num_groups; base += 32) {
+      const int gi = base + lane;
+      int cnt = 0;
+      if (gi < g.num_groups) {
+        const int64_t* d = g.groups + kGroupFields * gi;
+        const int64_t a0 = __ldg(d), b0 = __ldg(d + 1), o0 = __ldg(d + 2), m = __ldg(d + 3), k0 = __ldg(d + 4),
+                      k = __ldg(d + 5);
+        if (group_ok(a0, b0, o0, m, k0, k, g)) cnt = (int)((m + 255) / 256) * g.tiles_n;
+        else record_status(&g_gemm_status, kStatusBadGroup);
+      }
+      int incl = cnt;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+        if (lane >= o) incl += v;
+      }
+      if (gi < g.num_groups) sm.tile_prefix[gi + 1] = run + incl;
+      run += __shfl_sync(0xFFFFFFFFu, incl, 31);
+    }
+    if (lane == 0) sm.tile_prefix[0] = 0;
+  }
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages2; ++s) {
@@ -578,6 +666,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   cluster_sync();
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
+  const int n_tiles = (g.groups == nullptr) ? g.n_tiles : sm.tile_prefix[g.num_groups];
+  const int n_my = (cid < n_tiles) ? (n_tiles - cid + ncl - 1) / ncl : 0;  // 256x256 tiles of this pair
 
   if (warp == 0) {
     // ------------------------------------------------------------------ producer (both CTAs)
@@ -586,27 +676,29 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t phase = 0;
       bool ok = true;
       for (int i = 0; i < n_my && ok; ++i) {
-        int mt, nt;
-        tile_coords(cid + i * ncl, g.tiles_m, g.tiles_n, mt, nt);
-        const int arow = 2 * mt + (int)rank;  // this CTA's 128-row tile of A
+        const Tile2 T = tile2_at(cid + i * ncl, g, sm.tile_prefix);
+        const int64_t arow = T.arow + (int64_t)rank * kBM;  // this CTA's 128 rows of A
         // Each CTA supplies half of the tile's B rows: 128 for a 256-wide tile, 64 for a 128-wide
         // tail (rows loaded past that half are never read by the MMA).
-        const int width = (int)min((int64_t)kBN, g.N - (int64_t)nt * kBN);
-        const int brow = nt * kBN + (int)rank * (width / 2);
-        for (int ks = 0; ks < g.k_steps; ++ks) {
+        const int64_t brow = T.brow + (int64_t)rank * (T.width / 2);
+        // Scale atoms: one 256-byte row pair per (128-row tile, 64-wide K block).
+        const int64_t sa_row = (arow / kBM) * g.kb_total + T.kb0, sb_row = (T.brow / kBM) * g.kb_total + T.kb0;
+        const int k_steps = (T.k_blocks + 3) / 4;
+        for (int ks = 0; ks < k_steps; ++ks) {
           if (!mbar_wait_warp(&sm.empty[stage], phase ^ 1u)) {
             if (lane == 0) record_status(&g_gemm_status, kStatusTimeoutProducer);
             ok = false;
             break;
           }
           if (elect_one()) {
+            const int kx = (T.kb0 + 4 * ks) * 32;  // packed bytes
             if (rank == 0) mbar_arrive_expect_tx(&sm.full[stage], 2 * kStageBytes2);
-            tma_load_2d_to_leader(sm.a[stage], &tmA, &sm.full[stage], ks * kStepBytes, arow * kBM);
-            tma_load_2d_to_leader(sm.b[stage], &tmB, &sm.full[stage], ks * kStepBytes, brow);
-            tma_load_2d_to_leader(sm.sfa[stage], &tmSA, &sm.full[stage], 0, (arow * g.k_blocks + 4 * ks) * 2);
-            tma_load_2d_to_leader(sm.sfb[stage], &tmSB, &sm.full[stage], 0, ((2 * nt) * g.k_blocks + 4 * ks) * 2);
+            tma_load_2d_to_leader(sm.a[stage], &tmA, &sm.full[stage], kx, (int)arow);
+            tma_load_2d_to_leader(sm.b[stage], &tmB, &sm.full[stage], kx, (int)brow);
+            tma_load_2d_to_leader(sm.sfa[stage], &tmSA, &sm.full[stage], 0, (int)((sa_row + 4 * ks) * 2));
+            tma_load_2d_to_leader(sm.sfb[stage], &tmSB, &sm.full[stage], 0, (int)((sb_row + 4 * ks) * 2));
             tma_load_2d_to_leader(sm.sfb[stage] + kSfStep, &tmSB, &sm.full[stage], 0,
-                                  ((2 * nt + 1) * g.k_blocks + 4 * ks) * 2);
+                                  (int)((sb_row + g.kb_total + 4 * ks) * 2));
           }
           __syncwarp();
           if (++stage == kStages2) {
@@ -623,18 +715,25 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t phase = 0;
       bool ok = true;
       for (int i = 0; i < n_my && ok; ++i) {
-        int mt, nt;
-        tile_coords(cid + i * ncl, g.tiles_m, g.tiles_n, mt, nt);
-        const int width = (int)min((int64_t)kBN, g.N - (int64_t)nt * kBN);
+        const Tile2 T = tile2_at(cid + i * ncl, g, sm.tile_prefix);
+        const int width = T.width;
         const uint32_t idesc = idesc_nvf4_m256(width);
         const uint32_t acc = tmem + ((i & 1) ? kAcc1Col : 0);
-        for (int ks = 0; ks < g.k_steps; ++ks) {
+        if (i >= 1) {
+          if (!mbar_wait_warp(&sm.acc_empty, (uint32_t)((i - 1) & 1))) {
+            if (lane == 0) record_status(&g_gemm_status, kStatusTimeoutEpilogue);
+            break;
+          }
+          tc_fence_after();
+        }
+        const int k_steps = (T.k_blocks + 3) / 4;
+        for (int ks = 0; ks < k_steps; ++ks) {
           if (!mbar_wait_warp(&sm.full[stage], phase)) {
             if (lane == 0) record_status(&g_gemm_status, kStatusTimeoutTma);
             ok = false;
             break;
           }
-          const int nkb = min(4, g.k_blocks - 4 * ks);
+          const int nkb = min(4, T.k_blocks - 4 * ks);
           const uint32_t sfa_s = smem_u32(sm.sfa[stage]), sfb_s = smem_u32(sm.sfb[stage]);
           const uint32_t a_s = smem_u32(sm.a[stage]), b_s = smem_u32(sm.b[stage]);
           auto copy_scales = [&](int kb) {
@@ -642,14 +741,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             tc_cp_scale2(tmem + kSfbCol + 8 * kb, sdesc_scale(sfb_s + kb * 512));
             if (width > 128) tc_cp_scale2(tmem + kSfbCol + 8 * kb + 4, sdesc_scale(sfb_s + kSfStep + kb * 512));
           };
-          if (ks == 0 && i >= 1) {
-            if (!mbar_wait_warp(&sm.acc_empty, (uint32_t)((i - 1) & 1))) {
-              if (lane == 0) record_status(&g_gemm_status, kStatusTimeoutEpilogue);
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-          }
           if (elect_one()) {
             // As in the one-SM kernel, each K block's scale copies directly precede its MMA.
             for (int kb = 0; kb < nkb; ++kb) {
@@ -678,13 +769,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int q = warp & 3;  // TMEM lanes 32q .. 32q+31
     const uint32_t slots = smem_u32(sm.out[q]);
     int slot = 0;
-    float alpha = 1.0f;
-    if (g.alpha_a != nullptr) alpha = *g.alpha_a;
-    if (g.alpha_b != nullptr) alpha = __fmul_rn(alpha, *g.alpha_b);
     for (int i = 0; i < n_my; ++i) {
-      int mt, nt;
-      tile_coords(cid + i * ncl, g.tiles_m, g.tiles_n, mt, nt);
-      const int width = (int)min((int64_t)kBN, g.N - (int64_t)nt * kBN);
+      const Tile2 T = tile2_at(cid + i * ncl, g, sm.tile_prefix);
+      const int width = T.width;
+      float alpha = 1.0f;
+      if (g.alpha_a != nullptr) alpha = __ldg(g.alpha_a + T.group);
+      if (g.alpha_b != nullptr) alpha = __fmul_rn(alpha, __ldg(g.alpha_b + T.group));
       const int buf = i & 1;
       const int base_col = buf ? kAcc1Col : 0;
       if (!mbar_wait(&sm.acc_full, (uint32_t)(i & 1))) {
@@ -699,20 +789,25 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         else mbar_arrive_leader(&sm.acc_empty);
       };
       if (first < 0 && lane == 0) release();
-      const int64_t row0 = (int64_t)mt * 256 + (int64_t)rank * kBM + 32 * q;
+      const int64_t row0 = T.orow + (int64_t)rank * kBM + 32 * q;
       for (int step = 0; step < nch; ++step) {
         const int c = (first < 0) ? step : (step == 0 ? first : (buf == 0 ? step - 1 : step));
         uint32_t r[kEpiChunk];
-        const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(base_col + c * kEpiChunk);
-        RB_TMEM_LD_X32(taddr, r);
-        RB_TMEM_LD_X32(taddr + 32, (r + 32));
-        tmem_ld_wait();
+        if (T.k_blocks > 0) {
+          const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(base_col + c * kEpiChunk);
+          RB_TMEM_LD_X32(taddr, r);
+          RB_TMEM_LD_X32(taddr + 32, (r + 32));
+          tmem_ld_wait();
+        } else {  // an empty contraction: the product is zero (no MMA wrote the accumulator)
+#pragma unroll
+          for (int j = 0; j < kEpiChunk; ++j) r[j] = 0u;
+        }
         if (step == 0 && first >= 0) {
           tc_fence_before();
           __syncwarp();
           if (lane == 0) release();
         }
-        epilogue_piece(r, alpha, g, &tmO, slots, slot, nt * kBN + c * kEpiChunk, row0, lane);
+        epilogue_piece(r, alpha, g, &tmO, slots, slot, T.ncol0 + c * kEpiChunk, row0, T.row_end, lane);
       }
     }
     if (lane == 0) bulk_wait_all();
@@ -733,6 +828,75 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // Host entry points
 // =============================================================================================
 using namespace rb;
+
+namespace {
+
+// Launches the two-SM kernel on min(clusters_wanted, resident clusters) CTA pairs.  A and B scale
+// buffers are viewed as rows of 256 bytes (half a 512-byte atom): one K step of one 128-row tile
+// is 8 consecutive rows.
+int launch_two_sm(GemmArgs& g, const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmO,
+                  const void* a_scale, int64_t a_rows, const void* b_scale, int64_t b_rows, int clusters_wanted,
+                  int dev, cudaStream_t st) {
+  CUtensorMap tmSA, tmSB;
+  if (!rb_host::make_tmap_2d(&tmSA, a_scale, CU_TENSOR_MAP_DATA_TYPE_UINT8, 256,
+                             (uint64_t)(a_rows / 128) * (uint64_t)g.kb_total * 2, 256, 256, 8,
+                             CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !rb_host::make_tmap_2d(&tmSB, b_scale, CU_TENSOR_MAP_DATA_TYPE_UINT8, 256,
+                             (uint64_t)(b_rows / 128) * (uint64_t)g.kb_total * 2, 256, 256, 8,
+                             CU_TENSOR_MAP_SWIZZLE_NONE))
+    return RB_ERR_CUDA;
+  const int sms = rb_host::num_sms(dev);
+  const size_t smem = sizeof(Gemm2Smem) + 1024;
+  static int max_clusters[64] = {0};
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(kGemmThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (dev >= 0 && dev < 64 && max_clusters[dev] == 0) {
+    if (cudaFuncSetAttribute(nvfp4_gemm2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess) {
+      rb_host::set_error("cudaFuncSetAttribute(gemm2) failed: %s", cudaGetErrorString(cudaGetLastError()));
+      return RB_ERR_CUDA;
+    }
+    cfg.gridDim = dim3(2 * (sms / 2), 1, 1);
+    int nc = 0;
+    if (cudaOccupancyMaxActiveClusters(&nc, nvfp4_gemm2_kernel, &cfg) != cudaSuccess || nc < 1) {
+      cudaGetLastError();
+      nc = sms / 2;
+    }
+    max_clusters[dev] = nc;
+  }
+  const int cap = (dev >= 0 && dev < 64) ? max_clusters[dev] : sms / 2;
+  const int clusters = clusters_wanted < cap ? clusters_wanted : cap;
+  if (clusters < 1) return RB_OK;
+  cfg.gridDim = dim3(2 * clusters, 1, 1);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, nvfp4_gemm2_kernel, tmA, tmB, tmSA, tmSB, tmO, g);
+  if (e == cudaSuccess) e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    rb_host::set_error("nvfp4 gemm launch failed: %s", cudaGetErrorString(e));
+    return RB_ERR_CUDA;
+  }
+  return RB_OK;
+}
+
+bool sm100_device(int dev, const char* what) {
+  int major = 0;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  if (major != 10) {
+    rb_host::set_error("%s: the current device is not an sm_100 GPU", what);
+    return false;
+  }
+  return true;
+}
+
+}  // namespace
 
 extern "C" {
 
@@ -775,13 +939,11 @@ int rb_nvfp4_gemm(const void* a_packed, const void* a_scale, const void* b_packe
     return RB_ERR_ARG;
   }
   int dev = rb_host::current_device();
-  int major = 0;
-  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
-  if (major != 10) {
-    rb_host::set_error("nvfp4 gemm: the current device is not an sm_100 GPU");
-    return RB_ERR_DEVICE;
-  }
+  if (!sm100_device(dev, "nvfp4 gemm")) return RB_ERR_DEVICE;
   GemmArgs g;
+  g.groups = nullptr;
+  g.num_groups = 0;
+  g.out_rows = m;
   g.M = m;
   g.N = n;
   g.K = k;
@@ -795,6 +957,7 @@ int rb_nvfp4_gemm(const void* a_packed, const void* a_scale, const void* b_packe
   g.out_f32 = out_dtype == RB_OUT_F32;
   g.ldo = ldo;
   g.k_blocks = (int)(k / 64);
+  g.kb_total = g.k_blocks;
   g.k_steps = (g.k_blocks + 3) / 4;
   g.tiles_n = (int)((n + kBN - 1) / kBN);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
@@ -812,48 +975,11 @@ int rb_nvfp4_gemm(const void* a_packed, const void* a_scale, const void* b_packe
     return RB_ERR_CUDA;
   cudaError_t e = cudaSuccess;
   if (two_sm) {
-    // Scale buffers viewed as rows of 256 bytes (half a 512-byte atom): one K step of one 128-row
-    // tile is 8 consecutive rows.
-    CUtensorMap tmSA, tmSB;
-    if (!rb_host::make_tmap_2d(&tmSA, a_scale, CU_TENSOR_MAP_DATA_TYPE_UINT8, 256, (uint64_t)(m / 128) * (k / 64) * 2,
-                               256, 256, 8, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !rb_host::make_tmap_2d(&tmSB, b_scale, CU_TENSOR_MAP_DATA_TYPE_UINT8, 256, (uint64_t)(n / 128) * (k / 64) * 2,
-                               256, 256, 8, CU_TENSOR_MAP_SWIZZLE_NONE))
-      return RB_ERR_CUDA;
     g.tiles_m = (int)((m + 255) / 256);
     g.n_tiles = g.tiles_m * g.tiles_n;
-    const size_t smem = sizeof(Gemm2Smem) + 1024;
-    static int max_clusters[64] = {0};
-    cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.blockDim = dim3(kGemmThreads, 1, 1);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = st;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    if (dev >= 0 && dev < 64 && max_clusters[dev] == 0) {
-      if (cudaFuncSetAttribute(nvfp4_gemm2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-          cudaSuccess) {
-        rb_host::set_error("cudaFuncSetAttribute(gemm2) failed: %s", cudaGetErrorString(cudaGetLastError()));
-        return RB_ERR_CUDA;
-      }
-      cfg.gridDim = dim3(2 * (sms / 2), 1, 1);
-      int nc = 0;
-      if (cudaOccupancyMaxActiveClusters(&nc, nvfp4_gemm2_kernel, &cfg) != cudaSuccess || nc < 1) {
-        cudaGetLastError();
-        nc = sms / 2;
-      }
-      max_clusters[dev] = nc;
-    }
-    const int cap = (dev >= 0 && dev < 64) ? max_clusters[dev] : sms / 2;
-    const int clusters = g.n_tiles < cap ? g.n_tiles : cap;
-    cfg.gridDim = dim3(2 * clusters, 1, 1);
-    e = cudaLaunchKernelEx(&cfg, nvfp4_gemm2_kernel, tmA, tmB, tmSA, tmSB, tmO, g);
+    return launch_two_sm(g, tmA, tmB, tmO, a_scale, m, b_scale, n, g.n_tiles, dev, st);
   } else {
+    const int sms = rb_host::num_sms(dev);
     g.tiles_m = (int)(m / kBM);
     g.n_tiles = g.tiles_m * g.tiles_n;
     const size_t smem = sizeof(GemmSmem) + 1024;
@@ -875,6 +1001,84 @@ int rb_nvfp4_gemm(const void* a_packed, const void* a_scale, const void* b_packe
     return RB_ERR_CUDA;
   }
   return RB_OK;
+}
+
+int rb_nvfp4_gemm_grouped(const void* a_packed, const void* a_scale, int64_t a_rows, const void* b_packed,
+                          const void* b_scale, int64_t b_rows, int64_t n, int64_t k_total, const int64_t* groups,
+                          int num_groups, const float* alpha_a, const float* alpha_b, void* out, int out_dtype,
+                          int64_t out_rows, int64_t ldo, void* stream) {
+  if (a_rows <= 0 || b_rows <= 0 || n <= 0 || k_total <= 0 || out_rows <= 0 || a_rows % 128 != 0 ||
+      b_rows % 128 != 0 || n % 128 != 0 || k_total % 64 != 0) {
+    rb_host::set_error(
+        "nvfp4 grouped gemm needs a_rows %% 128 == 0, b_rows %% 128 == 0, n %% 128 == 0 and k_total %% 64 == 0, "
+        "got (%lld, %lld, %lld, %lld)",
+        (long long)a_rows, (long long)b_rows, (long long)n, (long long)k_total);
+    return RB_ERR_SHAPE;
+  }
+  if (num_groups < 0 || num_groups > kMaxGroups) {
+    rb_host::set_error("nvfp4 grouped gemm: num_groups must be in [0, %d], got %d", kMaxGroups, num_groups);
+    return RB_ERR_ARG;
+  }
+  if (num_groups == 0) return RB_OK;
+  if (a_packed == nullptr || a_scale == nullptr || b_packed == nullptr || b_scale == nullptr || out == nullptr ||
+      groups == nullptr) {
+    rb_host::set_error("nvfp4 grouped gemm: null pointer argument");
+    return RB_ERR_ARG;
+  }
+  if (out_dtype != RB_OUT_BF16 && out_dtype != RB_OUT_F32) {
+    rb_host::set_error("nvfp4 grouped gemm: unsupported output dtype %d", out_dtype);
+    return RB_ERR_ARG;
+  }
+  const int oesize = out_dtype == RB_OUT_F32 ? 4 : 2;
+  const auto misaligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) != 0; };
+  if (misaligned(a_packed) || misaligned(b_packed) || misaligned(a_scale) || misaligned(b_scale) || misaligned(out) ||
+      (reinterpret_cast<uintptr_t>(groups) & 7) != 0 || ldo < n || ((uint64_t)ldo * oesize) % 16 != 0) {
+    rb_host::set_error("nvfp4 grouped gemm: operands and output must be 16-byte aligned with 16-byte row strides");
+    return RB_ERR_ARG;
+  }
+  if (k_total / 64 > 0x7FFFFFFF / 2 || (a_rows / 128) * (k_total / 64) * 2 > 0x7FFFFFFF ||
+      (b_rows / 128) * (k_total / 64) * 2 > 0x7FFFFFFF || a_rows > 0x7FFFFFFF || b_rows > 0x7FFFFFFF ||
+      out_rows > 0x7FFFFFFF) {
+    rb_host::set_error("nvfp4 grouped gemm: operand too large for 32-bit tensor-map coordinates");
+    return RB_ERR_SHAPE;
+  }
+  int dev = rb_host::current_device();
+  if (!sm100_device(dev, "nvfp4 grouped gemm")) return RB_ERR_DEVICE;
+  GemmArgs g;
+  g.M = out_rows;
+  g.N = n;
+  g.K = k_total;
+  g.a_scale = reinterpret_cast<const uint8_t*>(a_scale);
+  g.b_scale = reinterpret_cast<const uint8_t*>(b_scale);
+  g.alpha_a = alpha_a;
+  g.alpha_b = alpha_b;
+  g.bias = nullptr;
+  g.bias_f32 = 0;
+  g.out = out;
+  g.out_f32 = out_dtype == RB_OUT_F32;
+  g.ldo = ldo;
+  g.tiles_m = 0;
+  g.tiles_n = (int)((n + kBN - 1) / kBN);
+  g.n_tiles = 0;
+  g.k_blocks = 0;
+  g.k_steps = 0;
+  g.groups = groups;
+  g.num_groups = num_groups;
+  g.kb_total = (int)(k_total / 64);
+  g.out_rows = out_rows;
+  CUtensorMap tmA, tmB, tmO;
+  if (!rb_host::make_tmap_2d(&tmA, a_packed, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)(k_total / 2), (uint64_t)a_rows,
+                             (uint64_t)(k_total / 2), kStepBytes, kBM, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !rb_host::make_tmap_2d(&tmB, b_packed, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)(k_total / 2), (uint64_t)b_rows,
+                             (uint64_t)(k_total / 2), kStepBytes, kBM, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !rb_host::make_tmap_2d(&tmO, out, oesize == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                             (uint64_t)n, (uint64_t)out_rows, (uint64_t)ldo * oesize, 128 / oesize, 32,
+                             CU_TENSOR_MAP_SWIZZLE_128B))
+    return RB_ERR_CUDA;
+  // The group sizes live on the device: every resident cluster starts, reads the table and takes
+  // its share of the tiles (clusters without one exit).
+  return launch_two_sm(g, tmA, tmB, tmO, a_scale, a_rows, b_scale, b_rows, 1 << 30, dev,
+                       reinterpret_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

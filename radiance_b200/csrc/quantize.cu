@@ -73,7 +73,22 @@ struct QuantArgs {
   // multiply-add by them (x >> s == umulhi(x, 2^(32-s))) so that it runs on the FMA pipe beside
   // the integer/logic pipe; literal constants would be strength-reduced back into shifts.
   uint32_t p2, p22, p25;
+  // Grouped mode (offs != nullptr): gs[g] is the global scale of rows [offs[g], offs[g+1]); each
+  // 128-row tile takes the group of its first row.
+  const int64_t* offs;
+  int ngroups;
 };
+
+// Group of row r: the last g with offs[g] <= r (empty groups share offsets with their neighbour).
+__device__ __forceinline__ int group_of_row(const int64_t* offs, int ngroups, int64_t r) {
+  int lo = 0, hi = ngroups - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (__ldg(offs + mid) <= r) lo = mid;
+    else hi = mid - 1;
+  }
+  return lo;
+}
 
 struct QHeader {
   uint64_t full[kQStages];
@@ -572,7 +587,10 @@ __global__ void __launch_bounds__(kQThreads, 2)
   }
   QCtx c;
   c.hdr = hdr;
-  const float gs = *a.gs;
+  const int first_group =
+      (a.offs != nullptr) ? group_of_row(a.offs, a.ngroups, (int64_t)((int)blockIdx.x / a.tiles_k) * kQRows) : 0;
+  const float gs = a.gs[first_group];
+  uint32_t cur_gs = __float_as_uint(gs);
   const float denom = __fmul_rn(6.0f, gs);
   c.nden = -denom;
   c.rden = __frcp_rn(denom);
@@ -635,6 +653,22 @@ __global__ void __launch_bounds__(kQThreads, 2)
     const int mt = t / a.tiles_k, kt = t - mt * a.tiles_k;
     const int64_t m0 = (int64_t)mt * kQRows, k0 = (int64_t)kt * kCols;
     const int valid_cols = (int)min((int64_t)kCols, a.K - k0);
+    if (a.offs != nullptr) {
+      // A tile of another group: rebuild the divisor table for its global scale (every thread is
+      // past the previous tile here, so the table is free).
+      const float gt = a.gs[group_of_row(a.offs, a.ngroups, m0)];
+      if (__float_as_uint(gt) != cur_gs) {
+        cur_gs = __float_as_uint(gt);
+        const float dn = __fmul_rn(6.0f, gt);
+        c.nden = -dn;
+        c.rden = __frcp_rn(dn);
+        if (tid < 127) {
+          const float d = __fmul_rn(e4m3_value(tid), gt);
+          hdr->table[tid] = make_float2(d, __frcp_rn(d));
+        }
+        __syncthreads();
+      }
+    }
     const uint32_t tile = smem_u32(smem + (size_t)s * kQTileBytes);
     if constexpr (DO_COL) {
       const int lane = tid & 31;
@@ -721,6 +755,71 @@ __global__ void __launch_bounds__(512) global_scale_kernel(const void* x, int64_
         *gs_out = gs;
       }
     }
+  }
+}
+
+// Per-group global scales: group g is rows [offs[g], offs[g+1]).  Each warp scans a contiguous run
+// of rows, 16 bytes per lane per load, and folds its running maximum into the group's workspace
+// word whenever its run crosses into the next group; the last block to finish converts every
+// group's maximum (quantize.py:205-213 per group) and resets the workspace.
+template <bool F32IN>
+__global__ void __launch_bounds__(256) global_scale_grouped_kernel(const void* x, int64_t rows, int64_t cols,
+                                                                   int64_t ld, const int64_t* offs, int ngroups,
+                                                                   uint32_t* ws, float* gs_out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp_id = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int64_t limit = min(rows, __ldg(offs + ngroups));
+  const int64_t per = (rows + nwarps - 1) / nwarps;
+  const int64_t r0 = max(warp_id * per, __ldg(offs)), r1 = min(limit, warp_id * per + per);
+  constexpr int kPer = F32IN ? 4 : 8;  // elements per 16-byte load
+  const int64_t nvec = cols / kPer;
+  const size_t row_bytes = (size_t)ld * (F32IN ? 4 : 2);
+  int gcur = -1;
+  int64_t gend = -1;
+  uint32_t m = 0;
+  auto flush = [&]() {
+    uint32_t v = m;
+    if constexpr (!F32IN) v = max(v & 0xFFFFu, v >> 16) << 16;  // bf16 bits -> fp32 bits
+    v = __reduce_max_sync(0xFFFFFFFFu, v);
+    if (lane == 0 && gcur >= 0) {
+      atomicMax(&ws[gcur], v);
+      __threadfence();
+    }
+    m = 0;
+  };
+  for (int64_t r = r0; r < r1; ++r) {
+    if (r >= gend) {
+      flush();
+      gcur = group_of_row(offs, ngroups, r);
+      gend = __ldg(offs + gcur + 1);
+    }
+    const uint4* row = reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(x) + (size_t)r * row_bytes);
+    for (int64_t c = lane; c < nvec; c += 32) {
+      const uint4 v = __ldg(row + c);
+      if constexpr (F32IN) {
+        m = max(m, max(max(v.x & 0x7FFFFFFFu, v.y & 0x7FFFFFFFu), max(v.z & 0x7FFFFFFFu, v.w & 0x7FFFFFFFu)));
+      } else {
+        m = __vmaxu2(m, __vmaxu2(__vmaxu2(v.x & 0x7FFF7FFFu, v.y & 0x7FFF7FFFu), __vmaxu2(v.z & 0x7FFF7FFFu, v.w & 0x7FFF7FFFu)));
+      }
+    }
+  }
+  flush();
+  __shared__ int last;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    last = atomicAdd(&ws[ngroups], 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (last) {
+    __threadfence();
+    for (int gi = threadIdx.x; gi < ngroups; gi += blockDim.x) {
+      const uint32_t mb = atomicExch(&ws[gi], 0u);
+      float gsv = __fdiv_rn(__uint_as_float(mb), 2688.0f);
+      gs_out[gi] = (gsv < 1e-12f) ? 1e-12f : gsv;
+    }
+    if (threadIdx.x == 0) atomicExch(&ws[ngroups], 0u);
   }
 }
 
@@ -862,9 +961,9 @@ int rb_nvfp4_global_scale(const void* x, int dtype, int64_t rows, int64_t cols, 
   return RB_OK;
 }
 
-int rb_nvfp4_quantize(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld, const float* gs,
-                      const float* hadamard, const int64_t* seed, void* row_packed, void* row_scale,
-                      void* col_packed, void* col_scale, void* stream) {
+static int quantize_impl(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld, const float* gs,
+                         const int64_t* offs, int ngroups, const float* hadamard, const int64_t* seed,
+                         void* row_packed, void* row_scale, void* col_packed, void* col_scale, void* stream) {
   const bool row = row_packed != nullptr || row_scale != nullptr;
   const bool col = col_packed != nullptr || col_scale != nullptr;
   if (!row && !col) {
@@ -926,10 +1025,73 @@ int rb_nvfp4_quantize(const void* x, int dtype, int64_t rows, int64_t cols, int6
   a.p22 = 1u << 22;
   a.p25 = 1u << 25;
   a.n_tiles = (int)((rows / 128) * a.tiles_k);
+  a.offs = offs;
+  a.ngroups = ngroups;
   const bool had = col && hadamard != nullptr;
   const bool sr = seed != nullptr;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   return f32 ? dispatch_forms<true>(tmap, a, row, col, had, sr, s) : dispatch_forms<false>(tmap, a, row, col, had, sr, s);
+}
+
+int rb_nvfp4_quantize(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld, const float* gs,
+                      const float* hadamard, const int64_t* seed, void* row_packed, void* row_scale,
+                      void* col_packed, void* col_scale, void* stream) {
+  return quantize_impl(x, dtype, rows, cols, ld, gs, nullptr, 0, hadamard, seed, row_packed, row_scale, col_packed,
+                       col_scale, stream);
+}
+
+int rb_nvfp4_quantize_grouped(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld,
+                              const int64_t* offsets, int num_groups, const float* group_gs, const float* hadamard,
+                              const int64_t* seed, void* row_packed, void* row_scale, void* col_packed,
+                              void* col_scale, void* stream) {
+  if (offsets == nullptr || num_groups < 1 || (reinterpret_cast<uintptr_t>(offsets) & 7) != 0) {
+    rb_host::set_error("nvfp4 quantize_grouped: needs at least one group and an 8-byte aligned offsets array");
+    return RB_ERR_ARG;
+  }
+  return quantize_impl(x, dtype, rows, cols, ld, group_gs, offsets, num_groups, hadamard, seed, row_packed,
+                       row_scale, col_packed, col_scale, stream);
+}
+
+int rb_nvfp4_global_scale_grouped(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld,
+                                  const int64_t* offsets, int num_groups, float* gs_out, void* workspace,
+                                  void* stream) {
+  if (gs_out == nullptr || workspace == nullptr || offsets == nullptr || x == nullptr || num_groups < 1 ||
+      (reinterpret_cast<uintptr_t>(offsets) & 7) != 0) {
+    rb_host::set_error("nvfp4 global_scale_grouped: null pointer argument or no groups");
+    return RB_ERR_ARG;
+  }
+  if (dtype != RB_DTYPE_BF16 && dtype != RB_DTYPE_F32) {
+    rb_host::set_error("nvfp4 global_scale_grouped: unsupported dtype %d", dtype);
+    return RB_ERR_ARG;
+  }
+  const int esize = dtype == RB_DTYPE_BF16 ? 2 : 4;
+  if (rows <= 0 || cols <= 0 || ld < cols || (cols * esize) % 16 != 0 || ((uint64_t)ld * esize) % 16 != 0 ||
+      (reinterpret_cast<uintptr_t>(x) & 15) != 0) {
+    rb_host::set_error("nvfp4 global_scale_grouped: needs 16-byte aligned rows of a multiple of 16 bytes "
+                       "(rows=%lld cols=%lld ld=%lld)", (long long)rows, (long long)cols, (long long)ld);
+    return RB_ERR_SHAPE;
+  }
+  if (!device_is_sm100()) {
+    rb_host::set_error("nvfp4 global_scale_grouped: the current device is not an sm_100 GPU");
+    return RB_ERR_DEVICE;
+  }
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int sms = rb_host::num_sms(rb_host::current_device());
+  const int64_t per = (int64_t)(16 / esize) * 256 * 8;  // ~8 loads per thread
+  int64_t grid = (rows * cols + per - 1) / per;
+  if (grid > 4 * sms) grid = 4 * sms;
+  if (grid < 1) grid = 1;
+  uint32_t* ws = reinterpret_cast<uint32_t*>(workspace);
+  if (dtype == RB_DTYPE_BF16)
+    rb::global_scale_grouped_kernel<false><<<(int)grid, 256, 0, s>>>(x, rows, cols, ld, offsets, num_groups, ws, gs_out);
+  else
+    rb::global_scale_grouped_kernel<true><<<(int)grid, 256, 0, s>>>(x, rows, cols, ld, offsets, num_groups, ws, gs_out);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    rb_host::set_error("nvfp4 global_scale_grouped launch failed: %s", cudaGetErrorString(e));
+    return RB_ERR_CUDA;
+  }
+  return RB_OK;
 }
 
 int rb_nvfp4_selftest_division(const float* x, const float* d, int64_t n, uint32_t* mismatches, void* stream) {

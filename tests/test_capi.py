@@ -66,3 +66,17 @@ def test_ops_refuse_cpu_tensors():
     with pytest.raises(RuntimeError, match="no CPU"):
         nv.global_scale_of(x)
     assert not nv.nvfp4_supported("cpu")
+
+
+def test_grouped_record_builders():
+    """The group records the grouped linears hand to the kernel (pure torch, CPU)."""
+    import torch
+
+    from radiance_b200.nvfp4.grouped import align_offsets, groups_over_contraction, groups_over_rows
+
+    offs = align_offsets(torch.tensor([5, 0, 130]))
+    assert offs.tolist() == [0, 128, 128, 384]
+    assert groups_over_rows(offs, 64, 320).tolist() == [
+        [0, 0, 0, 128, 0, 320], [128, 64, 128, 0, 0, 320], [128, 128, 128, 256, 0, 320]]
+    assert groups_over_contraction(offs, 256).tolist() == [
+        [0, 0, 0, 256, 0, 128], [0, 0, 256, 256, 128, 0], [0, 0, 512, 256, 128, 256]]
