@@ -464,6 +464,179 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+# --------------------------------------------------------------------------------------------------
+# Config 4: MoE expert FFN (grouped NVFP4 GEMMs), experts partitioned across ranks
+# --------------------------------------------------------------------------------------------------
+C4_D, C4_E, C4_FFN, C4_TOKENS, C4_TOPK = 2048, 8, 1408, 16384, 2
+C4_FLOPS = 6.0 * C4_TOKENS * C4_TOPK * (C4_D * 2 * C4_FFN + C4_FFN * C4_D)  # 1.701e12 per rank
+C4_METRIC = "NVFP4 MoE expert linears fwd+bwd TFLOPS (BASELINE config 4: 8 experts, top-2, 16384 tokens/GPU)"
+
+
+def _c4_counts(src_rank: int):
+    """Tokens of source rank s routed to each expert: router logits ~N(0,1) (seed s), softmax, top-2."""
+    import torch
+
+    g = torch.Generator().manual_seed(src_rank)
+    logits = torch.randn(C4_TOKENS, C4_E, generator=g)
+    top = logits.softmax(-1).topk(C4_TOPK, dim=-1).indices
+    return torch.bincount(top.flatten(), minlength=C4_E)
+
+
+def run_config4(args):
+    """One step = the expert FFN's two grouped linears (gate+up fused 2048->2816, down 1408->2048),
+    forward + dgrad + wgrad, on the rows this rank's experts receive.  With N ranks each rank owns
+    E/N experts and routes its own 16384 tokens; the routed rows travel to their expert's owner and
+    back with NCCL all-to-alls (dispatch before gate/up, combine after down, and the reverse pair for
+    the gradients), inside the timed region.  Work per rank is fixed as N grows (weak scaling)."""
+    import torch
+    import torch.distributed as dist
+
+    from radiance_b200.nvfp4 import _trace
+    from radiance_b200.nvfp4.grouped import FP4GroupedLinear, align_offsets
+
+    rank, world, local = _dist_setup(args)
+    if C4_E % world:
+        raise SystemExit(f"config 4 needs the {C4_E} experts to divide evenly over {world} ranks")
+    device = torch.device("cuda", local if world > 1 else 0)
+    per = C4_E // world
+    mine = list(range(rank * per, (rank + 1) * per))
+    counts = [_c4_counts(s) for s in range(world)]  # every rank knows every rank's routing (seeded)
+    send = [int(counts[rank][d * per:(d + 1) * per].sum()) for d in range(world)]
+    recv = [int(counts[s][mine].sum()) for s in range(world)]
+    # Received rows arrive source-major (each source's rows sorted by expert); the experts need them
+    # expert-major and padded to 128-row groups: a fixed gather index, built once.
+    exp_counts = torch.stack([counts[s][mine] for s in range(world)]).sum(0)
+    offsets = align_offsets(exp_counts).to(device)
+    t_pad = int(offsets[-1])
+    dst = []
+    fill = [int(o) for o in offsets[:-1].tolist()]
+    for s in range(world):
+        for j, e in enumerate(mine):
+            n = int(counts[s][e])
+            dst.extend(range(fill[j], fill[j] + n))
+            fill[j] += n
+    dst = torch.tensor(dst, dtype=torch.int64, device=device)
+    routed = int(exp_counts.sum())
+    flops = 6.0 * routed * (C4_D * 2 * C4_FFN + C4_FFN * C4_D)
+
+    torch.manual_seed(100 + rank)
+    gate_up = FP4GroupedLinear(per, C4_D, 2 * C4_FFN, device=device)
+    down = FP4GroupedLinear(per, C4_FFN, C4_D, device=device)
+    gate_up.refresh_fp4_cache()
+    down.refresh_fp4_cache()
+    x_send = torch.randn(sum(send), C4_D, device=device).to(torch.bfloat16)
+    h_in = torch.zeros(t_pad, C4_FFN, device=device, dtype=torch.bfloat16)
+    h_in[dst] = torch.randn(routed, C4_FFN, device=device).to(torch.bfloat16)
+    dy_gu = torch.zeros(t_pad, 2 * C4_FFN, device=device, dtype=torch.bfloat16)
+    dy_gu[dst] = (torch.randn(routed, 2 * C4_FFN, device=device) * 1e-3).to(torch.bfloat16)
+    dy_send = (torch.randn(sum(send), C4_D, device=device) * 1e-3).to(torch.bfloat16)
+
+    def a2a(t, out_rows, out_split, in_split):
+        if world == 1:
+            return t
+        out = torch.empty(out_rows, t.shape[1], device=device, dtype=t.dtype)
+        dist.all_to_all_single(out, t, out_split, in_split)
+        return out
+
+    def step():
+        # dispatch: routed rows -> their experts' owner, then expert-major with zero padding
+        xr = a2a(x_send, sum(recv), recv, send)
+        x_exp = torch.zeros(t_pad, C4_D, device=device, dtype=torch.bfloat16)
+        x_exp[dst] = xr
+        x_exp.requires_grad_(True)
+        y_gu = gate_up(x_exp, offsets)
+        h = h_in.detach().requires_grad_(True)  # silu(gate) * up of y_gu, synthetic here
+        y_d = down(h, offsets)
+        a2a(y_d[dst], sum(send), send, recv)  # combine: outputs back to the tokens' ranks
+        dyr = a2a(dy_send, sum(recv), recv, send)  # gradients of the combined outputs
+        dy_d = torch.zeros(t_pad, C4_D, device=device, dtype=torch.bfloat16)
+        dy_d[dst] = dyr
+        torch.autograd.grad(y_d, (h, down.weight), dy_d)
+        gx, _gw = torch.autograd.grad(y_gu, (x_exp, gate_up.weight), dy_gu)
+        a2a(gx[dst], sum(send), send, recv)  # input gradients back to the tokens' ranks
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+    phys = visible.split(",")[torch.cuda.current_device()] if visible else str(torch.cuda.current_device())
+    clocks = ClockSampler(phys)
+    clocks.start()
+    for _ in range(20):
+        step()
+    with _trace.kernel_timer() as kt:
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        torch.cuda.synchronize()
+        start.record()
+        for _ in range(args.steps):
+            step()
+        stop.record()
+        torch.cuda.synchronize()
+        barrier()
+    clk = clocks.stop()
+    ms = max_over_ranks(start.elapsed_time(stop)) / args.steps
+    per_kind = kt.summary()
+    if rank == 0:
+        peaks, peak_kind = _peaks()
+        fp4_peak = 4.0 * peaks["bf16_tflops"]
+        gemm = per_kind.get("gemm", {"launches": 0, "ms": 0.0})
+        gemm_ms = gemm["ms"] / args.steps
+        gemm_tflops = flops / (gemm_ms * 1e-3) / 1e12 if gemm_ms else None
+        line = {
+            "metric": C4_METRIC,
+            "value": round(world * C4_FLOPS / (ms * 1e-3) / 1e12, 2),
+            "unit": "TFLOPS",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "nvfp4 (e2m1 x e4m3 block scales, fp32 accumulate; bf16 in/out, fp32 dW)",
+            "data": "synthetic (seeded; router logits ~N(0,1), W~N(0,0.02), X~N(0,1), dY~N(0,1e-3))",
+            "config": {
+                "workload": "config4: MoE expert FFN linears (gate+up 2048->2816, down 1408->2048) fwd+dgrad+wgrad "
+                            "via FP4GroupedLinear",
+                "experts": C4_E, "experts_per_rank": per, "top_k": C4_TOPK, "tokens_per_gpu": C4_TOKENS,
+                "routed_rows_rank0": routed, "padded_rows_rank0": t_pad,
+                "rank0_expert_rows": exp_counts.tolist(),
+                "parallelism": f"expert-parallel ep{world} (NCCL all-to-all dispatch/combine)" if world > 1
+                else "single GPU, all experts",
+                "flops_basis": "6 x routed rows x (2048 x 2816 + 1408 x 2048); padding rows are overhead",
+            },
+            "kernels": {k: {"launches": v["launches"], "ms": round(v["ms"], 3)} for k, v in per_kind.items()},
+            "roofline": {
+                "kernel": "nvfp4_gemm2_kernel (grouped)",
+                "bound": "tensor",
+                "achieved": None if gemm_tflops is None else round(gemm_tflops, 1),
+                "peak": round(fp4_peak, 1),
+                "peak_basis": f"4 x {peak_kind} dense bf16 ({peaks['bf16_tflops']} TF/s)",
+                "unit": "TFLOP/s",
+                "frac": None if gemm_tflops is None else round(gemm_tflops / fp4_peak, 4),
+                "traffic": None,
+            },
+            "gpu_launches": kt.launches,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -472,11 +645,15 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
+    ap.add_argument("--config", choices=["3", "4"], default="3",
+                    help="3: dense block linears (the headline line); 4: MoE expert linears")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.config == "4":
+        run_config4(args)
     else:
         run_ours(args)
 
