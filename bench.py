@@ -37,9 +37,9 @@ LAYERS = [("qkv", 2048, 6144), ("o", 2048, 2048), ("gate_up", 2048, 11264), ("do
 STEP_FLOPS = 6.0 * TOKENS_PER_GPU * sum(k * n for _, k, n in LAYERS)  # 5.051e12
 METRIC = "NVFP4 linear fwd+bwd TFLOPS (BASELINE config 3 block linears, 16384 tokens/GPU)"
 
-# Average DRAM bytes per GEMM launch of this workload, from `ncu` (profiles/gemm_block_step.txt);
-# None until captured.
-GEMM_DRAM_BYTES_PER_LAUNCH = None
+# Average DRAM bytes (read + write) per GEMM launch of this workload's twelve GEMMs, from one `ncu`
+# capture (profiles/gemm_block_step_traffic.md).
+GEMM_DRAM_BYTES_PER_LAUNCH = 130318549
 
 
 def _peaks():
@@ -327,7 +327,7 @@ def run_ours(args):
                          "GBps": round(amax["work"] / (amax["ms"] * 1e-3) / 1e9, 1) if amax["ms"] else None},
             },
             "roofline": {
-                "kernel": "nvfp4_gemm_kernel (tcgen05 block-scaled GEMM)",
+                "kernel": "nvfp4_gemm2_kernel (tcgen05 cta_group::2 block-scaled GEMM)",
                 "bound": "tensor",
                 "achieved": None if gemm_tflops is None else round(gemm_tflops, 1),
                 "peak": round(fp4_peak, 1),
