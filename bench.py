@@ -637,6 +637,149 @@ def run_config4(args):
         dist.destroy_process_group()
 
 
+# --------------------------------------------------------------------------------------------------
+# Config 5: large dense block, attention linears token-sharded, FFN N-split with output all-gather
+# --------------------------------------------------------------------------------------------------
+C5_TOKENS = 65536
+C5_TOKEN_SHARDED = [("qkv", 4096, 6144), ("o", 4096, 4096), ("down", 14336, 4096)]
+C5_NSPLIT = [("gate_up", 4096, 28672)]  # the largest layer
+C5_FLOPS = 6.0 * C5_TOKENS * sum(k * n for _, k, n in C5_TOKEN_SHARDED + C5_NSPLIT)  # 85.76e12 per step (whole job)
+C5_METRIC = "NVFP4 linear fwd+bwd TFLOPS (BASELINE config 5: d_model 4096 block, 65536 tokens per job)"
+
+
+def run_config5(args):
+    """One step = the block's four linears fwd + dgrad + wgrad for a fixed 65536-token job.  QKV,
+    O and down are token-sharded (65536/N rows per rank, no collective).  The largest layer,
+    gate/up (4096 -> 28672), is split along N: every rank holds 28672/N rows of the weight
+    (quantized with the full weight's global scale), computes its column slice for all 65536 rows
+    and all-gathers the bf16 output; the partial input gradients are all-reduced.  Total work is
+    fixed as N grows (strong scaling)."""
+    import torch
+    import torch.distributed as dist
+
+    from radiance_b200 import nvfp4 as nv
+    from radiance_b200.nvfp4 import _trace
+    from radiance_b200.nvfp4.nsplit import FP4ColumnParallelLinear
+
+    rank, world, local = _dist_setup(args)
+    device = torch.device("cuda", local if world > 1 else 0)
+    if C5_TOKENS % (128 * world):
+        raise SystemExit(f"config 5 needs 65536 tokens to shard into multiples of 128 over {world} ranks")
+    m_local = C5_TOKENS // world
+    # The N-split layer's rows (all 65536 tokens of the job) are replicated over the group: every
+    # rank computes its column slice of gate_up for all of them.
+    m_ffn = C5_TOKENS
+    gen = torch.Generator(device=device).manual_seed(777)  # same on every rank: replicated weights/rows
+    layers, inputs, grads = [], [], []
+    for name, k, n in C5_TOKEN_SHARDED:
+        lin = nv.FP4Linear(k, n, bias=False, device=device)
+        with torch.no_grad():
+            lin.weight.copy_(torch.randn(n, k, device=device, generator=gen) * 0.02)
+        lin.refresh_fp4_cache()
+        layers.append((lin, lin.weight))
+        g_local = torch.Generator(device=device).manual_seed(1000 + rank)
+        inputs.append(torch.randn(m_local, k, device=device, generator=g_local).to(torch.bfloat16))
+        grads.append((torch.randn(m_local, n, device=device, generator=g_local) * 1e-3).to(torch.bfloat16))
+    for name, k, n in C5_NSPLIT:
+        lin = FP4ColumnParallelLinear(k, n, device=device)
+        lin.load_full_weight(torch.randn(n, k, device=device, generator=gen) * 0.02)
+        lin.refresh_fp4_cache()
+        layers.append((lin, lin.local.weight))
+        inputs.append(torch.randn(m_ffn, k, device=device, generator=gen).to(torch.bfloat16))
+        grads.append((torch.randn(m_ffn, n, device=device, generator=gen) * 1e-3).to(torch.bfloat16))
+    flops_rank = 6.0 * (m_local * sum(k * n for _, k, n in C5_TOKEN_SHARDED)
+                        + m_ffn * sum(k * n for _, k, n in C5_NSPLIT) / world)
+    gather_bytes = sum(m_ffn * n * 2 * (world - 1) // world for _, k, n in C5_NSPLIT) if world > 1 else 0
+    reduce_bytes = sum(m_ffn * k * 2 for _, k, n in C5_NSPLIT) if world > 1 else 0
+
+    def step():
+        for (lin, w), x0, dy in zip(layers, inputs, grads):
+            x = x0.detach().requires_grad_(True)
+            y = lin(x)
+            torch.autograd.grad(y, (x, w), dy)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    steps = max(3, min(args.steps, 20))
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+    phys = visible.split(",")[torch.cuda.current_device()] if visible else str(torch.cuda.current_device())
+    clocks = ClockSampler(phys)
+    clocks.start()
+    for _ in range(3):
+        step()
+    with _trace.kernel_timer() as kt:
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        torch.cuda.synchronize()
+        start.record()
+        for _ in range(steps):
+            step()
+        stop.record()
+        torch.cuda.synchronize()
+        barrier()
+    clk = clocks.stop()
+    ms = max_over_ranks(start.elapsed_time(stop)) / steps
+    per_kind = kt.summary()
+    if rank == 0:
+        peaks, peak_kind = _peaks()
+        fp4_peak = 4.0 * peaks["bf16_tflops"]
+        gemm = per_kind.get("gemm", {"launches": 0, "ms": 0.0, "work": 0.0})
+        gemm_tflops = gemm["work"] / (gemm["ms"] * 1e-3) / 1e12 if gemm["ms"] else None
+        line = {
+            "metric": C5_METRIC,
+            "value": round(C5_FLOPS / (ms * 1e-3) / 1e12, 2),
+            "unit": "TFLOPS",
+            "n_gpus": world,
+            "steps": steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms, 3),
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "nvfp4 (e2m1 x e4m3 block scales, fp32 accumulate; bf16 in/out, fp32 dW)",
+            "data": "synthetic (seeded; W~N(0,0.02), X~N(0,1), dY~N(0,1e-3))",
+            "config": {
+                "workload": "config5: d_model 4096 block linears fwd+dgrad+wgrad; QKV/O/down token-sharded, "
+                            "gate_up (the largest) N-split with an NCCL all-gather of its bf16 output",
+                "tokens_per_job": C5_TOKENS, "attention_rows_per_rank": m_local, "ffn_rows": m_ffn,
+                "layers": {n: [k, o] for n, k, o in C5_TOKEN_SHARDED + C5_NSPLIT},
+                "flops_per_rank_per_step": flops_rank,
+                "allgather_bytes_received_per_rank_per_step": gather_bytes,
+                "dgrad_allreduce_bytes_per_rank_per_step": reduce_bytes,
+                "parallelism": f"gate_up N-split over {world} + token-sharded QKV/O/down",
+            },
+            "kernels": {k: {"launches": v["launches"], "ms": round(v["ms"], 3)} for k, v in per_kind.items()},
+            "roofline": {
+                "kernel": "nvfp4_gemm2_kernel",
+                "bound": "tensor",
+                "achieved": None if gemm_tflops is None else round(gemm_tflops, 1),
+                "peak": round(fp4_peak, 1),
+                "peak_basis": f"4 x {peak_kind} dense bf16 ({peaks['bf16_tflops']} TF/s)",
+                "unit": "TFLOP/s",
+                "frac": None if gemm_tflops is None else round(gemm_tflops / fp4_peak, 4),
+                "traffic": None,
+            },
+            "gpu_launches": kt.launches,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -645,8 +788,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
-    ap.add_argument("--config", choices=["3", "4"], default="3",
-                    help="3: dense block linears (the headline line); 4: MoE expert linears")
+    ap.add_argument("--config", choices=["3", "4", "5"], default="3",
+                    help="3: dense block linears (the headline line); 4: MoE expert linears; "
+                         "5: d_model 4096 block with the FFN N-split")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -654,6 +798,8 @@ def main():
         run_reference(args)
     elif args.config == "4":
         run_config4(args)
+    elif args.config == "5":
+        run_config5(args)
     else:
         run_ours(args)
 

@@ -56,7 +56,7 @@ class _FP4LinearFn(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, x, weight, bias, w_fwd_packed, w_fwd_scale, w_fwd_gs, w_dgrad_packed, w_dgrad_scale,
-                w_dgrad_gs, hadamard, seed, recipe):
+                w_dgrad_gs, hadamard, seed, recipe, reduce_grad_scale=None):
         gx = global_scale_of(x)
         rot = hadamard if recipe.hadamard and hadamard.numel() else None
         save_quantized = recipe.save_activations and recipe.grad_gemms and quantize_supported_shape(*x.shape)
@@ -72,6 +72,7 @@ class _FP4LinearFn(torch.autograd.Function):
             saved = (x, x, weight, w_dgrad_packed, w_dgrad_scale, w_dgrad_gs, hadamard, seed, gx)
         ctx.save_for_backward(*saved)
         ctx.recipe = recipe
+        ctx.reduce_grad_scale = reduce_grad_scale
         ctx.has_bias = bias is not None
         ctx.save_quantized = save_quantized
         ctx.x_dtype = x.dtype
@@ -82,12 +83,15 @@ class _FP4LinearFn(torch.autograd.Function):
     def backward(ctx, grad_y):
         x_or_packed, x_or_scale, weight, wdp, wds, wdg, hadamard, seed, gx = ctx.saved_tensors
         recipe: FP4Recipe = ctx.recipe
-        grad_y = grad_y.contiguous()
+        if grad_y.stride(-1) != 1:  # row-strided gradients (an N-split slice) are read in place
+            grad_y = grad_y.contiguous()
         x_dtype = ctx.x_dtype
         fp4_backward = recipe.grad_gemms and quantize_supported_shape(*grad_y.shape)
         if fp4_backward:
             rot = hadamard if recipe.hadamard and hadamard.numel() else None
             gg = global_scale_of(grad_y)
+            if ctx.reduce_grad_scale is not None:  # e.g. the full gradient's scale for an N-split slice
+                ctx.reduce_grad_scale(gg)
             # dgrad operand (rowblock) and wgrad operand (colblock, rotated) from one read of dY,
             # both stochastically rounded with the same seed (linear.py:129, :133-136).
             gq, gqt = quantize_both(grad_y, global_scale=gg, hadamard=rot,
@@ -106,7 +110,7 @@ class _FP4LinearFn(torch.autograd.Function):
             grad_x.to(x_dtype),
             grad_w.to(weight.dtype),
             None if grad_b is None else grad_b.to(weight.dtype),
-            None, None, None, None, None, None, None, None, None,
+            None, None, None, None, None, None, None, None, None, None,
         )
 
 
@@ -132,23 +136,31 @@ class FP4Linear(nn.Linear):
         self.register_buffer("_w_dgrad_gs", torch.ones((), dtype=torch.float32, device=dev), persistent=False)
         self.register_buffer("_hadamard", hadamard_matrix(BLOCK, device=dev), persistent=False)
         self.register_buffer("_seed", torch.zeros((), dtype=torch.int64, device=dev), persistent=False)
+        # Optional in-place reduction of the upstream gradient's global scale (set by N-split layers,
+        # whose slices must share the full gradient's scale).
+        self.reduce_grad_scale = None
         self.register_load_state_dict_post_hook(lambda module, *_: module.invalidate_fp4_cache())
 
     def invalidate_fp4_cache(self) -> None:
         self._cache_valid = False
 
     @torch.no_grad()
-    def refresh_fp4_cache(self) -> None:
+    def refresh_fp4_cache(self, reduce_global_scale=None) -> None:
         """Re-quantize the weight into both orientations, in place (linear.py:193-210).
 
         One read of W writes the forward operand (rowblock) and the dgrad operand (colblock)
         directly into the cache buffers, so their data pointers never move.
+        ``reduce_global_scale``, when given, is applied in place to the 0-d global-scale tensor
+        before quantizing -- an N-split layer passes an all-reduce(MAX) over its ranks so every
+        slice uses the full weight's scale.
         """
         w = self.weight.detach()
         if not w.is_cuda:
             require_nvfp4("FP4Linear.refresh_fp4_cache")
             raise RuntimeError("FP4Linear.refresh_fp4_cache: the weight must be on the CUDA device")
         global_scale_of(w, out=self._w_fwd_gs)
+        if reduce_global_scale is not None:
+            reduce_global_scale(self._w_fwd_gs)
         self._w_dgrad_gs.copy_(self._w_fwd_gs)
         quantize_into_(
             w, global_scale=self._w_fwd_gs,
@@ -173,7 +185,7 @@ class FP4Linear(nn.Linear):
             self._w_fwd_gs,
             self._w_dgrad_packed.view(torch.float4_e2m1fn_x2), self._w_dgrad_scale.view(torch.float8_e4m3fn),
             self._w_dgrad_gs,
-            self._hadamard, self._seed, self.recipe,
+            self._hadamard, self._seed, self.recipe, self.reduce_grad_scale,
         )
         return y.view(*x.shape[:-1], self.out_features)
 

@@ -1,0 +1,136 @@
+"""N-split (column-parallel) NVFP4 linears across the GPUs of one box.
+
+For the largest layers each rank owns ``out_features / g`` output rows of the weight and computes
+its slice of the output for the (replicated) input; the bf16 slices are all-gathered over NVLink
+with NCCL.  Backward: the upstream gradient's local columns feed the rank's dgrad and wgrad; the
+partial input gradients are summed with an all-reduce, and each rank keeps the gradient of its own
+weight rows.
+
+Every slice is quantized with the *full* weight's global scale (an all-reduce(MAX) of the per-slice
+scales: ``max(amax_r) / 2688`` rounds the same as each rank's own division because RN is monotone),
+so a rank's cached operands are exactly the matching rows/columns of the unsplit layer's, and the
+forward output equals the unsplit ``FP4Linear``'s bit for bit.  Backward does the same for the
+upstream gradient's scale, so each rank's dY operands are the matching columns of the unsplit
+layer's; dgrad differs from the unsplit layer's only by the bf16 rounding of the partial sums.
+The collective logic is written against any local module (``ColumnParallel``), which is how it is
+tested on CPU with gloo.  Without an initialised process group everything runs as one rank.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+import torch.nn as nn
+
+from .linear import FP4Linear, FP4Recipe
+
+
+def _world(group) -> int:
+    return dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
+
+
+def _rank(group) -> int:
+    return dist.get_rank(group) if dist.is_available() and dist.is_initialized() else 0
+
+
+class _CopyToSplit(torch.autograd.Function):
+    """Identity forward; all-reduce (sum) of the input gradient backward: the replicated input of a
+    column-parallel layer receives one partial dgrad per rank."""
+
+    @staticmethod
+    def forward(ctx, x, group):
+        ctx.group = group
+        return x
+
+    @staticmethod
+    def backward(ctx, grad):
+        grad = grad.contiguous()
+        if _world(ctx.group) > 1:
+            dist.all_reduce(grad, group=ctx.group)
+        return grad, None
+
+
+class _GatherColumns(torch.autograd.Function):
+    """``(M, n)`` per rank -> ``(M, g * n)`` on every rank, rank r's slice at columns ``r*n ...``:
+    one all-gather into a ``(g, M, n)`` buffer and a column permute.  Backward takes the local
+    columns of the gradient (no communication)."""
+
+    @staticmethod
+    def forward(ctx, y, group):
+        g = _world(group)
+        ctx.group, ctx.g = group, g
+        ctx.rank = _rank(group)
+        y = y.contiguous()
+        if g == 1:
+            return y
+        m, n = y.shape
+        buf = torch.empty(g * m, n, dtype=y.dtype, device=y.device)
+        dist.all_gather_into_tensor(buf, y, group=group)
+        return buf.view(g, m, n).permute(1, 0, 2).reshape(m, g * n)
+
+    @staticmethod
+    def backward(ctx, grad):
+        if ctx.g == 1:
+            return grad, None
+        m, full = grad.shape
+        n = full // ctx.g
+        # A row-strided view: the quantizers read it in place (16-byte aligned rows, n % 128 == 0).
+        return grad.reshape(m, ctx.g, n)[:, ctx.rank, :], None
+
+
+def copy_to_split(x: torch.Tensor, group=None) -> torch.Tensor:
+    return _CopyToSplit.apply(x, group)
+
+
+def gather_split_columns(y: torch.Tensor, group=None) -> torch.Tensor:
+    return _GatherColumns.apply(y, group)
+
+
+class ColumnParallel(nn.Module):
+    """Wraps a local ``in -> out/g`` module as the rank's slice of an ``in -> out`` layer:
+    ``forward(x) = all_gather_columns(local(x))`` with the input-gradient all-reduce."""
+
+    def __init__(self, local: nn.Module, group=None):
+        super().__init__()
+        self.local = local
+        self.group = group
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        lead = x.shape[:-1]
+        y = self.local(copy_to_split(x.reshape(-1, x.shape[-1]), self.group))
+        return gather_split_columns(y, self.group).view(*lead, -1)
+
+
+class FP4ColumnParallelLinear(ColumnParallel):
+    """``FP4Linear(in_features, out_features)`` split along ``out_features`` over the ranks of
+    ``group``: rank r holds rows ``r * out/g : (r + 1) * out/g`` of the weight (``out/g`` a multiple
+    of 128).  ``load_full_weight`` takes the unsplit ``(out, in)`` weight and keeps this rank's rows."""
+
+    def __init__(self, in_features: int, out_features: int, group=None, recipe: FP4Recipe | None = None,
+                 device=None, dtype=None):
+        g = _world(group)
+        if out_features % (128 * g):
+            raise ValueError(f"FP4ColumnParallelLinear: out_features {out_features} must split into multiples of "
+                             f"128 over {g} ranks")
+        super().__init__(FP4Linear(in_features, out_features // g, bias=False, recipe=recipe, device=device,
+                                   dtype=dtype), group)
+        self.in_features, self.out_features, self.world = in_features, out_features, g
+        self.rank = _rank(group)
+        # The upstream gradient is the full dY on every rank (the gather's backward slices it), so
+        # every slice quantizes its columns with the full gradient's scale too.
+        self.local.reduce_grad_scale = self.full_weight_scale_
+
+    @torch.no_grad()
+    def load_full_weight(self, weight: torch.Tensor) -> None:
+        n = self.out_features // self.world
+        self.local.weight.copy_(weight[self.rank * n:(self.rank + 1) * n])
+        self.local.invalidate_fp4_cache()
+
+    def full_weight_scale_(self, gs: torch.Tensor) -> torch.Tensor:
+        """In place: the slice's global scale -> the full weight's (all-reduce MAX over the ranks)."""
+        if self.world > 1:
+            dist.all_reduce(gs, op=dist.ReduceOp.MAX, group=self.group)
+        return gs
+
+    def refresh_fp4_cache(self) -> None:
+        self.local.refresh_fp4_cache(reduce_global_scale=self.full_weight_scale_)

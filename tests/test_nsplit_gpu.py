@@ -1,0 +1,96 @@
+"""N-split NVFP4 linear on two GPUs (NCCL) against the unsplit FP4Linear on the same inputs:
+the forward output is bit-identical (every slice is quantized with the full weight's global
+scale); gradients agree to bf16 accumulation (dgrad partials are summed across ranks; each slice's
+upstream gradient has its own global scale).  Skipped with fewer than two GPUs."""
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, results):
+    import datetime
+
+    import torch.distributed as dist
+    import torch.nn.functional as F
+
+    from radiance_b200 import _lib
+    from radiance_b200.nvfp4 import FP4Linear, FP4Recipe
+    from radiance_b200.nvfp4.nsplit import FP4ColumnParallelLinear
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        g = torch.Generator().manual_seed(0)
+        m, k, n = 512, 512, 1024
+        w = (torch.randn(n, k, generator=g) * 0.02).cuda()
+        x = torch.randn(m, k, generator=g).to(torch.bfloat16).cuda()
+        dy = (torch.randn(m, n, generator=g) * 1e-3).to(torch.bfloat16).cuda()
+        # Round-to-nearest gradients: with stochastic rounding the split and unsplit layers draw
+        # different random bits for dY and agree only in distribution.
+        recipe = FP4Recipe(stochastic_rounding=False)
+        full = FP4Linear(k, n, bias=False, recipe=recipe).cuda()
+        with torch.no_grad():
+            full.weight.copy_(w)
+        full.refresh_fp4_cache()
+        split = FP4ColumnParallelLinear(k, n, recipe=recipe, device="cuda")
+        split.load_full_weight(w)
+        split.refresh_fp4_cache()
+        x1 = x.clone().requires_grad_(True)
+        y1 = full(x1)
+        gx1, gw1 = torch.autograd.grad(y1, (x1, full.weight), dy)
+        x2 = x.clone().requires_grad_(True)
+        y2 = split(x2)
+        gx2, gw2 = torch.autograd.grad(y2, (x2, split.local.weight), dy)
+        sl = slice(rank * (n // world), (rank + 1) * (n // world))
+
+        def cos(a, b):
+            return F.cosine_similarity(a.flatten().float(), b.flatten().float(), dim=0).item()
+
+        cx, cw = cos(gx1, gx2), cos(gw1[sl], gw2)
+        results[rank] = (
+            torch.equal(y1, y2),
+            cx > 0.999,
+            cw > 0.999,
+            torch.equal(full._w_fwd_gs, split.local._w_fwd_gs),
+            _lib.device_status() == 0,
+            f"dgrad cosine {cx:.6f}, wgrad cosine {cw:.6f}",
+        )
+    finally:
+        dist.destroy_process_group()
+
+
+def test_nsplit_two_gpus_matches_unsplit():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    world = 2
+    ctx = mp.get_context("spawn")
+    manager = ctx.Manager()
+    results = manager.dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, results)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    for r in range(world):
+        assert all(results[r][:5]), (r, results[r])
