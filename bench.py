@@ -681,7 +681,7 @@ def run_config5(args):
         inputs.append(torch.randn(m_local, k, device=device, generator=g_local).to(torch.bfloat16))
         grads.append((torch.randn(m_local, n, device=device, generator=g_local) * 1e-3).to(torch.bfloat16))
     for name, k, n in C5_NSPLIT:
-        lin = FP4ColumnParallelLinear(k, n, device=device)
+        lin = FP4ColumnParallelLinear(k, n, device=device, fused_gather=args.nsplit == "fused")
         lin.load_full_weight(torch.randn(n, k, device=device, generator=gen) * 0.02)
         lin.refresh_fp4_cache()
         layers.append((lin, lin.local.weight))
@@ -759,6 +759,9 @@ def run_config5(args):
                 "allgather_bytes_received_per_rank_per_step": gather_bytes,
                 "dgrad_allreduce_bytes_per_rank_per_step": reduce_bytes,
                 "parallelism": f"gate_up N-split over {world} + token-sharded QKV/O/down",
+                "nsplit_gather": ("GEMM epilogue stores each tile into every rank's output over NVLink "
+                                  "(rb_nvfp4_gemm_allgather, symmetric memory)") if args.nsplit == "fused"
+                else "NCCL all_gather_into_tensor + column permute",
             },
             "kernels": {k: {"launches": v["launches"], "ms": round(v["ms"], 3)} for k, v in per_kind.items()},
             "roofline": {
@@ -788,6 +791,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
+    ap.add_argument("--nsplit", choices=["fused", "nccl"], default="fused",
+                    help="config 5: the N-split layer's output all-gather (fused into the GEMM, or NCCL)")
     ap.add_argument("--config", choices=["3", "4", "5"], default="3",
                     help="3: dense block linears (the headline line); 4: MoE expert linears; "
                          "5: d_model 4096 block with the FFN N-split")

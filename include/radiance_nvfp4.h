@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define RB_NVFP4_ABI_VERSION 2
+#define RB_NVFP4_ABI_VERSION 3
 
 /* Input element types. */
 #define RB_DTYPE_BF16 0
@@ -129,6 +129,21 @@ int rb_nvfp4_quantize(const void* x, int dtype, int64_t rows, int64_t cols, int6
 int rb_nvfp4_gemm(const void* a_packed, const void* a_scale, const void* b_packed, const void* b_scale, int64_t m,
                   int64_t n, int64_t k, const float* alpha_a, const float* alpha_b, const void* bias, int bias_dtype,
                   void* out, int out_dtype, int64_t ldo, void* stream);
+
+/*
+ * rb_nvfp4_gemm whose epilogue also writes every output tile into `npeers` other GPUs' copies of
+ * the output: the all-gather of an N-split layer fused into the GEMM.  Rank r of g computes
+ * columns r*n .. r*n+n-1 of a (m, g*n) output and stores them into all g copies over NVLink while
+ * later tiles are still being multiplied.  peer_out is a host array of npeers (<= 7) device
+ * pointers, each at the position `out` has in that GPU's buffer (same ldo); the memory must be
+ * mapped into this process (peer access or symmetric memory).  The call only writes; the caller
+ * synchronises the GPUs before reading the peers' copies.  It stands in for the bf16 output
+ * all-gather of the N-split layers (no reference counterpart: radiance has no N-split path).
+ */
+int rb_nvfp4_gemm_allgather(const void* a_packed, const void* a_scale, const void* b_packed, const void* b_scale,
+                            int64_t m, int64_t n, int64_t k, const float* alpha_a, const float* alpha_b,
+                            const void* bias, int bias_dtype, void* out, int out_dtype, int64_t ldo,
+                            void* const* peer_out, int npeers, void* stream);
 
 /*
  * Grouped (mixture-of-experts) GEMMs, global scales and quantization.  radiance runs its experts

@@ -35,6 +35,11 @@ SIGNATURES: dict[str, tuple] = {
         [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _c_void_p, _c_void_p, _c_void_p, _int,
          _c_void_p, _int, _i64, _c_void_p],
     ),
+    "rb_nvfp4_gemm_allgather": (
+        _int,
+        [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _c_void_p, _c_void_p, _c_void_p, _int,
+         _c_void_p, _int, _i64, ctypes.POINTER(_c_void_p), _int, _c_void_p],
+    ),
     "rb_nvfp4_global_scale_grouped": (
         _int, [_c_void_p, _int, _i64, _i64, _i64, _c_void_p, _int, _c_void_p, _c_void_p, _c_void_p],
     ),
@@ -51,7 +56,7 @@ SIGNATURES: dict[str, tuple] = {
     "rb_nvfp4_selftest_division": (_int, [_c_void_p, _c_void_p, _i64, _c_void_p, _c_void_p]),
 }
 
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 RB_DTYPE_BF16 = 0
 RB_DTYPE_F32 = 1

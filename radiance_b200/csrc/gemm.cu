@@ -78,8 +78,14 @@ struct GemmArgs {
   int num_groups;
   int kb_total;
   int64_t out_rows;
+  // N-split all-gather fused into the epilogue: npeers device pointers into other GPUs' copies of
+  // the output (peer memory mapped into this process), each at the position `out` has in its
+  // own; every element stored to `out` is also written to each of them.
+  void* peer_out[7];
+  int npeers;
 };
 
+constexpr int kMaxPeers = 7;
 constexpr int kMaxGroups = 256;
 constexpr int kGroupFields = 6;
 
@@ -168,6 +174,14 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<const uint32_t*>(&v);
 }
 
+__device__ __forceinline__ void st_global_v4(void* p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.global.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+  return v;
+}
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
@@ -232,6 +246,21 @@ __device__ __forceinline__ void epilogue_piece(const uint32_t (&r)[kEpiChunk], f
   }
   const bool store = row0 < row_end;
   const uint32_t row_off = (uint32_t)lane * 128u, sw = (uint32_t)(lane & 7);
+  // Copies a staged box (32 rows x 128 B) to every peer output with coalesced 16-byte stores:
+  // lane l moves chunk l % 8 of rows 4i + l/8.  The loads from the box finish before the warp's
+  // next __syncwarp, so the box can be refilled right after.
+  auto to_peers = [&](uint32_t boxa, int64_t col_bytes) {
+    const int esz = g.out_f32 ? 4 : 2;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int r = 4 * i + (lane >> 3), c = lane & 7;
+      if (row0 + r >= row_end) continue;
+      const uint4 val = ld_shared_v4(boxa + r * 128 + ((c ^ (r & 7)) << 4));
+      const int64_t off = ((row0 + r) * g.ldo) * esz + col_bytes + c * 16;
+      for (int p = 0; p < g.npeers; ++p)
+        st_global_v4(reinterpret_cast<uint8_t*>(g.peer_out[p]) + off, val.x, val.y, val.z, val.w);
+    }
+  };
   if (g.out_f32) {
     if (lane == 0) bulk_wait_read<0>();
     __syncwarp();
@@ -249,6 +278,10 @@ __device__ __forceinline__ void epilogue_piece(const uint32_t (&r)[kEpiChunk], f
       tma_store_2d(tmO, slots + kOutBox, col0 + 32, (int)row0);
       bulk_commit_group();
     }
+    if (g.npeers > 0 && store) {
+      to_peers(slots, (int64_t)col0 * 4);
+      to_peers(slots + kOutBox, (int64_t)(col0 + 32) * 4);
+    }
   } else {
     if (lane == 0) bulk_wait_read<1>();
     __syncwarp();
@@ -264,6 +297,7 @@ __device__ __forceinline__ void epilogue_piece(const uint32_t (&r)[kEpiChunk], f
       tma_store_2d(tmO, box, col0, (int)row0);
       bulk_commit_group();
     }
+    if (g.npeers > 0 && store) to_peers(box, (int64_t)col0 * 2);
     slot ^= 1;
   }
 }
@@ -445,6 +479,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     // The staged boxes must not be overwritten or freed while a TMA store still reads them.
     if (lane == 0) bulk_wait_all();
+    if (g.npeers > 0) __threadfence_system();
     __syncwarp();
   }
 
@@ -811,6 +846,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
     if (lane == 0) bulk_wait_all();
+    if (g.npeers > 0) __threadfence_system();
     __syncwarp();
   }
 
@@ -911,9 +947,20 @@ uint32_t rb_internal_gemm_status(int clear) {
   return v;
 }
 
-int rb_nvfp4_gemm(const void* a_packed, const void* a_scale, const void* b_packed, const void* b_scale, int64_t m,
-                  int64_t n, int64_t k, const float* alpha_a, const float* alpha_b, const void* bias, int bias_dtype,
-                  void* out, int out_dtype, int64_t ldo, void* stream) {
+static int gemm_impl(const void* a_packed, const void* a_scale, const void* b_packed, const void* b_scale, int64_t m,
+                     int64_t n, int64_t k, const float* alpha_a, const float* alpha_b, const void* bias,
+                     int bias_dtype, void* out, int out_dtype, int64_t ldo, void* const* peer_out, int npeers,
+                     void* stream) {
+  if (npeers < 0 || npeers > kMaxPeers || (npeers > 0 && peer_out == nullptr)) {
+    rb_host::set_error("nvfp4 gemm: npeers must be in [0, %d] with a peer pointer array", kMaxPeers);
+    return RB_ERR_ARG;
+  }
+  for (int p = 0; p < npeers; ++p) {
+    if (peer_out[p] == nullptr || (reinterpret_cast<uintptr_t>(peer_out[p]) & 15) != 0) {
+      rb_host::set_error("nvfp4 gemm: peer output %d is null or not 16-byte aligned", p);
+      return RB_ERR_ARG;
+    }
+  }
   if (m <= 0 || n <= 0 || k <= 0 || m % 128 != 0 || n % 128 != 0 || k % 64 != 0) {
     rb_host::set_error("nvfp4 gemm needs m %% 128 == 0, n %% 128 == 0 and k %% 64 == 0, got (%lld, %lld, %lld)",
                        (long long)m, (long long)n, (long long)k);
@@ -944,6 +991,8 @@ int rb_nvfp4_gemm(const void* a_packed, const void* a_scale, const void* b_packe
   g.groups = nullptr;
   g.num_groups = 0;
   g.out_rows = m;
+  g.npeers = npeers;
+  for (int p = 0; p < kMaxPeers; ++p) g.peer_out[p] = p < npeers ? peer_out[p] : nullptr;
   g.M = m;
   g.N = n;
   g.K = k;
@@ -1001,6 +1050,21 @@ int rb_nvfp4_gemm(const void* a_packed, const void* a_scale, const void* b_packe
     return RB_ERR_CUDA;
   }
   return RB_OK;
+}
+
+int rb_nvfp4_gemm(const void* a_packed, const void* a_scale, const void* b_packed, const void* b_scale, int64_t m,
+                  int64_t n, int64_t k, const float* alpha_a, const float* alpha_b, const void* bias, int bias_dtype,
+                  void* out, int out_dtype, int64_t ldo, void* stream) {
+  return gemm_impl(a_packed, a_scale, b_packed, b_scale, m, n, k, alpha_a, alpha_b, bias, bias_dtype, out, out_dtype,
+                   ldo, nullptr, 0, stream);
+}
+
+int rb_nvfp4_gemm_allgather(const void* a_packed, const void* a_scale, const void* b_packed, const void* b_scale,
+                            int64_t m, int64_t n, int64_t k, const float* alpha_a, const float* alpha_b,
+                            const void* bias, int bias_dtype, void* out, int out_dtype, int64_t ldo,
+                            void* const* peer_out, int npeers, void* stream) {
+  return gemm_impl(a_packed, a_scale, b_packed, b_scale, m, n, k, alpha_a, alpha_b, bias, bias_dtype, out, out_dtype,
+                   ldo, peer_out, npeers, stream);
 }
 
 int rb_nvfp4_gemm_grouped(const void* a_packed, const void* a_scale, int64_t a_rows, const void* b_packed,
@@ -1066,6 +1130,8 @@ int rb_nvfp4_gemm_grouped(const void* a_packed, const void* a_scale, int64_t a_r
   g.num_groups = num_groups;
   g.kb_total = (int)(k_total / 64);
   g.out_rows = out_rows;
+  g.npeers = 0;
+  for (int p = 0; p < kMaxPeers; ++p) g.peer_out[p] = nullptr;
   CUtensorMap tmA, tmB, tmO;
   if (!rb_host::make_tmap_2d(&tmA, a_packed, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)(k_total / 2), (uint64_t)a_rows,
                              (uint64_t)(k_total / 2), kStepBytes, kBM, CU_TENSOR_MAP_SWIZZLE_128B) ||

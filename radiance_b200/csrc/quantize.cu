@@ -726,6 +726,26 @@ __global__ void __launch_bounds__(512) global_scale_kernel(const void* x, int64_
       if constexpr (F32IN) m = max(m, reinterpret_cast<const uint32_t*>(x)[e] & 0x7FFFFFFFu);
       else m = max(m, (uint32_t)(reinterpret_cast<const uint16_t*>(x)[e] & 0x7FFFu));
     }
+  } else if (((reinterpret_cast<uintptr_t>(x) | (uintptr_t)(ld * (F32IN ? 4 : 2)) |
+               (uintptr_t)(cols * (F32IN ? 4 : 2))) & 15) == 0) {
+    // Row-strided with 16-byte aligned rows (a column slice of a wider tensor): one warp per row,
+    // 16-byte loads along it.
+    constexpr int kPer = F32IN ? 4 : 8;
+    const int lane = threadIdx.x & 31;
+    const int64_t warp_id = gtid >> 5, nwarps = stride >> 5;
+    const int64_t nvec = cols / kPer, ldv = ld / kPer;
+    const uint4* xv = reinterpret_cast<const uint4*>(x);
+    for (int64_t r = warp_id; r < rows; r += nwarps) {
+      for (int64_t c = lane; c < nvec; c += 32) {
+        const uint4 v = __ldg(xv + r * ldv + c);
+        if constexpr (F32IN) {
+          m = max(m, max(max(v.x & 0x7FFFFFFFu, v.y & 0x7FFFFFFFu), max(v.z & 0x7FFFFFFFu, v.w & 0x7FFFFFFFu)));
+        } else {
+          m = __vmaxu2(m, __vmaxu2(__vmaxu2(v.x & 0x7FFF7FFFu, v.y & 0x7FFF7FFFu),
+                                   __vmaxu2(v.z & 0x7FFF7FFFu, v.w & 0x7FFF7FFFu)));
+        }
+      }
+    }
   } else {
     for (int64_t e = gtid; e < rows * cols; e += stride) {
       const int64_t r = e / cols, c = e - r * cols;

@@ -56,7 +56,7 @@ class _FP4LinearFn(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, x, weight, bias, w_fwd_packed, w_fwd_scale, w_fwd_gs, w_dgrad_packed, w_dgrad_scale,
-                w_dgrad_gs, hadamard, seed, recipe, reduce_grad_scale=None):
+                w_dgrad_gs, hadamard, seed, recipe, reduce_grad_scale=None, output_gemm=None):
         gx = global_scale_of(x)
         rot = hadamard if recipe.hadamard and hadamard.numel() else None
         save_quantized = recipe.save_activations and recipe.grad_gemms and quantize_supported_shape(*x.shape)
@@ -65,7 +65,11 @@ class _FP4LinearFn(torch.autograd.Function):
             xq, xqt = quantize_both(x, global_scale=gx, hadamard=rot)
         else:
             xq = quantize(x, -1, global_scale=gx)
-        y = mm(xq, NVFP4Tensor(w_fwd_packed, w_fwd_scale, w_fwd_gs), out_dtype=x.dtype, bias=bias)
+        wq = NVFP4Tensor(w_fwd_packed, w_fwd_scale, w_fwd_gs)
+        if output_gemm is None:
+            y = mm(xq, wq, out_dtype=x.dtype, bias=bias)
+        else:  # e.g. an N-split slice whose GEMM also writes the peers' copies of the output
+            y = output_gemm(xq, wq, bias, x.dtype)
         if save_quantized:
             saved = (xqt.packed, xqt.scale, weight, w_dgrad_packed, w_dgrad_scale, w_dgrad_gs, hadamard, seed, gx)
         else:
@@ -110,7 +114,7 @@ class _FP4LinearFn(torch.autograd.Function):
             grad_x.to(x_dtype),
             grad_w.to(weight.dtype),
             None if grad_b is None else grad_b.to(weight.dtype),
-            None, None, None, None, None, None, None, None, None, None,
+            None, None, None, None, None, None, None, None, None, None, None,
         )
 
 
@@ -137,8 +141,10 @@ class FP4Linear(nn.Linear):
         self.register_buffer("_hadamard", hadamard_matrix(BLOCK, device=dev), persistent=False)
         self.register_buffer("_seed", torch.zeros((), dtype=torch.int64, device=dev), persistent=False)
         # Optional in-place reduction of the upstream gradient's global scale (set by N-split layers,
-        # whose slices must share the full gradient's scale).
+        # whose slices must share the full gradient's scale), and an optional replacement for the
+        # forward GEMM, called as output_gemm(xq, wq, bias, out_dtype) (set by the fused N-split).
         self.reduce_grad_scale = None
+        self.output_gemm = None
         self.register_load_state_dict_post_hook(lambda module, *_: module.invalidate_fp4_cache())
 
     def invalidate_fp4_cache(self) -> None:
@@ -185,7 +191,7 @@ class FP4Linear(nn.Linear):
             self._w_fwd_gs,
             self._w_dgrad_packed.view(torch.float4_e2m1fn_x2), self._w_dgrad_scale.view(torch.float8_e4m3fn),
             self._w_dgrad_gs,
-            self._hadamard, self._seed, self.recipe, self.reduce_grad_scale,
+            self._hadamard, self._seed, self.recipe, self.reduce_grad_scale, self.output_gemm,
         )
         return y.view(*x.shape[:-1], self.out_features)
 

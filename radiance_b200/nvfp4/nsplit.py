@@ -18,11 +18,16 @@ tested on CPU with gloo.  Without an initialised process group everything runs a
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 import torch.distributed as dist
 import torch.nn as nn
 
+from .. import _lib
+from . import _trace
 from .linear import FP4Linear, FP4Recipe
+from .quantize import _stream_ptr
 
 
 def _world(group) -> int:
@@ -78,6 +83,23 @@ class _GatherColumns(torch.autograd.Function):
         return grad.reshape(m, ctx.g, n)[:, ctx.rank, :], None
 
 
+class _FusedGathered(torch.autograd.Function):
+    """The fused path's gather: the slice's GEMM already wrote every rank's copy of the full
+    output (``buf``), so forward just hands that buffer out; backward takes the local columns of
+    the gradient, as ``_GatherColumns`` does."""
+
+    @staticmethod
+    def forward(ctx, y_local, buf, g, rank):
+        ctx.g, ctx.rank = g, rank
+        return buf.detach()
+
+    @staticmethod
+    def backward(ctx, grad):
+        m, full = grad.shape
+        n = full // ctx.g
+        return grad.reshape(m, ctx.g, n)[:, ctx.rank, :], None, None, None
+
+
 def copy_to_split(x: torch.Tensor, group=None) -> torch.Tensor:
     return _CopyToSplit.apply(x, group)
 
@@ -104,10 +126,17 @@ class ColumnParallel(nn.Module):
 class FP4ColumnParallelLinear(ColumnParallel):
     """``FP4Linear(in_features, out_features)`` split along ``out_features`` over the ranks of
     ``group``: rank r holds rows ``r * out/g : (r + 1) * out/g`` of the weight (``out/g`` a multiple
-    of 128).  ``load_full_weight`` takes the unsplit ``(out, in)`` weight and keeps this rank's rows."""
+    of 128).  ``load_full_weight`` takes the unsplit ``(out, in)`` weight and keeps this rank's rows.
+
+    ``fused_gather=True`` replaces the NCCL all-gather with the GEMM's own epilogue: the slice's
+    GEMM (``rb_nvfp4_gemm_allgather``) stores every output tile into all ranks' copies of a
+    full-width output buffer in symmetric memory over NVLink, so the gather overlaps the
+    multiplication and needs no staging buffer or column permute.  The returned output is that
+    buffer: it stays valid until this layer's next forward (ranks synchronise before and after the
+    GEMM)."""
 
     def __init__(self, in_features: int, out_features: int, group=None, recipe: FP4Recipe | None = None,
-                 device=None, dtype=None):
+                 device=None, dtype=None, fused_gather: bool = False):
         g = _world(group)
         if out_features % (128 * g):
             raise ValueError(f"FP4ColumnParallelLinear: out_features {out_features} must split into multiples of "
@@ -119,6 +148,58 @@ class FP4ColumnParallelLinear(ColumnParallel):
         # The upstream gradient is the full dY on every rank (the gather's backward slices it), so
         # every slice quantizes its columns with the full gradient's scale too.
         self.local.reduce_grad_scale = self.full_weight_scale_
+        self.fused_gather = fused_gather and self.world > 1
+        self._buffers: dict = {}
+        self._current = None
+        if self.fused_gather:
+            self.local.output_gemm = self._gemm_into_all_ranks
+
+    def _symmetric_output(self, rows: int, dtype: torch.dtype, device: torch.device):
+        key = (rows, dtype)
+        if key not in self._buffers:
+            import torch.distributed._symmetric_memory as symm
+
+            group = self.group if self.group is not None else dist.group.WORLD
+            buf = symm.empty(rows, self.out_features, dtype=dtype, device=device)
+            handle = symm.rendezvous(buf, group)
+            self._buffers[key] = (buf, handle)
+        return self._buffers[key]
+
+    def _gemm_into_all_ranks(self, xq, wq, bias, out_dtype):
+        """The slice's forward GEMM writing its columns into every rank's full-width buffer."""
+        if out_dtype not in (torch.bfloat16, torch.float32) or bias is not None:
+            raise ValueError("FP4ColumnParallelLinear(fused_gather=True) supports bf16/fp32 outputs without bias")
+        m = xq.packed.shape[0]
+        n, k = wq.packed.shape[0], xq.packed.shape[1] * 2
+        buf, handle = self._symmetric_output(m, out_dtype, xq.packed.device)
+        esize = buf.element_size()
+        col0 = self.rank * n
+        peers = [handle.buffer_ptrs[p] + col0 * esize for p in range(self.world) if p != self.rank]
+        arr = (ctypes.c_void_p * len(peers))(*peers)
+        lib = _lib.load()
+        handle.barrier(channel=0)  # every rank is done with the previous contents
+        tok = _trace.begin("gemm", 2.0 * m * n * k)
+        _lib.check(
+            lib.rb_nvfp4_gemm_allgather(
+                xq.packed.data_ptr(), xq.scale.data_ptr(), wq.packed.data_ptr(), wq.scale.data_ptr(), m, n, k,
+                xq.global_scale.data_ptr(), wq.global_scale.data_ptr(), None, 0, buf[:, col0:].data_ptr(),
+                _lib.RB_OUT_BF16 if out_dtype == torch.bfloat16 else _lib.RB_OUT_F32, self.out_features, arr,
+                len(peers), _stream_ptr(buf.device),
+            ),
+            "nvfp4.gemm_allgather",
+        )
+        _trace.end(tok)
+        handle.barrier(channel=0)  # every rank's tiles are in every copy
+        self._current = buf
+        return buf[:, col0:col0 + n]
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if not self.fused_gather:
+            return super().forward(x)
+        lead = x.shape[:-1]
+        y_local = self.local(copy_to_split(x.reshape(-1, x.shape[-1]), self.group))
+        out = _FusedGathered.apply(y_local, self._current, self.world, self.rank)
+        return out.view(*lead, -1)
 
     @torch.no_grad()
     def load_full_weight(self, weight: torch.Tensor) -> None:

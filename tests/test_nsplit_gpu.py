@@ -63,12 +63,23 @@ def _worker(rank, world, port, results):
             return F.cosine_similarity(a.flatten().float(), b.flatten().float(), dim=0).item()
 
         cx, cw = cos(gx1, gx2), cos(gw1[sl], gw2)
+        # The fused path: the slice's GEMM writes every rank's copy of the output over NVLink.
+        fused = FP4ColumnParallelLinear(k, n, recipe=recipe, device="cuda", fused_gather=True)
+        fused.load_full_weight(w)
+        fused.refresh_fp4_cache()
+        x3 = x.clone().requires_grad_(True)
+        y3 = fused(x3)
+        same_fused = torch.equal(y1, y3)
+        gx3, gw3 = torch.autograd.grad(y3, (x3, fused.local.weight), dy)
+        y3b = fused(x3.detach())  # a second call reuses the buffer
         results[rank] = (
             torch.equal(y1, y2),
             cx > 0.999,
             cw > 0.999,
             torch.equal(full._w_fwd_gs, split.local._w_fwd_gs),
             _lib.device_status() == 0,
+            same_fused and torch.equal(y1, y3b),
+            torch.equal(gx2, gx3) and torch.equal(gw2, gw3),
             f"dgrad cosine {cx:.6f}, wgrad cosine {cw:.6f}",
         )
     finally:
@@ -93,4 +104,4 @@ def test_nsplit_two_gpus_matches_unsplit():
             p.kill()
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     for r in range(world):
-        assert all(results[r][:5]), (r, results[r])
+        assert all(results[r][:7]), (r, results[r])

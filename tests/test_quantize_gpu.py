@@ -210,6 +210,18 @@ def test_global_scale_shapes_and_workspace_reuse(nv):
                 assert np.float32(nv.global_scale_of(x).item()).view(np.uint32) == want.view(np.uint32)
 
 
+def test_global_scale_of_column_slices(nv):
+    """Row-strided inputs (an N-split layer's slice of the gradient): 16-byte aligned rows take the
+    vectorised strided path, others the element path; both equal the oracle bit for bit."""
+    for dtype in (torch.bfloat16, torch.float32):
+        base = torch.randn(300, 1536, device="cuda", dtype=dtype)
+        base[17, 700] = 55.0  # the maximum sits inside the slice
+        for sl in (slice(512, 1024), slice(8, 1032), slice(3, 1000)):
+            x = base[:, sl]
+            want = O.global_scale_of(to_numpy_f32(x))
+            assert np.float32(nv.global_scale_of(x).item()).view(np.uint32) == want.view(np.uint32), (dtype, sl)
+
+
 # --- stochastic rounding ----------------------------------------------------------------------------
 
 
