@@ -22,6 +22,8 @@ with the host, so routing counts never leave the GPU.  ``FP4BatchedExperts`` kee
 
 from __future__ import annotations
 
+import weakref
+
 import torch
 import torch.nn as nn
 import torch.nn.functional as F
@@ -224,6 +226,23 @@ def groups_over_contraction(offsets: torch.Tensor, out_rows_per_group: int) -> t
                         size], dim=1)
 
 
+_RECORD_CACHE: dict = {}
+
+
+def _records(kind: str, offsets: torch.Tensor, a: int, b: int) -> torch.Tensor:
+    """Group records for ``offsets``, cached per offsets tensor object (held weakly) and its version:
+    one step's routing is reused by every expert layer, forward and backward."""
+    key = (id(offsets), kind, a, b)
+    hit = _RECORD_CACHE.get(key)
+    if hit is not None and hit[0]() is offsets and hit[1] == offsets._version:
+        return hit[2]
+    if len(_RECORD_CACHE) > 64:
+        _RECORD_CACHE.clear()
+    rec = groups_over_rows(offsets, a, b) if kind == "rows" else groups_over_contraction(offsets, a)
+    _RECORD_CACHE[key] = (weakref.ref(offsets), offsets._version, rec)
+    return rec
+
+
 class _FP4GroupedLinearFn(torch.autograd.Function):
     """``y[rows of expert g] = x[rows of g] @ W_g`` for every expert, all three GEMMs in NVFP4.
 
@@ -241,9 +260,8 @@ class _FP4GroupedLinearFn(torch.autograd.Function):
         xrow = _row_buffers(t, k, x.device)
         xcol = _col_buffers(t, k, x.device) if recipe.grad_gemms else None
         quantize_grouped_into_(x, offsets, gx, row=xrow, col=xcol, hadamard=rot)
-        y = grouped_mm(xrow, (w_fwd_packed, w_fwd_scale), groups_over_rows(offsets, n, k), n=n, k_total=k,
-                       out_rows=t, alpha_a=gx, alpha_b=w_gs, out_dtype=x.dtype,
-                       out=torch.zeros(t, n, dtype=x.dtype, device=x.device))
+        y = grouped_mm(xrow, (w_fwd_packed, w_fwd_scale), _records("rows", offsets, n, k), n=n, k_total=k,
+                       out_rows=t, alpha_a=gx, alpha_b=w_gs, out_dtype=x.dtype)
         if recipe.grad_gemms:
             ctx.save_for_backward(offsets, xcol[0], xcol[1], gx, w_dgrad_packed, w_dgrad_scale, w_gs, hadamard, seed)
         else:
@@ -268,12 +286,11 @@ class _FP4GroupedLinearFn(torch.autograd.Function):
         gcol = _col_buffers(t, n, grad_y.device)
         quantize_grouped_into_(grad_y, offsets, gg, row=grow, col=gcol, hadamard=rot,
                                stochastic=recipe.stochastic_rounding, seed=seed)
-        grad_x = grouped_mm(grow, (wdp, wds), groups_over_rows(offsets, k, n), n=k, k_total=n, out_rows=t,
-                            alpha_a=gg, alpha_b=w_gs, out_dtype=ctx.x_dtype,
-                            out=torch.zeros(t, k, dtype=ctx.x_dtype, device=grad_y.device))
+        grad_x = grouped_mm(grow, (wdp, wds), _records("rows", offsets, k, n), n=k, k_total=n, out_rows=t,
+                            alpha_a=gg, alpha_b=w_gs, out_dtype=ctx.x_dtype)
         # dW_g in (in, out) storage = X_g^T dY_g: rows of the colblock X operand (in) times rows of
         # the colblock dY operand (out), contracted over the expert's tokens.
-        grad_w = grouped_mm((xcol_p, xcol_s), gcol, groups_over_contraction(offsets, k), n=n, k_total=t,
+        grad_w = grouped_mm((xcol_p, xcol_s), gcol, _records("contraction", offsets, k, 0), n=n, k_total=t,
                             out_rows=e * k, alpha_a=gx, alpha_b=gg, out_dtype=torch.float32)
         return grad_x, None, grad_w.view(e, k, n), None, None, None, None, None, None, None, None
 
@@ -335,8 +352,8 @@ class FP4GroupedLinear(nn.Module):
 
     def forward(self, x: torch.Tensor, offsets: torch.Tensor) -> torch.Tensor:
         """``x``: ``(T, in)`` tokens sorted by expert, ``T % 128 == 0``; ``offsets``: ``(E + 1,)``
-        device row offsets (multiples of 128).  Returns ``(T, out)``; rows past ``offsets[E]`` are
-        zero."""
+        device row offsets (multiples of 128).  Returns ``(T, out)``; rows past ``offsets[E]``
+        (a worst-case allocation's tail) are left undefined, and so are their input gradients."""
         if not x.is_cuda:
             require_nvfp4("FP4GroupedLinear")
             raise RuntimeError("FP4GroupedLinear: input must be a CUDA tensor on the sm_100 device (no CPU path)")
