@@ -197,25 +197,50 @@ def run_ours(args):
     clocks = ClockSampler(phys)
     barrier()
     torch.cuda.synchronize()
+    # The step is captured once in a CUDA graph and replayed: every kernel of the step runs on every
+    # replay; the graph removes the host's per-launch overhead, which with eight processes sharing
+    # the host's cores leaves gaps between kernels.  --eager times the Python loop instead.
+    run_step = (lambda: _step(layers, xs, dys))
+    graph = None
+    if not args.eager:
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                _step(layers, xs, dys)
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            _step(layers, xs, dys)
+        torch.cuda.synchronize()
+        run_step = graph.replay
     clocks.start()
     for _ in range(20):  # keep the GPU loaded while the sampler starts up (untimed)
-        _step(layers, xs, dys)
-    with _trace.kernel_timer() as kt:
-        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        barrier()
-        torch.cuda.synchronize()
-        start.record()
-        for _ in range(args.steps):
-            _step(layers, xs, dys)
-        stop.record()
-        torch.cuda.synchronize()
-        barrier()
-        torch.cuda.synchronize()
+        run_step()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    start.record()
+    for _ in range(args.steps):
+        run_step()
+    stop.record()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
     clk = clocks.stop()
     ms = start.elapsed_time(stop)
     ms_max = max_over_ranks(ms)
-    per_kind = kt.summary()
-    launches = kt.launches
+    # Per-kernel breakdown (the roofline's live timing): the same steps again, eagerly, with CUDA
+    # events around every launch.  Not part of `value`.
+    kt_steps = max(3, min(args.steps, 50))
+    with _trace.kernel_timer() as kt:
+        for _ in range(kt_steps):
+            _step(layers, xs, dys)
+        torch.cuda.synchronize()
+    per_kind = {k: {kk: (int(round(vv * args.steps / kt_steps)) if kk == "launches" else vv * args.steps / kt_steps)
+                    for kk, vv in v.items()} for k, v in kt.summary().items()}
+    launches = kt.launches * args.steps // kt_steps
 
     # ---- with the data-parallel weight-gradient reduction (N > 1) -----------------------------
     # Token sharding needs no collective on the fwd/dgrad path, but wgrad contracts over tokens:
@@ -315,6 +340,8 @@ def run_ours(args):
                 "recipe": "grad_gemms, stochastic_rounding, hadamard, save_activations",
                 "parallelism": f"token-sharded dp{world} (no data-path collective)",
                 "l2": "inputs larger than L2 (about 1 GB of activations and gradients per step)",
+                "timing": "eager Python step loop" if args.eager else
+                          "the step captured in one CUDA graph, replayed K times (per-kernel times from an eager pass)",
             },
             "tokens_per_s": round(world * TOKENS_PER_GPU / (ms_step * 1e-3), 1),
             "gpu_launches": launches,
@@ -353,6 +380,7 @@ def run_ours(args):
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(budget_s=args.cpu_budget)
         print(json.dumps(line), flush=True)
+    del graph, run_step
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -791,6 +819,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
+    ap.add_argument("--eager", action="store_true",
+                    help="config 3: time the Python step loop instead of a captured CUDA graph of the step")
     ap.add_argument("--nsplit", choices=["fused", "nccl"], default="fused",
                     help="config 5: the N-split layer's output all-gather (fused into the GEMM, or NCCL)")
     ap.add_argument("--config", choices=["3", "4", "5"], default="3",
