@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define RB_NVFP4_ABI_VERSION 3
+#define RB_NVFP4_ABI_VERSION 4
 
 /* Input element types. */
 #define RB_DTYPE_BF16 0
@@ -99,13 +99,18 @@ int rb_nvfp4_global_scale_noalloc(const void* x, int dtype, int64_t rows, int64_
  *                every 16-row group (quantize.py:261-262).  Not applied to the rowblock form.
  *   seed       : device int64 seed for stochastic rounding (read on the device); NULL = round to
  *                nearest even.  With a seed both forms use stochastic rounding with the rule of
- *                quantize.py:122-138 (up with probability (a - lo) / (hi - lo), resolved to
- *                2^-22); each 16-element block draws from its own counter-based stream keyed by
- *                the seed and the block's index, so results depend on (seed, element position)
- *                only -- not on the launch shape -- and differ from radiance's tl.rand draws.
- *   row_packed : NULL or rows x cols/2 bytes;  row_scale: NULL or (rows/128)*(cols/64)*512 bytes.
- *   col_packed : NULL or cols x rows/2 bytes;  col_scale: NULL or ceil(cols/128)*(rows/64)*512 bytes
- *                (padding rows are written as zero).
+ *                quantize.py:122-138 (up with probability (a - lo) / (hi - lo)), resolved to
+ *                2^-16 of a grid step by the hardware convert cvt.rs.satfinite.e2m1x4.f32 (up with
+ *                probability floor(f * 2^16) / 2^16 for the fraction f).  Each 32-element unit
+ *                (rowblock: 32 columns of a row; colblock: a column pair's 16-row blocks) draws
+ *                from its own counter-based stream keyed by the seed and the unit's index, so
+ *                results depend on (seed, element position) only -- not on the launch shape --
+ *                and differ from radiance's tl.rand draws.
+ *   row_packed : NULL or rows x cols/2 bytes, 16-byte aligned;  row_scale: NULL or
+ *                (rows/128)*(cols/64)*512 bytes, 4-byte aligned.
+ *   col_packed : NULL or cols x rows/2 bytes, 16-byte aligned;  col_scale: NULL or
+ *                ceil(cols/128)*(rows/64)*512 bytes, 16-byte aligned (padding rows are written as
+ *                zero).
  * At least one of the two forms must be requested; each form needs both of its pointers.
  */
 int rb_nvfp4_quantize(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld, const float* gs,
@@ -203,6 +208,15 @@ int rb_nvfp4_gemm_grouped(const void* a_packed, const void* a_scale, int64_t a_r
  * counterpart in the reference.
  */
 int rb_nvfp4_selftest_division(const float* x, const float* d, int64_t n, uint32_t* mismatches, void* stream);
+
+/*
+ * Self-test of the quantizer's block-scale shortcut: for i < n, compares the scale byte the
+ * quantizer derives for a block amax of amax[i] (a hardware e4m3 rounding of amax / (6 gs) and one
+ * per-CTA threshold) with the exact evaluation (correctly rounded quotient, clamp, round up to
+ * e4m3), under the device fp32 global scale *gs, and counts mismatches into *mismatches (device
+ * uint32, accumulated).  Test aid; no counterpart in the reference.
+ */
+int rb_nvfp4_selftest_scale(const float* amax, int64_t n, const float* gs, uint32_t* mismatches, void* stream);
 
 #ifdef __cplusplus
 }

@@ -54,9 +54,10 @@ SIGNATURES: dict[str, tuple] = {
          _c_void_p, _int, _i64, _i64, _c_void_p],
     ),
     "rb_nvfp4_selftest_division": (_int, [_c_void_p, _c_void_p, _i64, _c_void_p, _c_void_p]),
+    "rb_nvfp4_selftest_scale": (_int, [_c_void_p, _i64, _c_void_p, _c_void_p, _c_void_p]),
 }
 
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 RB_DTYPE_BF16 = 0
 RB_DTYPE_F32 = 1

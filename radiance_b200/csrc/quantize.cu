@@ -10,12 +10,17 @@
 //
 // Design (persistent CTAs, two per SM, 256 threads each):
 //   * A 128-row x 128-byte-wide input tile (128 x 128 bf16 or 128 x 64 fp32) is brought into
-//     shared memory by TMA as two 128-byte-swizzled boxes, three tiles in flight per CTA.  The
-//     swizzle makes both walks below bank-conflict free.
-//   * The rowblock form reads each 16-element run along a row; the colblock form reads 16 rows of
-//     two adjacent columns and works on float2 pairs with Blackwell's packed f32x2 FMA path.  Its
-//     output (a transpose) is staged in shared memory and written as whole 64-byte rows and whole
-//     512-byte scale atoms.
+//     shared memory by TMA as two 128-byte-swizzled boxes, three tiles in flight per CTA.  Every
+//     address a thread reads is (a per-tile base) XOR (a constant below 128) plus a constant, so
+//     the swizzle costs eight logic ops per tile and the loads take immediate offsets; both walks
+//     below are bank-conflict free.
+//   * Rowblock form: thread t owns row t % 128 and the 64 (bf16) or 32 (fp32) columns of box
+//     t / 128: four or two 16-element blocks, one 4- or 2-byte run of its scale-atom row, and a
+//     32- or 16-byte run of its packed row.
+//   * Colblock form: warp g owns rows 16g..16g+15; a unit is two adjacent columns, whose 16-row
+//     blocks are worked as float2 pairs on Blackwell's packed f32x2 FMA path.  The output (a
+//     transpose) is staged in shared memory and written as whole 64-byte rows and whole 512-byte
+//     scale atoms.
 //   * x / D is never computed with a divide instruction.  Each block looks up D and
 //     Y = RN(1/D) in a 127-entry table (one entry per e4m3 byte, built per CTA with the IEEE
 //     reciprocal) and refines q0 = x*Y with two residual corrections r = x - q*D, q += r*Y, each a
@@ -26,16 +31,22 @@
 //     the correctly rounded quotient after the second.  It holds while the residual x - q*d is a
 //     normal number, i.e. for every quotient above ~1e-20 -- far below 0.25, the smallest quotient
 //     with a non-zero e2m1 code.  Smaller quotients only decide the sign bit of a zero code, and
-//     that sign is fixed up exactly (see underflow_mask8).  The block scale amax / (6 gs) uses the
-//     same method with a per-CTA reciprocal of 6 gs.  rb_nvfp4_selftest_division checks the
+//     that sign is fixed up exactly (see underflow_mask8).  rb_nvfp4_selftest_division checks the
 //     identity against the IEEE divide on the GPU.
+//   * The block-scale byte: byte(amax) = ceil_e4m3(clamp(RN(amax / 6gs))) is monotone in amax, so
+//     it is e + [amax >= thr[e]], where e = RN_e4m3(amax * rup) (the hardware convert, with rup a
+//     hair above 1/(6gs)) is provably the byte or the one below it, and thr[e] is the smallest
+//     amax whose byte exceeds e.  The 126 thresholds are found per CTA from the exact Markstein
+//     evaluation (scale_threshold); rb_nvfp4_selftest_scale checks the shortcut against it.
 //   * Codes come from the hardware round-to-nearest-even convert cvt.rn.satfinite.e2m1x2.f32,
 //     which rounds exactly like the reference's comparison ladder (ties to the even code).
+//     Stochastic rounding uses the hardware convert cvt.rs.satfinite.e2m1x4.f32 with 16 random
+//     bits per element (see sr_rbits).
 //   * The Hadamard fast path: radiance's rotation is a Sylvester matrix with row signs, scaled by
 //     1/4 (quantize.py:647-659).  Then y_i = 1/4 * sum_j syl(j,i) * (s_j x_j) with the same
 //     left-to-right rounding, since scaling by a power of two commutes with every rounding; the
-//     kernel sums the sign-flipped inputs with packed adds and folds the 1/4 into the divisor.
-//     Any other 16x16 matrix takes a general path (multiply then add, j = 0..15).
+//     kernel flips the input signs while unpacking, sums with packed adds and folds the 1/4 into
+//     the divisor.  Any other 16x16 matrix takes a general path (multiply then add, j = 0..15).
 #include <stdio.h>
 
 #include "common.cuh"
@@ -68,11 +79,6 @@ struct QuantArgs {
   uint8_t* col_scale;
   int tiles_k;
   int n_tiles;
-  // Powers of two handed to the kernel at run time (the host sets p2 = 2, p22 = 2^22,
-  // p25 = 2^25).  Part of the stochastic-rounding arithmetic is written as multiply-high /
-  // multiply-add by them (x >> s == umulhi(x, 2^(32-s))) so that it runs on the FMA pipe beside
-  // the integer/logic pipe; literal constants would be strength-reduced back into shifts.
-  uint32_t p2, p22, p25;
   // Grouped mode (offs != nullptr): gs[g] is the global scale of rows [offs[g], offs[g+1]); each
   // 128-row tile takes the group of its first row.
   const int64_t* offs;
@@ -93,8 +99,9 @@ __device__ __forceinline__ int group_of_row(const int64_t* offs, int ngroups, in
 struct QHeader {
   uint64_t full[kQStages];
   float2 table[128];  // (D, RN(1/D)) for each e4m3 byte; entry 127 unused
+  float thr[128];     // thr[e]: the smallest block amax whose scale byte exceeds e (NaN: none)
   float had[256];
-  uint32_t sign_mask[16];
+  uint32_t sign_word[16];
   int had_fast;
   alignas(16) uint8_t stage_pk[8 * 1024];  // colblock codes: 8 warps x 128 rows x 8 bytes
   alignas(16) uint8_t stage_sc[2 * 512];   // colblock scales: the tile's two SWIZZLE_32_4_4 atoms
@@ -126,9 +133,9 @@ __device__ __forceinline__ uint32_t e4m3_ceil_byte(float s) {
   return s >= 0.015625f ? nb : sb;
 }
 
-// Block-scale byte for a block amax: smallest e4m3 >= clamp(RN(amax / denom), 1e-12, 448).  The
-// quotient is Markstein's (rd = RN(1/denom), nd = -denom); a quotient above 512 saturates to 448
-// directly, since the corrections would overflow there.
+// Block-scale byte for a block amax, evaluated exactly: smallest e4m3 >= clamp(RN(amax / denom),
+// 1e-12, 448).  The quotient is Markstein's (rd = RN(1/denom), nd = -denom); a quotient above 512
+// saturates to 448 directly, since the corrections would overflow there.
 __device__ __forceinline__ uint32_t block_scale_byte(float amax, float nd, float rd) {
   const float q0 = amax * rd;
   float q = q0;
@@ -138,6 +145,72 @@ __device__ __forceinline__ uint32_t block_scale_byte(float amax, float nd, float
   q = fmaf(r, rd, q);
   q = (q0 > 512.0f) ? 448.0f : fminf(fmaxf(q, 1e-12f), 448.0f);
   return e4m3_ceil_byte(q);
+}
+
+// The smallest non-negative float amax with block_scale_byte(amax) >= target (1 <= target <= 126).
+// The byte is monotone in amax (a composition of monotone roundings); the search starts next to
+// the boundary, value(target - 1) * denom, and falls back to bisection over the bit patterns of
+// the non-negative floats (which order like the floats).
+__device__ float scale_threshold(uint32_t target, float nd, float rd) {
+  if (target <= 1) return 0.0f;  // every block's byte is at least 1 (the 1e-12 clamp)
+  uint32_t a = __float_as_uint(__fmul_rn(e4m3_value(target - 1), -nd));
+  if (a > 0x7F800000u) a = 0x7F800000u;
+  int steps = 0;
+  if (block_scale_byte(__uint_as_float(a), nd, rd) >= target) {
+    while (a > 0 && steps < 16 && block_scale_byte(__uint_as_float(a - 1), nd, rd) >= target) --a, ++steps;
+  } else {
+    while (steps < 16 && block_scale_byte(__uint_as_float(a), nd, rd) < target) ++a, ++steps;
+  }
+  if (steps < 16) return __uint_as_float(a);
+  uint32_t lo = 0, hi = 0x7F800000u;  // byte(+inf) = 126 >= target
+  while (lo < hi) {
+    const uint32_t mid = lo + ((hi - lo) >> 1);
+    if (block_scale_byte(__uint_as_float(mid), nd, rd) >= target) hi = mid;
+    else lo = mid + 1;
+  }
+  return __uint_as_float(lo);
+}
+
+// e4m3 bytes of RN(hi) (bits 8..15) and RN(lo) (bits 0..7), saturating to 448.
+__device__ __forceinline__ uint32_t e4m3x2_rn(float hi, float lo) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ uint2 lds64(uint32_t addr) {
+  uint2 v;
+  asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+__device__ __forceinline__ void sts8(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared.b8 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+
+// Scale bytes of two blocks from their amaxes: e = RN_e4m3(amax * rup) is the exact byte or the
+// one below it, and thr[e] decides.  (rup >= (1 + 2^-21) / (6gs) puts amax * rup above the exact
+// quotient s; it stays below s (1 + 2^-19), far short of the next e4m3 rounding boundary above
+// ceil_e4m3(s), so RN_e4m3 lands on ceil_e4m3(s) or the value below.  The clamps agree: e = 0
+// below 1e-12 where the byte is 1 = e + [amax >= thr[0] = 0], and e = 126 = byte at saturation,
+// where thr[126] is NaN.)
+__device__ __forceinline__ void scale_bytes2(float a0, float a1, float rup, uint32_t thr, uint32_t& b0, uint32_t& b1) {
+  const uint32_t e = e4m3x2_rn(a1 * rup, a0 * rup);
+  const uint32_t e0 = e & 0xFFu, e1 = e >> 8;
+  b0 = e0 + (a0 >= __uint_as_float(lds32(thr + 4 * e0)) ? 1u : 0u);
+  b1 = e1 + (a1 >= __uint_as_float(lds32(thr + 4 * e1)) ? 1u : 0u);
 }
 
 // q = RN(x / d) for a float2, given nd = -d and y = RN(1/d) (Markstein, two corrections).
@@ -164,9 +237,29 @@ __device__ __forceinline__ uint32_t e2m1x8(float e0, float e1, float e2, float e
   return out;
 }
 
-// Random bits for stochastic rounding: a two-round xor-shift / multiply mixer applied to
-// (element index ^ key) -- the "lowbias32" finalizer from C. Wellons' hash-prospector search
-// (public domain constants), a bijection on 32-bit words with full avalanche.
+// Stochastic rounding of four quotients to e2m1 by the hardware convert: element i lands in
+// nibble i.  The convert rounds a magnitude up with probability floor(f * 2^16) / 2^16, f the
+// fraction of the grid step above the level below (quantize.py:122-138 rounds up with probability
+// f), using 16 random bits per element drawn from `rbits`: with R0 = rbits[23:16]:rbits[7:0] and
+// R2 = rbits[31:24]:rbits[15:8], element 0 takes R0, element 1 the bit reversal of R0, element 2
+// R2 and element 3 the bit reversal of R2, and rounds up when floor(f * 2^16) + R >= 2^16.
+__device__ __forceinline__ uint32_t e2m1x4_rs(float e0, float e1, float e2, float e3, uint32_t rbits) {
+  uint16_t d;
+  asm("cvt.rs.satfinite.e2m1x4.f32 %0, {%1, %2, %3, %4}, %5;"
+      : "=h"(d)
+      : "f"(e3), "f"(e2), "f"(e1), "f"(e0), "r"(rbits));
+  return d;
+}
+
+// Random bits for stochastic rounding.  A unit of 32 elements (rowblock: one row's 32-column
+// group; colblock: two adjacent columns' 16-row blocks) draws from its own stream:
+//   S    = mix32(lo32(unit) ^ key(hi32(unit)))   (mix32: the "lowbias32" finalizer from
+//          C. Wellons' hash-prospector search, public-domain constants; a bijection with full
+//          avalanche)
+//   r_j  = A^j S + C_j mod 2^32 (j = 0..15; a full-period LCG with the multiplier and increment of
+//          PCG's 32-bit generator), each one multiply-add from S
+//   rbits of convert c (elements 4c..4c+3 of the unit) = hi16(r_2c) | hi16(r_2c+1) << 16
+// so every convert draws only the upper halves of two LCG words.
 __device__ __forceinline__ uint32_t mix32(uint32_t x) {
   x ^= x >> 16;
   x *= 0x7FEB352Du;
@@ -182,18 +275,12 @@ __device__ __forceinline__ uint32_t sr_key(const int64_t* seed) {
   return mix32((uint32_t)s ^ 0x9E3779B9u) ^ mix32((uint32_t)(s >> 32) + 0x7F4A7C15u);
 }
 
-// Key for indices sharing the same upper 32 bits.
+// Key for unit indices sharing the same upper 32 bits.
 __device__ __forceinline__ uint32_t sr_key_hi(uint32_t key, uint64_t idx) {
   const uint32_t hi = (uint32_t)(idx >> 32);
   return hi ? key ^ mix32(hi + 0x632BE5ABu) : key;
 }
 
-// Random words of one 16-element block: s_0 = mix32(block index ^ key), then the block's draws
-// follow a full-period 32-bit LCG (multiplier and increment of PCG's 32-bit generator),
-// r_j = A^j s_0 + C_j, each one multiply-add from s_0 (no dependency chain).  The rowblock form
-// numbers its blocks row-major, (row * K + col) / 16, with the launch key; the colblock form
-// numbers them by output row, col * (M / 16) + row / 16, with a second key.  Draw j goes to
-// element j of the block (column offset in the rowblock form, row offset in the colblock form).
 constexpr uint32_t kLcgA = 747796405u, kLcgC = 2891336453u;
 __host__ __device__ constexpr uint32_t lcg_mul(int j) {
   uint32_t a = 1u;
@@ -205,37 +292,11 @@ __host__ __device__ constexpr uint32_t lcg_add(int j) {
   for (int i = 0; i < j; ++i) c = c * kLcgA + kLcgC;
   return c;
 }
-__device__ __forceinline__ uint32_t sr_block_seed(uint64_t blk, uint32_t key) {
-  return mix32((uint32_t)blk ^ sr_key_hi(key, blk));
+__device__ __forceinline__ uint32_t sr_unit_seed(uint64_t unit, uint32_t key) {
+  return mix32((uint32_t)unit ^ sr_key_hi(key, unit));
 }
-
-// Stochastic rounding of a quotient q (= RN(x / D)) to a signed e2m1 code, with 32 random bits r
-// (rule of quantize.py:122-138: lo = the grid level at or below a = min(|q|, 6), round up with
-// probability (a - lo) / (hi - lo)).  On [1, 8) the e2m1 grid keeps one fp32 mantissa bit, so the
-// 22 bits below it hold the fraction (a - lo) / (hi - lo) in units of 2^-22: adding 22 uniform
-// random bits carries into the kept bit exactly with that probability, and the carry moves the
-// value to the next level (into the exponent where the level is a power of two).  [0, 1) is
-// shifted to [1, 2), where the grid step (0.5) is the same, and the code shifted back by 2.
-//
-// The kernels evaluate the same rule on q4 = 4q (their SR divisor is D / 4, an exact scaling of
-// the same quotient): t4 = min(max(m4, m4/2 + 2), 24) with m4 = |q4| is 4 max(a, (a+1)/2) -- the
-// [0, 1) range mapped onto [0.5, 1), one binade below a + 1, so every magnitude shares one offset
-// -- and bits(4t) = bits(t) + (4 << 22).  The code, sign included, is then bits 22..25 of
-// bits(t4) + (r >> 10) + sign(q) << 25: exponent-and-kept-bit 256..263 (t = 0.5 .. 6) is codes
-// 0..7 modulo 16, the carry never reaches bit 25 (t4 = 24 has no fraction bits), and bit 25 is
-// the sign.  The sign is the quotient's sign bit: the Markstein quotient of +-0 is +0, so it
-// equals the reference's q < 0 wherever the quotient is not an underflowed zero (those nibbles
-// are cleared by underflow_mask8).  Returns the nibble in place: bits 22..25 moved to 4e..4e+3
-// (e is a constant after unrolling, so the move is one shift).
-__device__ __forceinline__ uint32_t sr_nibble_at(float q4, uint32_t r, const QuantArgs& a, int e) {
-  const float m = fabsf(q4);
-  const float t = fminf(fmaxf(m, fmaf(m, 0.5f, 2.0f)), 24.0f);
-  const uint32_t sgn = __umulhi(__float_as_uint(q4), a.p2);         // sign bit
-  const uint32_t u = sgn * a.p25 + __float_as_uint(t);
-  const uint32_t b = __umulhi(r, a.p22) + u;                        // + (r >> 10)
-  const int sh = 22 - 4 * e;
-  const uint32_t moved = sh >= 0 ? (b >> sh) : (b << -sh);
-  return moved & (0xFu << (4 * e));
+__device__ __forceinline__ uint32_t sr_rbits(uint32_t s, int c) {
+  return __byte_perm(s * lcg_mul(2 * c) + lcg_add(2 * c), s * lcg_mul(2 * c + 1) + lcg_add(2 * c + 1), 0x7632);
 }
 
 // A quotient that rounds to +-0 must produce nibble 0 (the reference's sign is `q < 0`, false for
@@ -251,31 +312,6 @@ __device__ __forceinline__ uint32_t underflow_mask8(const float* v, int stride, 
   return keep;
 }
 
-// ---------------------------------------------------------------------------------------------
-// Shared-memory access
-// ---------------------------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
-  uint32_t v;
-  asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
-  return v;
-}
-__device__ __forceinline__ uint2 lds64(uint32_t addr) {
-  uint2 v;
-  asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
-  return v;
-}
-__device__ __forceinline__ uint4 lds128(uint32_t addr) {
-  uint4 v;
-  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
-  return v;
-}
-__device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
-}
-__device__ __forceinline__ void sts8(uint32_t addr, uint32_t v) {
-  asm volatile("st.shared.b8 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
-}
-
 __device__ __forceinline__ float2 bf16x2_to_float2(uint32_t w) {
   return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
 }
@@ -288,175 +324,177 @@ __device__ __forceinline__ void st_global_v4(void* p, uint32_t a, uint32_t b, ui
 }
 
 struct QCtx {
-  const QHeader* hdr;
-  float nden, rden;  // -(6 gs) and RN(1/(6 gs))
+  uint32_t tab;      // shared address of QHeader::table
+  uint32_t thr;      // shared address of QHeader::thr
+  uint32_t had;      // shared address of QHeader::had
+  float rup;         // RN(1/(6 gs)) (1 + 2^-20)
   uint32_t key;      // stochastic rounding: rowblock-form key
   uint32_t key_col;  // colblock-form key
 };
 
-// ---------------------------------------------------------------------------------------------
-// The rowblock form of one 16-element block: returns its two packed words and its scale byte.
-// ---------------------------------------------------------------------------------------------
-template <bool SR>
-__device__ __forceinline__ uint32_t row_block(const float2 (&v)[8], const QCtx& c, const QuantArgs& a, uint64_t lin0,
-                                              uint32_t& w0, uint32_t& w1, bool f32in) {
-  float amax = 0.0f;
-#pragma unroll
-  for (int e = 0; e < 8; ++e) amax = fmax3(amax, fabsf(v[e].x), fabsf(v[e].y));
-  const uint32_t sbyte = block_scale_byte(amax, c.nden, c.rden);
-  const float2 dy = c.hdr->table[sbyte];
-  const float2 nd = make_float2(-dy.x, -dy.x), yy = make_float2(dy.y, dy.y);
-  if constexpr (SR) {
-    const uint32_t s0 = sr_block_seed(lin0 >> 4, c.key);
-    const float2 nd4 = make_float2(0.25f * nd.x, 0.25f * nd.y), y4 = make_float2(4.0f * yy.x, 4.0f * yy.y);
-    w0 = w1 = 0;
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const float2 q = div2(v[e], nd4, y4);  // 4 * (x / D)
-      const uint32_t rx = s0 * lcg_mul(2 * e) + lcg_add(2 * e);
-      const uint32_t ry = s0 * lcg_mul(2 * e + 1) + lcg_add(2 * e + 1);
-      if (e < 4) {
-        w0 |= sr_nibble_at(q.x, rx, a, 2 * e) | sr_nibble_at(q.y, ry, a, 2 * e + 1);
-      } else {
-        w1 |= sr_nibble_at(q.x, rx, a, 2 * e - 8) | sr_nibble_at(q.y, ry, a, 2 * e - 7);
-      }
-    }
-  } else {
-    float2 q[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) q[e] = div2(v[e], nd, yy);
-    w0 = e2m1x8(q[0].x, q[0].y, q[1].x, q[1].y, q[2].x, q[2].y, q[3].x, q[3].y);
-    w1 = e2m1x8(q[4].x, q[4].y, q[5].x, q[5].y, q[6].x, q[6].y, q[7].x, q[7].y);
+// Divisor/reciprocal table and scale thresholds for one global scale (threads 0..127).
+__device__ __forceinline__ void build_tables(QHeader* hdr, float gs, QCtx& c) {
+  const int tid = threadIdx.x;
+  const float den = __fmul_rn(6.0f, gs);
+  const float rd = __frcp_rn(den);
+  c.rup = rd * 1.00000095367431640625f;  // 1 + 2^-20
+  if (tid < 127) {
+    const float d = __fmul_rn(e4m3_value(tid), gs);
+    hdr->table[tid] = make_float2(d, __frcp_rn(d));
   }
-  if (dy.x >= (f32in ? 1.0f : 65536.0f)) {
-    w0 &= underflow_mask8(&v[0].x, 1, dy.x);
-    w1 &= underflow_mask8(&v[4].x, 1, dy.x);
-  }
-  return sbyte;
+  if (tid < 128) hdr->thr[tid] = tid < 126 ? scale_threshold(tid + 1, -den, rd) : __uint_as_float(0x7FFFFFFFu);
 }
 
-// Rowblock form of a tile.  bf16: thread (warp w, lane l) takes block l % 8 of rows
-// 16w + 4p + l/8 (p = 0..3); fp32: block l % 4 of rows 16w + 8p + l/4 (p = 0, 1).  Two blocks are
-// processed together for instruction-level parallelism.
+// ---------------------------------------------------------------------------------------------
+// Rowblock form of a tile: thread t owns row t % 128 of box t / 128.  `rk[c]` is the shared
+// address of 16-byte chunk c of that box row.
+// ---------------------------------------------------------------------------------------------
 template <bool F32IN, bool SR>
-__device__ __forceinline__ void row_tile(uint32_t tile, const QCtx& c, const QuantArgs& a, int64_t m0, int64_t k0,
-                                         int mt, int kt, int valid_cols) {
-  constexpr int kBlocksPerRow = F32IN ? 4 : 8;
-  constexpr int kRowsPerPass = 32 / kBlocksPerRow;
-  constexpr int kPasses = 16 / kRowsPerPass;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int b = lane % kBlocksPerRow;
-  const bool valid = 16 * b < valid_cols;
-#pragma unroll 1
-  for (int pp = 0; pp < kPasses; pp += 2) {
-    float2 v[2][8];
-    int rr[2];
+__device__ __forceinline__ void row_part(const uint32_t (&rk)[8], const QCtx& c, const QuantArgs& a, int64_t m0,
+                                         int64_t k0, int mt, bool valid) {
+  constexpr int kUnits = F32IN ? 1 : 2;  // 32-column stochastic-rounding units per thread
+  const int r = threadIdx.x & 127, h = threadIdx.x >> 7;
+  const int64_t col0 = k0 + (F32IN ? 32 : 64) * h;
+  uint32_t w[kUnits][4];
+  uint32_t sb[kUnits][2];
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const int r = 16 * warp + kRowsPerPass * (pp + u) + lane / kBlocksPerRow;
-      rr[u] = r;
+  for (int u = 0; u < kUnits; ++u) {
+    float2 v[2][8];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
       if constexpr (!F32IN) {
-        const uint32_t row = tile + (b >> 2) * kQBoxBytes + r * 128;
-        const uint4 c0 = lds128(row + (((2 * (b & 3)) ^ (r & 7)) << 4));
-        const uint4 c1 = lds128(row + (((2 * (b & 3) + 1) ^ (r & 7)) << 4));
-        v[u][0] = bf16x2_to_float2(c0.x); v[u][1] = bf16x2_to_float2(c0.y);
-        v[u][2] = bf16x2_to_float2(c0.z); v[u][3] = bf16x2_to_float2(c0.w);
-        v[u][4] = bf16x2_to_float2(c1.x); v[u][5] = bf16x2_to_float2(c1.y);
-        v[u][6] = bf16x2_to_float2(c1.z); v[u][7] = bf16x2_to_float2(c1.w);
+        const uint4 c0 = lds128(rk[4 * u + 2 * i]), c1 = lds128(rk[4 * u + 2 * i + 1]);
+        v[i][0] = bf16x2_to_float2(c0.x); v[i][1] = bf16x2_to_float2(c0.y);
+        v[i][2] = bf16x2_to_float2(c0.z); v[i][3] = bf16x2_to_float2(c0.w);
+        v[i][4] = bf16x2_to_float2(c1.x); v[i][5] = bf16x2_to_float2(c1.y);
+        v[i][6] = bf16x2_to_float2(c1.z); v[i][7] = bf16x2_to_float2(c1.w);
       } else {
-        const uint32_t row = tile + (b >> 1) * kQBoxBytes + r * 128;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          const uint4 w = lds128(row + ((((b & 1) * 4 + q) ^ (r & 7)) << 4));
-          v[u][2 * q] = make_float2(__uint_as_float(w.x), __uint_as_float(w.y));
-          v[u][2 * q + 1] = make_float2(__uint_as_float(w.z), __uint_as_float(w.w));
+          const uint4 x = lds128(rk[4 * i + q]);
+          v[i][2 * q] = make_float2(__uint_as_float(x.x), __uint_as_float(x.y));
+          v[i][2 * q + 1] = make_float2(__uint_as_float(x.z), __uint_as_float(x.w));
         }
       }
     }
+    float am[2];
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const int r = rr[u];
-      const uint64_t lin0 = (uint64_t)(m0 + r) * (uint64_t)a.K + (uint64_t)(k0 + 16 * b);
-      uint32_t w0, w1;
-      const uint32_t sbyte = row_block<SR>(v[u], c, a, lin0, w0, w1, F32IN);
-      if (valid) st_global_v2(a.row_packed + (m0 + r) * (a.K >> 1) + (k0 >> 1) + 8 * b, w0, w1);
-      // Gather the four scale bytes of an atom column group (lanes l..l+3) into one store.
-      uint32_t s4 = sbyte;
-      s4 |= __shfl_down_sync(0xFFFFFFFFu, sbyte, 1) << 8;
-      s4 |= __shfl_down_sync(0xFFFFFFFFu, sbyte, 2) << 16;
-      s4 |= __shfl_down_sync(0xFFFFFFFFu, sbyte, 3) << 24;
-      if ((b & 3) == 0 && valid) {
-        uint8_t* atom = a.row_scale + ((int64_t)mt * (a.K >> 6) + (k0 >> 6) + (b >> 2)) * 512;
-        *reinterpret_cast<uint32_t*>(atom + (r & 31) * 16 + (r >> 5) * 4) = s4;
+    for (int i = 0; i < 2; ++i) {
+      float m = 0.0f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) m = fmax3(m, fabsf(v[i][e].x), fabsf(v[i][e].y));
+      am[i] = m;
+    }
+    scale_bytes2(am[0], am[1], c.rup, c.thr, sb[u][0], sb[u][1]);
+    uint32_t seed = 0;
+    if constexpr (SR) seed = sr_unit_seed((uint64_t)(m0 + r) * (uint64_t)(a.K >> 5) + (uint64_t)(col0 >> 5) + u, c.key);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const uint2 t = lds64(c.tab + 8 * sb[u][i]);
+      const float d = __uint_as_float(t.x), y = __uint_as_float(t.y);
+      const float2 nd = make_float2(-d, -d), yy = make_float2(y, y);
+      float2 q[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) q[e] = div2(v[i][e], nd, yy);
+      if constexpr (SR) {
+        const uint32_t h0 = e2m1x4_rs(q[0].x, q[0].y, q[1].x, q[1].y, sr_rbits(seed, 4 * i));
+        const uint32_t h1 = e2m1x4_rs(q[2].x, q[2].y, q[3].x, q[3].y, sr_rbits(seed, 4 * i + 1));
+        const uint32_t h2 = e2m1x4_rs(q[4].x, q[4].y, q[5].x, q[5].y, sr_rbits(seed, 4 * i + 2));
+        const uint32_t h3 = e2m1x4_rs(q[6].x, q[6].y, q[7].x, q[7].y, sr_rbits(seed, 4 * i + 3));
+        w[u][2 * i] = __byte_perm(h0, h1, 0x5410);
+        w[u][2 * i + 1] = __byte_perm(h2, h3, 0x5410);
+      } else {
+        w[u][2 * i] = e2m1x8(q[0].x, q[0].y, q[1].x, q[1].y, q[2].x, q[2].y, q[3].x, q[3].y);
+        w[u][2 * i + 1] = e2m1x8(q[4].x, q[4].y, q[5].x, q[5].y, q[6].x, q[6].y, q[7].x, q[7].y);
+      }
+      const float risk = F32IN ? 1.0f : 65536.0f;  // smallest |x|: 2^-149 (fp32), 2^-133 (bf16)
+      if (__any_sync(0xFFFFFFFFu, d >= risk) && d >= risk) {
+        w[u][2 * i] &= underflow_mask8(&v[i][0].x, 1, d);
+        w[u][2 * i + 1] &= underflow_mask8(&v[i][4].x, 1, d);
       }
     }
+  }
+  if (!valid) return;
+  uint8_t* prow = a.row_packed + (m0 + r) * (a.K >> 1) + (col0 >> 1);
+  st_global_v4(prow, w[0][0], w[0][1], w[0][2], w[0][3]);
+  if constexpr (!F32IN) st_global_v4(prow + 16, w[1][0], w[1][1], w[1][2], w[1][3]);
+  // Scale bytes: atom (mt, col0 / 64), 16-byte row r % 32, 4-byte group r / 32, byte (col0 % 64) / 16.
+  uint8_t* atom = a.row_scale + ((int64_t)mt * (a.K >> 6) + (col0 >> 6)) * 512 + (r & 31) * 16 + (r >> 5) * 4;
+  if constexpr (!F32IN) {
+    *reinterpret_cast<uint32_t*>(atom) = sb[0][0] | (sb[0][1] << 8) | (sb[1][0] << 16) | (sb[1][1] << 24);
+  } else {
+    *reinterpret_cast<uint16_t*>(atom + ((col0 & 32) ? 2 : 0)) = (uint16_t)(sb[0][0] | (sb[0][1] << 8));
   }
 }
 
 // ---------------------------------------------------------------------------------------------
-// The colblock form: warp g handles rows 16g..16g+15; each unit is two adjacent columns.  Its two
+// The colblock form: warp g handles rows 16g..16g+15; each unit is two adjacent columns.  `bk[k]`
+// is (the unit's base address) ^ (k << 4): row j of the unit is at bk[j % 8] + j * 128.  Its two
 // 8-byte packed runs go to warp g's staging region (rows permuted by `row ^ 4g`, so both the
 // write and the row-wise read-back are conflict-free) and its two scale bytes into the staged
-// SWIZZLE_32_4_4 atoms.
+// SWIZZLE_32_4_4 atoms.  HADM: 0 no rotation, 1 the Sylvester fast path (`sgn[j]` = 0 or
+// 0x80000000, the sign of row j of the matrix), 2 any other matrix.
 // ---------------------------------------------------------------------------------------------
-template <bool F32IN, bool HAD, bool SR>
-__device__ __forceinline__ void col_unit(uint32_t tile, const QCtx& c, const QuantArgs& a, int64_t m0, int64_t k0,
-                                         int cp, bool valid, uint32_t stage_pk, uint32_t stage_sc) {
-  const QHeader* hdr = c.hdr;
+template <bool F32IN, int HADM, bool SR>
+__device__ __forceinline__ void col_unit(const uint32_t (&bk)[8], uint32_t box_off, const uint32_t (&sgn)[16],
+                                         const QCtx& c, const QuantArgs& a, int64_t m0, int64_t k0, int cp,
+                                         bool valid, uint32_t stage_pk, uint32_t stage_sc) {
   const int g = threadIdx.x >> 5;
   float2 v[16];
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
-    const int r = 16 * g + j;
-    uint32_t sm = 0;
-    if constexpr (HAD) sm = hdr->had_fast ? hdr->sign_mask[j] : 0u;
+    const uint32_t addr = bk[j & 7] + box_off + j * 128;
     if constexpr (!F32IN) {
-      const int cpl = cp & 31;  // pair within its 64-column box
-      const uint32_t w = lds32(tile + (cp >> 5) * kQBoxBytes + r * 128 + ((((cpl >> 2) ^ (j & 7)) << 4) | ((cpl & 3) << 2)));
-      v[j] = bf16x2_to_float2(w ^ (sm & 0x80008000u));
+      const uint32_t w = lds32(addr);
+      if constexpr (HADM == 1) {
+        // Flipping the sign bit is adding 2^31: low half (w << 16) + s, high half (w & ~0xFFFF) ^ s.
+        v[j] = make_float2(__uint_as_float(w * 65536u + sgn[j]), __uint_as_float((w & 0xFFFF0000u) ^ sgn[j]));
+      } else {
+        v[j] = bf16x2_to_float2(w);
+      }
     } else {
-      const int cpp = cp & 15;  // pair within its 32-column box
-      const uint2 w =
-          lds64(tile + (cp >> 4) * kQBoxBytes + r * 128 + ((((cpp >> 1) ^ (j & 7)) << 4) | ((cpp & 1) << 3)));
-      v[j] = make_float2(__uint_as_float(w.x ^ (sm & 0x80000000u)), __uint_as_float(w.y ^ (sm & 0x80000000u)));
+      const uint2 w = lds64(addr);
+      if constexpr (HADM == 1) v[j] = make_float2(__uint_as_float(w.x ^ sgn[j]), __uint_as_float(w.y ^ sgn[j]));
+      else v[j] = make_float2(__uint_as_float(w.x), __uint_as_float(w.y));
     }
   }
-  float scale_fold = 1.0f;  // divisor multiplier: 4 on the Hadamard fast path (y = acc / 4)
-  if constexpr (HAD) {
+  float fold = 1.0f;  // the rotated values are fold * y (4 on the Hadamard fast path)
+  if constexpr (HADM == 1) {
+    // y_i = sum_j syl(j, i) v_j, summed left to right.  syl(j, i) = (-1)^popc(i & j), so after
+    // term j the partial sum of output i depends only on i mod w (w = the power of two above j):
+    // outputs that agree there share it.  The prefixes double at j = 1, 2, 4, 8 -- 170 adds for
+    // the 16 outputs instead of 240, each output's additions unchanged and in the same order.
     float2 y[16];
-    if (hdr->had_fast) {
-      // y_i = sum_j syl(j, i) v_j, summed left to right.  syl(j, i) = (-1)^popc(i & j), so after
-      // term j the partial sum of output i depends only on i mod w (w = the power of two above j):
-      // outputs that agree there share it.  The prefixes double at j = 1, 2, 4, 8 -- 170 adds for
-      // the 16 outputs instead of 240, each output's additions unchanged and in the same order.
-      const float2 pos = make_float2(1.0f, 1.0f), neg = make_float2(-1.0f, -1.0f);
-      y[0] = v[0];
-      int w = 1;
+    const float2 pos = make_float2(1.0f, 1.0f), neg = make_float2(-1.0f, -1.0f);
+    y[0] = v[0];
+    int w = 1;
+#pragma unroll
+    for (int j = 1; j < 16; ++j) {
+      const bool grow = (j & (j - 1)) == 0;
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        if (grow && i >= w && i < 2 * w) y[i] = __ffma2_rn(v[j], (__popc(i & j) & 1) ? neg : pos, y[i - w]);
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        if (i < w) y[i] = __ffma2_rn(v[j], (__popc(i & j) & 1) ? neg : pos, y[i]);
+      if (grow) w *= 2;
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = y[i];
+    fold = 4.0f;
+  } else if constexpr (HADM == 2) {
+    float2 y[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      float h = __uint_as_float(lds32(c.had + 4 * i));
+      float2 acc = make_float2(__fmul_rn(h, v[0].x), __fmul_rn(h, v[0].y));
 #pragma unroll
       for (int j = 1; j < 16; ++j) {
-        const bool grow = (j & (j - 1)) == 0;
-#pragma unroll
-        for (int i = 0; i < 16; ++i)
-          if (grow && i >= w && i < 2 * w) y[i] = __ffma2_rn(v[j], (__popc(i & j) & 1) ? neg : pos, y[i - w]);
-#pragma unroll
-        for (int i = 0; i < 16; ++i)
-          if (i < w) y[i] = __ffma2_rn(v[j], (__popc(i & j) & 1) ? neg : pos, y[i]);
-        if (grow) w *= 2;
+        h = __uint_as_float(lds32(c.had + 4 * (j * 16 + i)));
+        acc.x = __fadd_rn(acc.x, __fmul_rn(h, v[j].x));
+        acc.y = __fadd_rn(acc.y, __fmul_rn(h, v[j].y));
       }
-      scale_fold = 4.0f;
-    } else {
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        float h = hdr->had[i];
-        float2 acc = make_float2(__fmul_rn(h, v[0].x), __fmul_rn(h, v[0].y));
-#pragma unroll
-        for (int j = 1; j < 16; ++j) {
-          h = hdr->had[j * 16 + i];
-          acc.x = __fadd_rn(acc.x, __fmul_rn(h, v[j].x));
-          acc.y = __fadd_rn(acc.y, __fmul_rn(h, v[j].y));
-        }
-        y[i] = acc;
-      }
+      y[i] = acc;
     }
 #pragma unroll
     for (int i = 0; i < 16; ++i) v[i] = y[i];
@@ -467,51 +505,47 @@ __device__ __forceinline__ void col_unit(uint32_t tile, const QCtx& c, const Qua
     ax = fmax3(ax, fabsf(v[i].x), fabsf(v[i + 1].x));
     ay = fmax3(ay, fabsf(v[i].y), fabsf(v[i + 1].y));
   }
-  const float unfold = 1.0f / scale_fold;  // exact (1 or 1/4)
-  const uint32_t bx = block_scale_byte(ax * unfold, c.nden, c.rden);
-  const uint32_t by = block_scale_byte(ay * unfold, c.nden, c.rden);
-  const float2 tx = hdr->table[bx], ty = hdr->table[by];
-  const float dx = tx.x * scale_fold, dyv = ty.x * scale_fold;
-  const float2 nd = make_float2(-dx, -dyv), yy = make_float2(tx.y * unfold, ty.y * unfold);
+  const float unfold = 1.0f / fold;  // exact (1 or 1/4)
+  uint32_t bx, by;
+  scale_bytes2(ax * unfold, ay * unfold, c.rup, c.thr, bx, by);
+  const uint2 tx = lds64(c.tab + 8 * bx), ty = lds64(c.tab + 8 * by);
+  const float dx = __uint_as_float(tx.x) * fold, dyv = __uint_as_float(ty.x) * fold;
+  const float2 nd = make_float2(-dx, -dyv);
+  const float2 yy = make_float2(__uint_as_float(tx.y) * unfold, __uint_as_float(ty.y) * unfold);
+  float2 q[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) q[i] = div2(v[i], nd, yy);
   uint32_t wx0, wx1, wy0, wy1;
   if constexpr (SR) {
-    // Blocks of output rows 2cp and 2cp + 1 (input columns k0 + 2cp, + 1), 16-row group m0/16 + g.
-    const uint64_t mb = (uint64_t)(a.M >> 4);
-    const uint64_t bx = (uint64_t)(k0 + 2 * cp) * mb + (uint64_t)(m0 >> 4) + (uint64_t)g;
-    const uint32_t sx = sr_block_seed(bx, c.key_col), sy = sr_block_seed(bx + mb, c.key_col);
-    const float2 nd4 = make_float2(0.25f * nd.x, 0.25f * nd.y), y4 = make_float2(4.0f * yy.x, 4.0f * yy.y);
-    wx0 = wx1 = wy0 = wy1 = 0;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const float2 q = div2(v[i], nd4, y4);
-      const uint32_t cx = sr_nibble_at(q.x, sx * lcg_mul(i) + lcg_add(i), a, i & 7);
-      const uint32_t cy = sr_nibble_at(q.y, sy * lcg_mul(i) + lcg_add(i), a, i & 7);
-      if (i < 8) {
-        wx0 |= cx;
-        wy0 |= cy;
-      } else {
-        wx1 |= cx;
-        wy1 |= cy;
-      }
-    }
+    // Unit: column pair k0/2 + cp, 16-row group m0/16 + g; converts 0..3 take column 2cp's rows
+    // 4c..4c+3, converts 4..7 column 2cp + 1's.
+    const uint64_t unit = ((uint64_t)(k0 >> 1) + (uint64_t)cp) * (uint64_t)(a.M >> 4) + (uint64_t)(m0 >> 4) + g;
+    const uint32_t s = sr_unit_seed(unit, c.key_col);
+    wx0 = __byte_perm(e2m1x4_rs(q[0].x, q[1].x, q[2].x, q[3].x, sr_rbits(s, 0)),
+                      e2m1x4_rs(q[4].x, q[5].x, q[6].x, q[7].x, sr_rbits(s, 1)), 0x5410);
+    wx1 = __byte_perm(e2m1x4_rs(q[8].x, q[9].x, q[10].x, q[11].x, sr_rbits(s, 2)),
+                      e2m1x4_rs(q[12].x, q[13].x, q[14].x, q[15].x, sr_rbits(s, 3)), 0x5410);
+    wy0 = __byte_perm(e2m1x4_rs(q[0].y, q[1].y, q[2].y, q[3].y, sr_rbits(s, 4)),
+                      e2m1x4_rs(q[4].y, q[5].y, q[6].y, q[7].y, sr_rbits(s, 5)), 0x5410);
+    wy1 = __byte_perm(e2m1x4_rs(q[8].y, q[9].y, q[10].y, q[11].y, sr_rbits(s, 6)),
+                      e2m1x4_rs(q[12].y, q[13].y, q[14].y, q[15].y, sr_rbits(s, 7)), 0x5410);
   } else {
-    float2 q[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) q[i] = div2(v[i], nd, yy);
     wx0 = e2m1x8(q[0].x, q[1].x, q[2].x, q[3].x, q[4].x, q[5].x, q[6].x, q[7].x);
     wx1 = e2m1x8(q[8].x, q[9].x, q[10].x, q[11].x, q[12].x, q[13].x, q[14].x, q[15].x);
     wy0 = e2m1x8(q[0].y, q[1].y, q[2].y, q[3].y, q[4].y, q[5].y, q[6].y, q[7].y);
     wy1 = e2m1x8(q[8].y, q[9].y, q[10].y, q[11].y, q[12].y, q[13].y, q[14].y, q[15].y);
   }
   // Smallest non-zero |v|: 2^-133 for bf16 inputs and sums of them, 2^-149 otherwise.
-  const float risk = (F32IN || (HAD && !hdr->had_fast)) ? 1.0f : 65536.0f;
-  if (dx >= risk) {
-    wx0 &= underflow_mask8(&v[0].x, 2, dx);
-    wx1 &= underflow_mask8(&v[8].x, 2, dx);
-  }
-  if (dyv >= risk) {
-    wy0 &= underflow_mask8(&v[0].y, 2, dyv);
-    wy1 &= underflow_mask8(&v[8].y, 2, dyv);
+  const float risk = (F32IN || HADM == 2) ? 1.0f : 65536.0f;
+  if (__any_sync(0xFFFFFFFFu, dx >= risk || dyv >= risk)) {
+    if (dx >= risk) {
+      wx0 &= underflow_mask8(&v[0].x, 2, dx);
+      wx1 &= underflow_mask8(&v[8].x, 2, dx);
+    }
+    if (dyv >= risk) {
+      wy0 &= underflow_mask8(&v[0].y, 2, dyv);
+      wy1 &= underflow_mask8(&v[8].y, 2, dyv);
+    }
   }
   // Columns past K (the zero-filled half of a K % 128 == 64 tile) stage zeros: their scale bytes
   // are the contract's zero padding, and their packed rows are never stored.
@@ -564,17 +598,96 @@ __device__ __forceinline__ void col_store(const QuantArgs& a, int64_t m0, int64_
 }
 
 // ---------------------------------------------------------------------------------------------
-// The kernel
+// The tile loop and the kernel
 // ---------------------------------------------------------------------------------------------
+template <bool F32IN>
+__device__ __forceinline__ void issue_tile(const CUtensorMap& tmap, const QuantArgs& a, QHeader* hdr, uint8_t* smem,
+                                           int it) {
+  const int s = it % kQStages;
+  const int t = (int)blockIdx.x + it * (int)gridDim.x;
+  const int mt = t / a.tiles_k, kt = t - mt * a.tiles_k;
+  uint8_t* dst = smem + (size_t)s * kQTileBytes;
+  mbar_arrive_expect_tx(&hdr->full[s], kQTileBytes);
+  tma_load_2d(dst, &tmap, &hdr->full[s], kt * QTile<F32IN>::kCols, mt * kQRows);
+  tma_load_2d(dst + kQBoxBytes, &tmap, &hdr->full[s], kt * QTile<F32IN>::kCols + QTile<F32IN>::kBoxCols,
+              mt * kQRows);
+}
+
+template <bool F32IN, bool DO_ROW, bool DO_COL, int HADM, bool SR>
+__device__ __forceinline__ void quant_loop(const CUtensorMap& tmap, const QuantArgs& a, QHeader* hdr, uint8_t* smem,
+                                           QCtx& c, uint32_t cur_gs, int n_my) {
+  constexpr int S = kQStages;
+  constexpr int kCols = QTile<F32IN>::kCols;
+  const int tid = threadIdx.x, lane = tid & 31, g = tid >> 5;
+  const uint32_t stage_pk = smem_u32(hdr->stage_pk), stage_sc = smem_u32(hdr->stage_sc);
+  uint32_t sgn[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) sgn[j] = (HADM == 1) ? hdr->sign_word[j] : 0u;
+
+  for (int it = 0; it < n_my; ++it) {
+    const int s = it % S;
+    const bool ok = mbar_wait(&hdr->full[s], (uint32_t)((it / S) & 1));
+    // Every thread has finished tile it-1 once past this barrier, so its stage may be refilled
+    // and the colblock staging area reused.
+    if (__syncthreads_or(!ok)) {
+      if (tid == 0) record_status(&g_quant_status, kStatusTimeoutTma);
+      return;
+    }
+    if (tid == 0 && it >= 1 && it - 1 + S < n_my) issue_tile<F32IN>(tmap, a, hdr, smem, it - 1 + S);
+
+    const int t = (int)blockIdx.x + it * (int)gridDim.x;
+    const int mt = t / a.tiles_k, kt = t - mt * a.tiles_k;
+    const int64_t m0 = (int64_t)mt * kQRows, k0 = (int64_t)kt * kCols;
+    const int valid_cols = (int)min((int64_t)kCols, a.K - k0);
+    if (a.offs != nullptr) {
+      // A tile of another group: rebuild the tables for its global scale (every thread is past
+      // the previous tile here, so the tables are free).
+      const float gt = a.gs[group_of_row(a.offs, a.ngroups, m0)];
+      if (__float_as_uint(gt) != cur_gs) {
+        cur_gs = __float_as_uint(gt);
+        build_tables(hdr, gt, c);
+        __syncthreads();
+      }
+    }
+    const uint32_t tile = smem_u32(smem + (size_t)s * kQTileBytes);
+    if constexpr (DO_COL) {
+      // Unit base: box (cp / pairs-per-box), row 16g, the pair's 16-byte chunk and offset in it.
+      uint32_t base;
+      if constexpr (!F32IN) {
+        base = tile + 16 * g * 128 + (((lane >> 2) & 7) << 4) + ((lane & 3) << 2);
+      } else {
+        base = tile + (lane >> 4) * kQBoxBytes + 16 * g * 128 + (((lane & 15) >> 1) << 4) + ((lane & 1) << 3);
+      }
+      uint32_t bk[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) bk[k] = base ^ (uint32_t)(k << 4);
+      col_unit<F32IN, HADM, SR>(bk, 0, sgn, c, a, m0, k0, lane, 2 * lane < valid_cols, stage_pk, stage_sc);
+      if constexpr (!F32IN)
+        col_unit<F32IN, HADM, SR>(bk, kQBoxBytes, sgn, c, a, m0, k0, lane + 32, 2 * (lane + 32) < valid_cols,
+                                  stage_pk, stage_sc);
+    }
+    if constexpr (DO_ROW) {
+      const int r = tid & 127, h = tid >> 7;
+      const uint32_t rb = tile + h * kQBoxBytes + r * 128 + ((r & 7) << 4);
+      uint32_t rk[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) rk[k] = rb ^ (uint32_t)(k << 4);
+      row_part<F32IN, SR>(rk, c, a, m0, k0, mt, (F32IN ? 32 : 64) * h < valid_cols);
+    }
+    if constexpr (DO_COL) {
+      __syncthreads();
+      col_store<F32IN>(a, m0, k0, mt, valid_cols, stage_pk, stage_sc);
+    }
+  }
+}
+
 template <bool F32IN, bool DO_ROW, bool DO_COL, bool HAD, bool SR>
 __global__ void __launch_bounds__(kQThreads, 2)
     nvfp4_quantize_kernel(const __grid_constant__ CUtensorMap tmap, const QuantArgs a) {
   constexpr int S = kQStages;
-  constexpr int kCols = QTile<F32IN>::kCols;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   QHeader* hdr = reinterpret_cast<QHeader*>(smem + (size_t)kQTileBytes * S);
-  const uint32_t stage_pk = smem_u32(hdr->stage_pk), stage_sc = smem_u32(hdr->stage_sc);
   const int tid = threadIdx.x;
 
   if ((int)blockIdx.x >= a.n_tiles) return;
@@ -585,24 +698,21 @@ __global__ void __launch_bounds__(kQThreads, 2)
     fence_mbar_init();
     prefetch_tensormap(&tmap);
   }
+  __syncthreads();
+  if (tid == 0) {
+    for (int it = 0; it < S && it < n_my; ++it) issue_tile<F32IN>(tmap, a, hdr, smem, it);
+  }
   QCtx c;
-  c.hdr = hdr;
+  c.tab = smem_u32(hdr->table);
+  c.thr = smem_u32(hdr->thr);
+  c.had = smem_u32(hdr->had);
+  c.key = 0;
+  c.key_col = 0;
   const int first_group =
       (a.offs != nullptr) ? group_of_row(a.offs, a.ngroups, (int64_t)((int)blockIdx.x / a.tiles_k) * kQRows) : 0;
   const float gs = a.gs[first_group];
-  uint32_t cur_gs = __float_as_uint(gs);
-  const float denom = __fmul_rn(6.0f, gs);
-  c.nden = -denom;
-  c.rden = __frcp_rn(denom);
-  c.key = 0;
-  c.key_col = 0;
-  if (tid < 127) {
-    const float d = __fmul_rn(e4m3_value(tid), gs);
-    hdr->table[tid] = make_float2(d, __frcp_rn(d));
-  }
-  if constexpr (HAD) {
-    hdr->had[tid] = a.hadamard[tid];
-  }
+  build_tables(hdr, gs, c);
+  if constexpr (HAD) hdr->had[tid] = a.hadamard[tid];
   if constexpr (SR) {
     c.key = sr_key(a.seed);
     c.key_col = mix32(c.key ^ 0x85EBCA6Bu);
@@ -619,68 +729,14 @@ __global__ void __launch_bounds__(kQThreads, 2)
         ok = ok && (hdr->had[e] == want) && (fabsf(rj) == 0.25f);
       }
       ok = __all_sync(0xFFFFFFFFu, ok);
-      if (tid < 16) hdr->sign_mask[tid] = (hdr->had[tid * 16] < 0.0f) ? 0xFFFFFFFFu : 0u;
+      if (tid < 16) hdr->sign_word[tid] = (hdr->had[tid * 16] < 0.0f) ? 0x80000000u : 0u;
       if (tid == 0) hdr->had_fast = ok ? 1 : 0;
     }
     __syncthreads();
-  }
-
-  auto issue = [&](int it) {
-    const int s = it % S;
-    const int t = (int)blockIdx.x + it * (int)gridDim.x;
-    const int mt = t / a.tiles_k, kt = t - mt * a.tiles_k;
-    uint8_t* dst = smem + (size_t)s * kQTileBytes;
-    mbar_arrive_expect_tx(&hdr->full[s], kQTileBytes);
-    tma_load_2d(dst, &tmap, &hdr->full[s], kt * kCols, mt * kQRows);
-    tma_load_2d(dst + kQBoxBytes, &tmap, &hdr->full[s], kt * kCols + QTile<F32IN>::kBoxCols, mt * kQRows);
-  };
-  if (tid == 0) {
-    for (int it = 0; it < S && it < n_my; ++it) issue(it);
-  }
-
-  for (int it = 0; it < n_my; ++it) {
-    const int s = it % S;
-    const bool ok = mbar_wait(&hdr->full[s], (uint32_t)((it / S) & 1));
-    // Every thread has finished tile it-1 once past this barrier, so its stage may be refilled
-    // and the colblock staging area reused.
-    if (__syncthreads_or(!ok)) {
-      if (tid == 0) record_status(&g_quant_status, kStatusTimeoutTma);
-      return;
-    }
-    if (tid == 0 && it >= 1 && it - 1 + S < n_my) issue(it - 1 + S);
-
-    const int t = (int)blockIdx.x + it * (int)gridDim.x;
-    const int mt = t / a.tiles_k, kt = t - mt * a.tiles_k;
-    const int64_t m0 = (int64_t)mt * kQRows, k0 = (int64_t)kt * kCols;
-    const int valid_cols = (int)min((int64_t)kCols, a.K - k0);
-    if (a.offs != nullptr) {
-      // A tile of another group: rebuild the divisor table for its global scale (every thread is
-      // past the previous tile here, so the table is free).
-      const float gt = a.gs[group_of_row(a.offs, a.ngroups, m0)];
-      if (__float_as_uint(gt) != cur_gs) {
-        cur_gs = __float_as_uint(gt);
-        const float dn = __fmul_rn(6.0f, gt);
-        c.nden = -dn;
-        c.rden = __frcp_rn(dn);
-        if (tid < 127) {
-          const float d = __fmul_rn(e4m3_value(tid), gt);
-          hdr->table[tid] = make_float2(d, __frcp_rn(d));
-        }
-        __syncthreads();
-      }
-    }
-    const uint32_t tile = smem_u32(smem + (size_t)s * kQTileBytes);
-    if constexpr (DO_COL) {
-      const int lane = tid & 31;
-      col_unit<F32IN, HAD, SR>(tile, c, a, m0, k0, lane, 2 * lane < valid_cols, stage_pk, stage_sc);
-      if constexpr (!F32IN)
-        col_unit<F32IN, HAD, SR>(tile, c, a, m0, k0, lane + 32, 2 * (lane + 32) < valid_cols, stage_pk, stage_sc);
-    }
-    if constexpr (DO_ROW) row_tile<F32IN, SR>(tile, c, a, m0, k0, mt, kt, valid_cols);
-    if constexpr (DO_COL) {
-      __syncthreads();
-      col_store<F32IN>(a, m0, k0, mt, valid_cols, stage_pk, stage_sc);
-    }
+    if (hdr->had_fast) quant_loop<F32IN, DO_ROW, DO_COL, 1, SR>(tmap, a, hdr, smem, c, __float_as_uint(gs), n_my);
+    else quant_loop<F32IN, DO_ROW, DO_COL, 2, SR>(tmap, a, hdr, smem, c, __float_as_uint(gs), n_my);
+  } else {
+    quant_loop<F32IN, DO_ROW, DO_COL, 0, SR>(tmap, a, hdr, smem, c, __float_as_uint(gs), n_my);
   }
 }
 
@@ -858,6 +914,29 @@ __global__ void selftest_division_kernel(const float* x, const float* d, int64_t
   if ((threadIdx.x & 31) == 0 && bad) atomicAdd(mismatches, bad);
 }
 
+// Compares the scale-byte shortcut (scale_bytes2 with the per-CTA thresholds) with the exact
+// evaluation for amax[i] under the global scale *gs; counts mismatches.
+__global__ void __launch_bounds__(256) selftest_scale_kernel(const float* amax, int64_t n, const float* gs,
+                                                             uint32_t* mismatches) {
+  __shared__ float thr[128];
+  const float g = *gs;
+  const float den = __fmul_rn(6.0f, g), rd = __frcp_rn(den);
+  const float rup = rd * 1.00000095367431640625f;
+  if (threadIdx.x < 128)
+    thr[threadIdx.x] = threadIdx.x < 126 ? scale_threshold(threadIdx.x + 1, -den, rd) : __uint_as_float(0x7FFFFFFFu);
+  __syncthreads();
+  const uint32_t thr_addr = smem_u32(thr);
+  uint32_t bad = 0;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const float a0 = amax[i];
+    uint32_t b0, b1;
+    scale_bytes2(a0, a0, rup, thr_addr, b0, b1);
+    bad += (b0 != block_scale_byte(a0, -den, rd)) ? 1u : 0u;
+  }
+  bad = __reduce_add_sync(0xFFFFFFFFu, bad);
+  if ((threadIdx.x & 31) == 0 && bad) atomicAdd(mismatches, bad);
+}
+
 }  // namespace rb
 
 // =============================================================================================
@@ -1010,9 +1089,9 @@ static int quantize_impl(const void* x, int dtype, int64_t rows, int64_t cols, i
                        (long long)ld);
     return RB_ERR_ARG;
   }
-  if ((row && ((reinterpret_cast<uintptr_t>(row_packed) & 7) || (reinterpret_cast<uintptr_t>(row_scale) & 3))) ||
-      (col && (reinterpret_cast<uintptr_t>(col_packed) & 7 || (reinterpret_cast<uintptr_t>(col_scale) & 7)))) {
-    rb_host::set_error("nvfp4 quantize: output buffers must be 8-byte aligned");
+  if ((row && ((reinterpret_cast<uintptr_t>(row_packed) & 15) || (reinterpret_cast<uintptr_t>(row_scale) & 3))) ||
+      (col && (reinterpret_cast<uintptr_t>(col_packed) & 15 || (reinterpret_cast<uintptr_t>(col_scale) & 15)))) {
+    rb_host::set_error("nvfp4 quantize: packed outputs must be 16-byte aligned, scales 16 (colblock) or 4 (rowblock)");
     return RB_ERR_ARG;
   }
   if ((rows / 128) * (cols / 64) > (int64_t)0x7FFFFFFF) {
@@ -1041,9 +1120,6 @@ static int quantize_impl(const void* x, int dtype, int64_t rows, int64_t cols, i
   a.col_scale = reinterpret_cast<uint8_t*>(col_scale);
   const int tile_cols = f32 ? QTile<true>::kCols : QTile<false>::kCols;
   a.tiles_k = (int)((cols + tile_cols - 1) / tile_cols);
-  a.p2 = 2u;
-  a.p22 = 1u << 22;
-  a.p25 = 1u << 25;
   a.n_tiles = (int)((rows / 128) * a.tiles_k);
   a.offs = offs;
   a.ngroups = ngroups;
@@ -1125,6 +1201,25 @@ int rb_nvfp4_selftest_division(const float* x, const float* d, int64_t n, uint32
   }
   const int sms = rb_host::num_sms(rb_host::current_device());
   rb::selftest_division_kernel<<<4 * sms, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(x, d, n, mismatches);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    rb_host::set_error("selftest launch failed: %s", cudaGetErrorString(e));
+    return RB_ERR_CUDA;
+  }
+  return RB_OK;
+}
+
+int rb_nvfp4_selftest_scale(const float* amax, int64_t n, const float* gs, uint32_t* mismatches, void* stream) {
+  if (amax == nullptr || gs == nullptr || mismatches == nullptr || n < 0) {
+    rb_host::set_error("nvfp4 selftest_scale: bad arguments");
+    return RB_ERR_ARG;
+  }
+  if (!device_is_sm100()) {
+    rb_host::set_error("nvfp4 selftest_scale: the current device is not an sm_100 GPU");
+    return RB_ERR_DEVICE;
+  }
+  const int sms = rb_host::num_sms(rb_host::current_device());
+  rb::selftest_scale_kernel<<<2 * sms, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(amax, n, gs, mismatches);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     rb_host::set_error("selftest launch failed: %s", cudaGetErrorString(e));

@@ -355,3 +355,56 @@ def test_division_matches_ieee(nv):
     _lib.check(lib.rb_nvfp4_selftest_division(xx.data_ptr(), dd.data_ptr(), xx.numel(), mism.data_ptr(),
                                               torch.cuda.current_stream().cuda_stream), "selftest")
     assert mism.item() == 0
+
+
+def test_scale_byte_shortcut_matches_exact(nv):
+    """The quantizer's block-scale byte (hardware e4m3 rounding of amax / (6 gs) plus one threshold
+    compare) equals the exact evaluation (correctly rounded quotient, clamp, round up to e4m3) for
+    every amax near every threshold, for every bf16 magnitude, and for random fp32 amaxes, over a
+    spread of global scales."""
+    from radiance_b200 import _lib
+
+    lib = _lib.load()
+    g = torch.Generator().manual_seed(3)
+    gss = torch.cat([torch.tensor([1e-12, 1.0, 2.0**-20, 3.7e-5, 0.11, 1.5e30]),
+                     torch.rand(26, generator=g) * 10.0 ** torch.randint(-12, 8, (26,), generator=g)])
+    bf16 = (torch.arange(0, 0x7F81, dtype=torch.int32) << 16).view(torch.float32)  # 0, every bf16, +inf
+    mism = torch.zeros(1, dtype=torch.int32, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    for gsv in gss.tolist():
+        gs = torch.tensor([gsv], dtype=torch.float32, device="cuda")
+        den = np.float32(6.0) * np.float32(gsv)
+        # amaxes around value(b) * den for every e4m3 byte b, +-64 ulps
+        centers = (O.E4M3_VALUES[:127].astype(np.float32) * den).astype(np.float32).view(np.int32)
+        near = (centers[:, None] + np.arange(-64, 65, dtype=np.int32)[None, :]).reshape(-1)
+        near = near[(near >= 0) & (near < 0x7F800000)].view(np.float32)
+        rnd = (torch.rand(1 << 16, generator=g) * 10.0 ** torch.randint(-40, 38, (1 << 16,), generator=g)).float()
+        amax = torch.cat([torch.from_numpy(near.copy()), bf16, rnd]).cuda()
+        _lib.check(lib.rb_nvfp4_selftest_scale(amax.data_ptr(), amax.numel(), gs.data_ptr(), mism.data_ptr(), stream),
+                   "selftest_scale")
+    assert mism.item() == 0
+
+
+def test_stochastic_rounding_wide_range_matches_oracle(nv):
+    """Stochastic rounding against the oracle on inputs spanning 2^-30 .. 2^4 inside each block, so
+    that most quotients fall below the first e2m1 level (the convert's subnormal range) and some
+    underflow entirely; both forms, fused."""
+    torch.manual_seed(11)
+    rows, cols = 512, 384
+    mag = torch.exp2(torch.rand(rows, cols) * 34.0 - 30.0)
+    x = (torch.randn(rows, cols).sign() * mag).to(torch.bfloat16).cuda()
+    gs = nv.global_scale_of(x)
+    gs_np = np.float32(gs.item())
+    seed_value = 99
+    seed = torch.tensor(seed_value, device="cuda", dtype=torch.int64)
+    had = O.hadamard_matrix()
+    h = torch.from_numpy(had).cuda()
+    row, col = nv.quantize_both(x, global_scale=gs, hadamard=h, stochastic=True, seed=seed)
+    xn = to_numpy_f32(x)
+    pr, sr_, _ = O.quantize(xn, -1, gs=gs_np, r=O.sr_stream_row(rows, cols, seed_value))
+    pc, sc, _ = O.quantize(xn, 0, gs=gs_np, hadamard=had, r=O.sr_stream_col(rows, cols, seed_value))
+    np.testing.assert_array_equal(u8(row.packed), pr)
+    np.testing.assert_array_equal(u8(row.scale), sr_)
+    np.testing.assert_array_equal(u8(col.packed), pc)
+    np.testing.assert_array_equal(u8(col.scale), sc)
+    _status_ok()
