@@ -98,8 +98,10 @@ __device__ __forceinline__ int group_of_row(const int64_t* offs, int ngroups, in
 
 struct QHeader {
   uint64_t full[kQStages];
-  float2 table[128];  // (D, RN(1/D)) for each e4m3 byte; entry 127 unused
-  float thr[128];     // thr[e]: the smallest block amax whose scale byte exceeds e (NaN: none)
+  // Per e4m3 byte e: (D_e, RN(1/D_e), thr_e, 0), D_e = value(e) * gs and thr_e the smallest block
+  // amax whose scale byte exceeds e (NaN: none).  16-byte entries, so both loads of pick_scale
+  // are aligned.
+  float4 sct[128];
   float had[256];
   uint32_t sign_word[16];
   int had_fast;
@@ -200,17 +202,42 @@ __device__ __forceinline__ void sts8(uint32_t addr, uint32_t v) {
   asm volatile("st.shared.b8 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
 }
 
-// Scale bytes of two blocks from their amaxes: e = RN_e4m3(amax * rup) is the exact byte or the
-// one below it, and thr[e] decides.  (rup >= (1 + 2^-21) / (6gs) puts amax * rup above the exact
-// quotient s; it stays below s (1 + 2^-19), far short of the next e4m3 rounding boundary above
-// ceil_e4m3(s), so RN_e4m3 lands on ceil_e4m3(s) or the value below.  The clamps agree: e = 0
-// below 1e-12 where the byte is 1 = e + [amax >= thr[0] = 0], and e = 126 = byte at saturation,
-// where thr[126] is NaN.)
-__device__ __forceinline__ void scale_bytes2(float a0, float a1, float rup, uint32_t thr, uint32_t& b0, uint32_t& b1) {
+// Scale bytes, divisors and reciprocals of two blocks from their amaxes: e = RN_e4m3(amax * rup) is
+// the exact byte or the one below it, and thr_e decides; entries e and e + 1 are read together.
+// (rup >= (1 + 2^-21) / (6gs) puts amax * rup above the exact quotient s; it stays below
+// s (1 + 2^-19), far short of the next e4m3 rounding boundary above ceil_e4m3(s), so RN_e4m3 lands on
+// ceil_e4m3(s) or the value below.  The clamps agree: e = 0 below 1e-12 where the byte is
+// 1 = e + [amax >= thr_0 = 0], and e = 126 = byte at saturation, where thr_126 is NaN.)
+struct BlockScale {
+  uint32_t byte;
+  float d, y;
+};
+__device__ __forceinline__ BlockScale pick_scale(float amax, uint32_t e, uint32_t sct) {
+  const uint4 t = lds128(sct + 16 * e);       // (D_e, Y_e, thr_e, 0)
+  const uint2 n = lds64(sct + 16 * (e + 1));  // (D_e+1, Y_e+1)
+  const bool up = amax >= __uint_as_float(t.z);
+  BlockScale b;
+  b.byte = e + (up ? 1u : 0u);
+  b.d = __uint_as_float(up ? n.x : t.x);
+  b.y = __uint_as_float(up ? n.y : t.y);
+  return b;
+}
+__device__ __forceinline__ void scale_lookup2(float a0, float a1, float rup, uint32_t sct, BlockScale& s0,
+                                              BlockScale& s1) {
   const uint32_t e = e4m3x2_rn(a1 * rup, a0 * rup);
-  const uint32_t e0 = e & 0xFFu, e1 = e >> 8;
-  b0 = e0 + (a0 >= __uint_as_float(lds32(thr + 4 * e0)) ? 1u : 0u);
-  b1 = e1 + (a1 >= __uint_as_float(lds32(thr + 4 * e1)) ? 1u : 0u);
+  // e <= 126 for every finite product; the clamp keeps entry e + 1 inside the table for a NaN one.
+  s0 = pick_scale(a0, min(e & 0xFFu, 126u), sct);
+  s1 = pick_scale(a1, min(e >> 8, 126u), sct);
+}
+
+// max(0, |a[0]|, |a[s]|, ..., |a[15 s]|) as a depth-3 tree of three-input maxima.
+__device__ __forceinline__ float amax16(const float* a, int st) {
+  const float m0 = fmax3(fabsf(a[0]), fabsf(a[st]), fabsf(a[2 * st]));
+  const float m1 = fmax3(fabsf(a[3 * st]), fabsf(a[4 * st]), fabsf(a[5 * st]));
+  const float m2 = fmax3(fabsf(a[6 * st]), fabsf(a[7 * st]), fabsf(a[8 * st]));
+  const float m3 = fmax3(fabsf(a[9 * st]), fabsf(a[10 * st]), fabsf(a[11 * st]));
+  const float m4 = fmax3(fabsf(a[12 * st]), fabsf(a[13 * st]), fabsf(a[14 * st]));
+  return fmax3(fmax3(m0, m1, m2), fmax3(m3, m4, fabsf(a[15 * st])), 0.0f);
 }
 
 // q = RN(x / d) for a float2, given nd = -d and y = RN(1/d) (Markstein, two corrections).
@@ -324,26 +351,26 @@ __device__ __forceinline__ void st_global_v4(void* p, uint32_t a, uint32_t b, ui
 }
 
 struct QCtx {
-  uint32_t tab;      // shared address of QHeader::table
-  uint32_t thr;      // shared address of QHeader::thr
+  uint32_t sct;      // shared address of QHeader::sct
   uint32_t had;      // shared address of QHeader::had
   float rup;         // RN(1/(6 gs)) (1 + 2^-20)
   uint32_t key;      // stochastic rounding: rowblock-form key
   uint32_t key_col;  // colblock-form key
 };
 
-// Divisor/reciprocal table and scale thresholds for one global scale (threads 0..127).
-__device__ __forceinline__ void build_tables(QHeader* hdr, float gs, QCtx& c) {
+// The per-byte scale table for one global scale (threads 0..127); returns rup.
+__device__ __forceinline__ float build_scale_table(float4* sct, float gs) {
   const int tid = threadIdx.x;
   const float den = __fmul_rn(6.0f, gs);
   const float rd = __frcp_rn(den);
-  c.rup = rd * 1.00000095367431640625f;  // 1 + 2^-20
-  if (tid < 127) {
-    const float d = __fmul_rn(e4m3_value(tid), gs);
-    hdr->table[tid] = make_float2(d, __frcp_rn(d));
+  if (tid < 128) {
+    const float d = tid < 127 ? __fmul_rn(e4m3_value(tid), gs) : 1.0f;
+    const float thr = tid < 126 ? scale_threshold(tid + 1, -den, rd) : __uint_as_float(0x7FFFFFFFu);
+    sct[tid] = make_float4(d, __frcp_rn(d), thr, 0.0f);
   }
-  if (tid < 128) hdr->thr[tid] = tid < 126 ? scale_threshold(tid + 1, -den, rd) : __uint_as_float(0x7FFFFFFFu);
+  return rd * 1.00000095367431640625f;  // 1 + 2^-20
 }
+__device__ __forceinline__ void build_tables(QHeader* hdr, float gs, QCtx& c) { c.rup = build_scale_table(hdr->sct, gs); }
 
 // ---------------------------------------------------------------------------------------------
 // Rowblock form of a tile: thread t owns row t % 128 of box t / 128.  `rk[c]` is the shared
@@ -377,21 +404,22 @@ __device__ __forceinline__ void row_part(const uint32_t (&rk)[8], const QCtx& c,
         }
       }
     }
-    float am[2];
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      float m = 0.0f;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) m = fmax3(m, fabsf(v[i][e].x), fabsf(v[i][e].y));
-      am[i] = m;
-    }
-    scale_bytes2(am[0], am[1], c.rup, c.thr, sb[u][0], sb[u][1]);
+    BlockScale bs[2];
+    scale_lookup2(amax16(&v[0][0].x, 1), amax16(&v[1][0].x, 1), c.rup, c.sct, bs[0], bs[1]);
+    sb[u][0] = bs[0].byte;
+    sb[u][1] = bs[1].byte;
     uint32_t seed = 0;
     if constexpr (SR) seed = sr_unit_seed((uint64_t)(m0 + r) * (uint64_t)(a.K >> 5) + (uint64_t)(col0 >> 5) + u, c.key);
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
-      const uint2 t = lds64(c.tab + 8 * sb[u][i]);
-      const float d = __uint_as_float(t.x), y = __uint_as_float(t.y);
+      const float d = bs[i].d, y = bs[i].y;
+      // Quotients that underflow to +-0 (possible only for large divisors) must give nibble 0.
+      const float risk = F32IN ? 1.0f : 65536.0f;  // smallest |x|: 2^-149 (fp32), 2^-133 (bf16)
+      uint32_t keep0 = 0xFFFFFFFFu, keep1 = 0xFFFFFFFFu;
+      if (__any_sync(0xFFFFFFFFu, d >= risk) && d >= risk) {
+        keep0 = underflow_mask8(&v[i][0].x, 1, d);
+        keep1 = underflow_mask8(&v[i][4].x, 1, d);
+      }
       const float2 nd = make_float2(-d, -d), yy = make_float2(y, y);
       float2 q[8];
 #pragma unroll
@@ -407,11 +435,8 @@ __device__ __forceinline__ void row_part(const uint32_t (&rk)[8], const QCtx& c,
         w[u][2 * i] = e2m1x8(q[0].x, q[0].y, q[1].x, q[1].y, q[2].x, q[2].y, q[3].x, q[3].y);
         w[u][2 * i + 1] = e2m1x8(q[4].x, q[4].y, q[5].x, q[5].y, q[6].x, q[6].y, q[7].x, q[7].y);
       }
-      const float risk = F32IN ? 1.0f : 65536.0f;  // smallest |x|: 2^-149 (fp32), 2^-133 (bf16)
-      if (__any_sync(0xFFFFFFFFu, d >= risk) && d >= risk) {
-        w[u][2 * i] &= underflow_mask8(&v[i][0].x, 1, d);
-        w[u][2 * i + 1] &= underflow_mask8(&v[i][4].x, 1, d);
-      }
+      w[u][2 * i] &= keep0;
+      w[u][2 * i + 1] &= keep1;
     }
   }
   if (!valid) return;
@@ -499,19 +524,27 @@ __device__ __forceinline__ void col_unit(const uint32_t (&bk)[8], uint32_t box_o
 #pragma unroll
     for (int i = 0; i < 16; ++i) v[i] = y[i];
   }
-  float ax = 0.0f, ay = 0.0f;
-#pragma unroll
-  for (int i = 0; i < 16; i += 2) {
-    ax = fmax3(ax, fabsf(v[i].x), fabsf(v[i + 1].x));
-    ay = fmax3(ay, fabsf(v[i].y), fabsf(v[i + 1].y));
-  }
   const float unfold = 1.0f / fold;  // exact (1 or 1/4)
-  uint32_t bx, by;
-  scale_bytes2(ax * unfold, ay * unfold, c.rup, c.thr, bx, by);
-  const uint2 tx = lds64(c.tab + 8 * bx), ty = lds64(c.tab + 8 * by);
-  const float dx = __uint_as_float(tx.x) * fold, dyv = __uint_as_float(ty.x) * fold;
+  BlockScale sx, sy;
+  scale_lookup2(amax16(&v[0].x, 2) * unfold, amax16(&v[0].y, 2) * unfold, c.rup, c.sct, sx, sy);
+  const uint32_t bx = sx.byte, by = sy.byte;
+  const float dx = sx.d * fold, dyv = sy.d * fold;
+  // Quotients that underflow to +-0 (possible only for large divisors) must give nibble 0.
+  // Smallest non-zero |v|: 2^-133 for bf16 inputs and sums of them, 2^-149 otherwise.
+  const float risk = (F32IN || HADM == 2) ? 1.0f : 65536.0f;
+  uint32_t kx0 = 0xFFFFFFFFu, kx1 = 0xFFFFFFFFu, ky0 = 0xFFFFFFFFu, ky1 = 0xFFFFFFFFu;
+  if (__any_sync(0xFFFFFFFFu, dx >= risk || dyv >= risk)) {
+    if (dx >= risk) {
+      kx0 = underflow_mask8(&v[0].x, 2, dx);
+      kx1 = underflow_mask8(&v[8].x, 2, dx);
+    }
+    if (dyv >= risk) {
+      ky0 = underflow_mask8(&v[0].y, 2, dyv);
+      ky1 = underflow_mask8(&v[8].y, 2, dyv);
+    }
+  }
   const float2 nd = make_float2(-dx, -dyv);
-  const float2 yy = make_float2(__uint_as_float(tx.y) * unfold, __uint_as_float(ty.y) * unfold);
+  const float2 yy = make_float2(sx.y * unfold, sy.y * unfold);
   float2 q[16];
 #pragma unroll
   for (int i = 0; i < 16; ++i) q[i] = div2(v[i], nd, yy);
@@ -535,18 +568,10 @@ __device__ __forceinline__ void col_unit(const uint32_t (&bk)[8], uint32_t box_o
     wy0 = e2m1x8(q[0].y, q[1].y, q[2].y, q[3].y, q[4].y, q[5].y, q[6].y, q[7].y);
     wy1 = e2m1x8(q[8].y, q[9].y, q[10].y, q[11].y, q[12].y, q[13].y, q[14].y, q[15].y);
   }
-  // Smallest non-zero |v|: 2^-133 for bf16 inputs and sums of them, 2^-149 otherwise.
-  const float risk = (F32IN || HADM == 2) ? 1.0f : 65536.0f;
-  if (__any_sync(0xFFFFFFFFu, dx >= risk || dyv >= risk)) {
-    if (dx >= risk) {
-      wx0 &= underflow_mask8(&v[0].x, 2, dx);
-      wx1 &= underflow_mask8(&v[8].x, 2, dx);
-    }
-    if (dyv >= risk) {
-      wy0 &= underflow_mask8(&v[0].y, 2, dyv);
-      wy1 &= underflow_mask8(&v[8].y, 2, dyv);
-    }
-  }
+  wx0 &= kx0;
+  wx1 &= kx1;
+  wy0 &= ky0;
+  wy1 &= ky1;
   // Columns past K (the zero-filled half of a K % 128 == 64 tile) stage zeros: their scale bytes
   // are the contract's zero padding, and their packed rows are never stored.
   const uint32_t sbx = valid ? bx : 0u, sby = valid ? by : 0u;
@@ -703,8 +728,7 @@ __global__ void __launch_bounds__(kQThreads, 2)
     for (int it = 0; it < S && it < n_my; ++it) issue_tile<F32IN>(tmap, a, hdr, smem, it);
   }
   QCtx c;
-  c.tab = smem_u32(hdr->table);
-  c.thr = smem_u32(hdr->thr);
+  c.sct = smem_u32(hdr->sct);
   c.had = smem_u32(hdr->had);
   c.key = 0;
   c.key_col = 0;
@@ -914,24 +938,24 @@ __global__ void selftest_division_kernel(const float* x, const float* d, int64_t
   if ((threadIdx.x & 31) == 0 && bad) atomicAdd(mismatches, bad);
 }
 
-// Compares the scale-byte shortcut (scale_bytes2 with the per-CTA thresholds) with the exact
+// Compares the scale lookup (scale_lookup2 with the per-CTA table) with the exact
 // evaluation for amax[i] under the global scale *gs; counts mismatches.
 __global__ void __launch_bounds__(256) selftest_scale_kernel(const float* amax, int64_t n, const float* gs,
                                                              uint32_t* mismatches) {
-  __shared__ float thr[128];
+  __shared__ float4 sct[128];
   const float g = *gs;
   const float den = __fmul_rn(6.0f, g), rd = __frcp_rn(den);
-  const float rup = rd * 1.00000095367431640625f;
-  if (threadIdx.x < 128)
-    thr[threadIdx.x] = threadIdx.x < 126 ? scale_threshold(threadIdx.x + 1, -den, rd) : __uint_as_float(0x7FFFFFFFu);
+  const float rup = build_scale_table(sct, g);
   __syncthreads();
-  const uint32_t thr_addr = smem_u32(thr);
+  const uint32_t sct_addr = smem_u32(sct);
   uint32_t bad = 0;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     const float a0 = amax[i];
-    uint32_t b0, b1;
-    scale_bytes2(a0, a0, rup, thr_addr, b0, b1);
-    bad += (b0 != block_scale_byte(a0, -den, rd)) ? 1u : 0u;
+    BlockScale s0, s1;
+    scale_lookup2(a0, a0, rup, sct_addr, s0, s1);
+    const uint32_t want = block_scale_byte(a0, -den, rd);
+    const float d = __fmul_rn(e4m3_value(want), g);
+    bad += (s0.byte != want || s0.d != d || s0.y != __frcp_rn(d)) ? 1u : 0u;
   }
   bad = __reduce_add_sync(0xFFFFFFFFu, bad);
   if ((threadIdx.x & 31) == 0 && bad) atomicAdd(mismatches, bad);
