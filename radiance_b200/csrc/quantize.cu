@@ -17,10 +17,10 @@
 //   * Rowblock form: thread t owns row t % 128 and the 64 (bf16) or 32 (fp32) columns of box
 //     t / 128: four or two 16-element blocks, one 4- or 2-byte run of its scale-atom row, and a
 //     32- or 16-byte run of its packed row.
-//   * Colblock form: warp g owns rows 16g..16g+15; a unit is two adjacent columns, whose 16-row
-//     blocks are worked as float2 pairs on Blackwell's packed f32x2 FMA path.  The output (a
-//     transpose) is staged in shared memory and written as whole 64-byte rows and whole 512-byte
-//     scale atoms.
+//   * Colblock form: a unit is a 16-row group of two adjacent columns, whose two blocks are worked
+//     as float2 pairs on Blackwell's packed f32x2 FMA path.  A bf16 thread owns one column pair
+//     over 32 rows (two units) and stores each column's 16-byte run of the transposed output and
+//     its 2-byte run of scales directly: no staging and no block-wide barrier inside a tile.
 //   * x / D is never computed with a divide instruction.  Each block looks up D and
 //     Y = RN(1/D) in a 127-entry table (one entry per e4m3 byte, built per CTA with the IEEE
 //     reciprocal) and refines q0 = x*Y with two residual corrections r = x - q*D, q += r*Y, each a
@@ -105,8 +105,6 @@ struct QHeader {
   float had[256];
   uint32_t sign_word[16];
   int had_fast;
-  alignas(16) uint8_t stage_pk[8 * 1024];  // colblock codes: 8 warps x 128 rows x 8 bytes
-  alignas(16) uint8_t stage_sc[2 * 512];   // colblock scales: the tile's two SWIZZLE_32_4_4 atoms
 };
 
 constexpr size_t quant_smem_bytes() { return 1024 + (size_t)kQTileBytes * kQStages + sizeof(QHeader); }
@@ -194,12 +192,6 @@ __device__ __forceinline__ uint4 lds128(uint32_t addr) {
   uint4 v;
   asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
   return v;
-}
-__device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
-}
-__device__ __forceinline__ void sts8(uint32_t addr, uint32_t v) {
-  asm volatile("st.shared.b8 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
 }
 
 // Scale bytes, divisors and reciprocals of two blocks from their amaxes: e = RN_e4m3(amax * rup) is
@@ -453,37 +445,64 @@ __device__ __forceinline__ void row_part(const uint32_t (&rk)[8], const QCtx& c,
 }
 
 // ---------------------------------------------------------------------------------------------
-// The colblock form: warp g handles rows 16g..16g+15; each unit is two adjacent columns.  `bk[k]`
-// is (the unit's base address) ^ (k << 4): row j of the unit is at bk[j % 8] + j * 128.  Its two
-// 8-byte packed runs go to warp g's staging region (rows permuted by `row ^ 4g`, so both the
-// write and the row-wise read-back are conflict-free) and its two scale bytes into the staged
-// SWIZZLE_32_4_4 atoms.  HADM: 0 no rotation, 1 the Sylvester fast path (`sgn[j]` = 0 or
-// 0x80000000, the sign of row j of the matrix), 2 any other matrix.
+// The colblock form.  A unit is the 16-row group rg of two adjacent columns (pair cp of the tile):
+// two blocks, worked as float2 pairs.  `bk[k]` is (the unit's base address) ^ (k << 4) and
+// `box_off` a constant: row j of the unit is at bk[j % 8] + box_off + j * 128.  Returns the unit's
+// packed codes (8 bytes per column) and scale bytes.  HADM: 0 no rotation, 1 the Sylvester fast
+// path (`sgn[j]` = 0 or 0x80000000, the sign of row j of the matrix), 2 any other matrix.
 // ---------------------------------------------------------------------------------------------
+struct ColOut {
+  uint32_t wx0, wx1, wy0, wy1;  // codes of column 2cp (rows 0-7, 8-15) and of column 2cp + 1
+  uint32_t bx, by;              // their scale bytes
+};
+
 template <bool F32IN, int HADM, bool SR>
-__device__ __forceinline__ void col_unit(const uint32_t (&bk)[8], uint32_t box_off, const uint32_t (&sgn)[16],
-                                         const QCtx& c, const QuantArgs& a, int64_t m0, int64_t k0, int cp,
-                                         bool valid, uint32_t stage_pk, uint32_t stage_sc) {
-  const int g = threadIdx.x >> 5;
-  float2 v[16];
-#pragma unroll
-  for (int j = 0; j < 16; ++j) {
+__device__ __forceinline__ ColOut col_unit(const uint32_t (&bk)[8], uint32_t box_off, const uint32_t (&sgn)[16],
+                                           const QCtx& c, const QuantArgs& a, int64_t m0, int64_t k0, int cp,
+                                           int rg) {
+  // Row j of the unit as a float2 (columns 2cp, 2cp + 1), with the row sign of the fast path.
+  auto load_row = [&](int j) -> float2 {
     const uint32_t addr = bk[j & 7] + box_off + j * 128;
     if constexpr (!F32IN) {
       const uint32_t w = lds32(addr);
       if constexpr (HADM == 1) {
         // Flipping the sign bit is adding 2^31: low half (w << 16) + s, high half (w & ~0xFFFF) ^ s.
-        v[j] = make_float2(__uint_as_float(w * 65536u + sgn[j]), __uint_as_float((w & 0xFFFF0000u) ^ sgn[j]));
+        return make_float2(__uint_as_float(w * 65536u + sgn[j]), __uint_as_float((w & 0xFFFF0000u) ^ sgn[j]));
       } else {
-        v[j] = bf16x2_to_float2(w);
+        return bf16x2_to_float2(w);
       }
     } else {
       const uint2 w = lds64(addr);
-      if constexpr (HADM == 1) v[j] = make_float2(__uint_as_float(w.x ^ sgn[j]), __uint_as_float(w.y ^ sgn[j]));
-      else v[j] = make_float2(__uint_as_float(w.x), __uint_as_float(w.y));
+      if constexpr (HADM == 1) return make_float2(__uint_as_float(w.x ^ sgn[j]), __uint_as_float(w.y ^ sgn[j]));
+      else return make_float2(__uint_as_float(w.x), __uint_as_float(w.y));
     }
-  }
+  };
+  float2 v[16];
   float fold = 1.0f;  // the rotated values are fold * y (4 on the Hadamard fast path)
+  if constexpr (HADM == 2) {
+    // Any matrix: y_i = sum_j R[j][i] x_j, each product rounded, then added left to right.  Row j
+    // is loaded when its turn comes (a rolled loop), so only the 16 running sums stay live.
+#pragma unroll 1
+    for (int j = 0; j < 16; ++j) {
+      const uint32_t addr = (bk[0] ^ (uint32_t)((j & 7) << 4)) + box_off + j * 128;
+      float2 x;
+      if constexpr (!F32IN) {
+        x = bf16x2_to_float2(lds32(addr));
+      } else {
+        const uint2 w = lds64(addr);
+        x = make_float2(__uint_as_float(w.x), __uint_as_float(w.y));
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float h = __uint_as_float(lds32(c.had + 4 * (j * 16 + i)));
+        const float2 p = make_float2(__fmul_rn(h, x.x), __fmul_rn(h, x.y));
+        v[i] = j == 0 ? p : make_float2(__fadd_rn(v[i].x, p.x), __fadd_rn(v[i].y, p.y));
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = load_row(j);
+  }
   if constexpr (HADM == 1) {
     // y_i = sum_j syl(j, i) v_j, summed left to right.  syl(j, i) = (-1)^popc(i & j), so after
     // term j the partial sum of output i depends only on i mod w (w = the power of two above j):
@@ -507,22 +526,6 @@ __device__ __forceinline__ void col_unit(const uint32_t (&bk)[8], uint32_t box_o
 #pragma unroll
     for (int i = 0; i < 16; ++i) v[i] = y[i];
     fold = 4.0f;
-  } else if constexpr (HADM == 2) {
-    float2 y[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      float h = __uint_as_float(lds32(c.had + 4 * i));
-      float2 acc = make_float2(__fmul_rn(h, v[0].x), __fmul_rn(h, v[0].y));
-#pragma unroll
-      for (int j = 1; j < 16; ++j) {
-        h = __uint_as_float(lds32(c.had + 4 * (j * 16 + i)));
-        acc.x = __fadd_rn(acc.x, __fmul_rn(h, v[j].x));
-        acc.y = __fadd_rn(acc.y, __fmul_rn(h, v[j].y));
-      }
-      y[i] = acc;
-    }
-#pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = y[i];
   }
   const float unfold = 1.0f / fold;  // exact (1 or 1/4)
   BlockScale sx, sy;
@@ -550,9 +553,9 @@ __device__ __forceinline__ void col_unit(const uint32_t (&bk)[8], uint32_t box_o
   for (int i = 0; i < 16; ++i) q[i] = div2(v[i], nd, yy);
   uint32_t wx0, wx1, wy0, wy1;
   if constexpr (SR) {
-    // Unit: column pair k0/2 + cp, 16-row group m0/16 + g; converts 0..3 take column 2cp's rows
+    // Unit: column pair k0/2 + cp, 16-row group m0/16 + rg; converts 0..3 take column 2cp's rows
     // 4c..4c+3, converts 4..7 column 2cp + 1's.
-    const uint64_t unit = ((uint64_t)(k0 >> 1) + (uint64_t)cp) * (uint64_t)(a.M >> 4) + (uint64_t)(m0 >> 4) + g;
+    const uint64_t unit = ((uint64_t)(k0 >> 1) + (uint64_t)cp) * (uint64_t)(a.M >> 4) + (uint64_t)(m0 >> 4) + rg;
     const uint32_t s = sr_unit_seed(unit, c.key_col);
     wx0 = __byte_perm(e2m1x4_rs(q[0].x, q[1].x, q[2].x, q[3].x, sr_rbits(s, 0)),
                       e2m1x4_rs(q[4].x, q[5].x, q[6].x, q[7].x, sr_rbits(s, 1)), 0x5410);
@@ -568,57 +571,82 @@ __device__ __forceinline__ void col_unit(const uint32_t (&bk)[8], uint32_t box_o
     wy0 = e2m1x8(q[0].y, q[1].y, q[2].y, q[3].y, q[4].y, q[5].y, q[6].y, q[7].y);
     wy1 = e2m1x8(q[8].y, q[9].y, q[10].y, q[11].y, q[12].y, q[13].y, q[14].y, q[15].y);
   }
-  wx0 &= kx0;
-  wx1 &= kx1;
-  wy0 &= ky0;
-  wy1 &= ky1;
-  // Columns past K (the zero-filled half of a K % 128 == 64 tile) stage zeros: their scale bytes
-  // are the contract's zero padding, and their packed rows are never stored.
-  const uint32_t sbx = valid ? bx : 0u, sby = valid ? by : 0u;
-  // Packed runs of columns 2cp and 2cp+1 -> rows (2cp ^ 4g), (2cp ^ 4g) + 1 of region g.
-  sts128(stage_pk + g * 1024 + (((2 * cp) ^ (4 * g)) << 3), wx0, wx1, wy0, wy1);
-  // Scale bytes: atom g/4; 16-byte row (kk % 32); 4-byte group (k0 % 128 + kk) / 32; byte g % 4.
-  const int kk0 = (int)(k0 & 127) + 2 * cp;
-  const uint32_t sc = stage_sc + (g >> 2) * 512 + (kk0 & 31) * 16 + (kk0 >> 5) * 4 + (g & 3);
-  sts8(sc, sbx);
-  sts8(sc + 16, sby);
+  ColOut o;
+  o.wx0 = wx0 & kx0;
+  o.wx1 = wx1 & kx1;
+  o.wy0 = wy0 & ky0;
+  o.wy1 = wy1 & ky1;
+  o.bx = bx;
+  o.by = by;
+  return o;
 }
 
-// Writes the staged colblock outputs of one tile: `valid_cols` output rows of 64 bytes, and the
-// tile's scale atoms (whole atoms for a 128-column tile, the tile's half for a 64-column one).
-template <bool F32IN>
-__device__ __forceinline__ void col_store(const QuantArgs& a, int64_t m0, int64_t k0, int mt, int valid_cols,
-                                          uint32_t stage_pk, uint32_t stage_sc) {
-  constexpr int kCols = QTile<F32IN>::kCols;
-  const int t = threadIdx.x;
+// Stores of the colblock form.  Output row kk (input column k0 + kk) holds M/2 bytes; its scale
+// bytes live in SWIZZLE_32_4_4 atom (kk / 128, m / 64) at 16-byte row kk % 32, 4-byte group
+// (kk % 128) / 32, byte (m / 16) % 4.  Columns past K (the zero-filled half of a K % 128 == 64 tile)
+// store only their scale bytes, as zeros: the contract's padding.
+__device__ __forceinline__ uint8_t* col_scale_at(const QuantArgs& a, int64_t kk, int64_t m16) {
+  return a.col_scale + ((kk >> 7) * (a.M >> 6) + (m16 >> 2)) * 512 + (kk & 31) * 16 + ((kk & 127) >> 5) * 4 + (m16 & 3);
+}
+
+// bf16 tiles: warp w owns column pairs 32 (w % 2) + lane and the 32 rows 32 (w / 2) .. +31 (two
+// units), so each of its two columns gets one 16-byte run and one 2-byte run of scales.
+template <int HADM, bool SR>
+__device__ __forceinline__ void col_part_bf16(uint32_t tile, const uint32_t (&sgn)[16], const QCtx& c,
+                                              const QuantArgs& a, int64_t m0, int64_t k0, int valid_cols) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int ch = w & 1, q = w >> 1;
+  const int cp = 32 * ch + lane;
+  const uint32_t base = tile + ch * kQBoxBytes + 32 * q * 128 + (((lane >> 2) & 7) << 4) + ((lane & 3) << 2);
+  uint32_t bk[8];
 #pragma unroll
-  for (int item = t; item < kCols * 4; item += kQThreads) {
-    const int kk = item >> 2, p = item & 3;  // output row k0 + kk, bytes 16p .. 16p+15
-    if (kk < valid_cols) {
-      const uint2 lo = lds64(stage_pk + (2 * p) * 1024 + ((kk ^ (8 * p)) << 3));
-      const uint2 hi = lds64(stage_pk + (2 * p + 1) * 1024 + ((kk ^ (8 * p + 4)) << 3));
-      st_global_v4(a.col_packed + (k0 + kk) * (a.M >> 1) + (m0 >> 1) + 16 * p, lo.x, lo.y, hi.x, hi.y);
+  for (int k = 0; k < 8; ++k) bk[k] = base ^ (uint32_t)(k << 4);
+  const int64_t kk = k0 + 2 * cp;
+  const bool valid = 2 * cp < valid_cols;
+  uint8_t* px = a.col_packed + kk * (a.M >> 1) + (m0 >> 1) + 16 * q;
+  const ColOut u0 = col_unit<false, HADM, SR>(bk, 0, sgn, c, a, m0, k0, cp, 2 * q);
+  if constexpr (HADM == 2) {  // the general rotation: store each unit at once (fewer live registers)
+    if (valid) {
+      st_global_v2(px, u0.wx0, u0.wx1);
+      st_global_v2(px + (a.M >> 1), u0.wy0, u0.wy1);
     }
   }
-  const int64_t atom0 = (k0 >> 7) * (a.M >> 6) + 2 * mt;
-  if constexpr (!F32IN) {
-    if (t < 64) {  // two whole 512-byte atoms, 16 bytes per thread
-      const int at = t >> 5, off = (t & 31) * 16;
-      const uint4 s = lds128(stage_sc + at * 512 + off);
-      st_global_v4(a.col_scale + (atom0 + at) * 512 + off, s.x, s.y, s.z, s.w);
+  const ColOut u1 = col_unit<false, HADM, SR>(bk, 16 * 128, sgn, c, a, m0, k0, cp, 2 * q + 1);
+  if (valid) {
+    if constexpr (HADM == 2) {
+      st_global_v2(px + 8, u1.wx0, u1.wx1);
+      st_global_v2(px + (a.M >> 1) + 8, u1.wy0, u1.wy1);
+    } else {
+      st_global_v4(px, u0.wx0, u0.wx1, u1.wx0, u1.wx1);
+      st_global_v4(px + (a.M >> 1), u0.wy0, u0.wy1, u1.wy0, u1.wy1);
     }
-  } else {
-    if (t < 64) {  // the tile's 8-byte half of each 16-byte atom row
-      const int at = t >> 5, r = t & 31, half = (k0 & 64) ? 8 : 0;
-      const uint2 s = lds64(stage_sc + at * 512 + r * 16 + half);
-      st_global_v2(a.col_scale + (atom0 + at) * 512 + r * 16 + half, s.x, s.y);
-    }
-    // A K that is not a multiple of 128 ends on a 64-column tile whose atoms' other halves are
-    // padding rows: they must read as zero.
-    if ((a.K & 127) != 0 && (k0 >> 6) == (a.K >> 6) - 1 && t >= 64 && t < 128) {
-      const int u = t - 64;
-      st_global_v2(a.col_scale + (atom0 + (u >> 5)) * 512 + (u & 31) * 16 + 8, 0u, 0u);
-    }
+  }
+  const int64_t m16 = (m0 >> 4) + 2 * q;
+  *reinterpret_cast<uint16_t*>(col_scale_at(a, kk, m16)) = valid ? (uint16_t)(u0.bx | (u1.bx << 8)) : (uint16_t)0;
+  *reinterpret_cast<uint16_t*>(col_scale_at(a, kk + 1, m16)) = valid ? (uint16_t)(u0.by | (u1.by << 8)) : (uint16_t)0;
+}
+
+// fp32 tiles (32 column pairs): warp w owns rows 16w..16w+15 of pair `lane` (one unit).
+template <int HADM, bool SR>
+__device__ __forceinline__ void col_part_f32(uint32_t tile, const uint32_t (&sgn)[16], const QCtx& c,
+                                             const QuantArgs& a, int64_t m0, int64_t k0) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const uint32_t base = tile + (lane >> 4) * kQBoxBytes + 16 * w * 128 + (((lane & 15) >> 1) << 4) + ((lane & 1) << 3);
+  uint32_t bk[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) bk[k] = base ^ (uint32_t)(k << 4);
+  const ColOut u = col_unit<true, HADM, SR>(bk, 0, sgn, c, a, m0, k0, lane, w);
+  const int64_t kk = k0 + 2 * lane;
+  uint8_t* px = a.col_packed + kk * (a.M >> 1) + (m0 >> 1) + 8 * w;
+  st_global_v2(px, u.wx0, u.wx1);
+  st_global_v2(px + (a.M >> 1), u.wy0, u.wy1);
+  const int64_t m16 = (m0 >> 4) + w;
+  *col_scale_at(a, kk, m16) = (uint8_t)u.bx;
+  *col_scale_at(a, kk + 1, m16) = (uint8_t)u.by;
+  // K % 128 == 64: the last 64-column tile also zeroes the padding rows kk + 64 of its atoms.
+  if ((a.K & 127) != 0 && k0 + 64 == a.K) {
+    *col_scale_at(a, kk + 64, m16) = 0;
+    *col_scale_at(a, kk + 65, m16) = 0;
   }
 }
 
@@ -643,8 +671,7 @@ __device__ __forceinline__ void quant_loop(const CUtensorMap& tmap, const QuantA
                                            QCtx& c, uint32_t cur_gs, int n_my) {
   constexpr int S = kQStages;
   constexpr int kCols = QTile<F32IN>::kCols;
-  const int tid = threadIdx.x, lane = tid & 31, g = tid >> 5;
-  const uint32_t stage_pk = smem_u32(hdr->stage_pk), stage_sc = smem_u32(hdr->stage_sc);
+  const int tid = threadIdx.x;
   uint32_t sgn[16];
 #pragma unroll
   for (int j = 0; j < 16; ++j) sgn[j] = (HADM == 1) ? hdr->sign_word[j] : 0u;
@@ -652,8 +679,7 @@ __device__ __forceinline__ void quant_loop(const CUtensorMap& tmap, const QuantA
   for (int it = 0; it < n_my; ++it) {
     const int s = it % S;
     const bool ok = mbar_wait(&hdr->full[s], (uint32_t)((it / S) & 1));
-    // Every thread has finished tile it-1 once past this barrier, so its stage may be refilled
-    // and the colblock staging area reused.
+    // Every thread has finished tile it-1 once past this barrier, so its stage may be refilled.
     if (__syncthreads_or(!ok)) {
       if (tid == 0) record_status(&g_quant_status, kStatusTimeoutTma);
       return;
@@ -676,20 +702,8 @@ __device__ __forceinline__ void quant_loop(const CUtensorMap& tmap, const QuantA
     }
     const uint32_t tile = smem_u32(smem + (size_t)s * kQTileBytes);
     if constexpr (DO_COL) {
-      // Unit base: box (cp / pairs-per-box), row 16g, the pair's 16-byte chunk and offset in it.
-      uint32_t base;
-      if constexpr (!F32IN) {
-        base = tile + 16 * g * 128 + (((lane >> 2) & 7) << 4) + ((lane & 3) << 2);
-      } else {
-        base = tile + (lane >> 4) * kQBoxBytes + 16 * g * 128 + (((lane & 15) >> 1) << 4) + ((lane & 1) << 3);
-      }
-      uint32_t bk[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) bk[k] = base ^ (uint32_t)(k << 4);
-      col_unit<F32IN, HADM, SR>(bk, 0, sgn, c, a, m0, k0, lane, 2 * lane < valid_cols, stage_pk, stage_sc);
-      if constexpr (!F32IN)
-        col_unit<F32IN, HADM, SR>(bk, kQBoxBytes, sgn, c, a, m0, k0, lane + 32, 2 * (lane + 32) < valid_cols,
-                                  stage_pk, stage_sc);
+      if constexpr (!F32IN) col_part_bf16<HADM, SR>(tile, sgn, c, a, m0, k0, valid_cols);
+      else col_part_f32<HADM, SR>(tile, sgn, c, a, m0, k0);
     }
     if constexpr (DO_ROW) {
       const int r = tid & 127, h = tid >> 7;
@@ -698,10 +712,6 @@ __device__ __forceinline__ void quant_loop(const CUtensorMap& tmap, const QuantA
 #pragma unroll
       for (int k = 0; k < 8; ++k) rk[k] = rb ^ (uint32_t)(k << 4);
       row_part<F32IN, SR>(rk, c, a, m0, k0, mt, (F32IN ? 32 : 64) * h < valid_cols);
-    }
-    if constexpr (DO_COL) {
-      __syncthreads();
-      col_store<F32IN>(a, m0, k0, mt, valid_cols, stage_pk, stage_sc);
     }
   }
 }
