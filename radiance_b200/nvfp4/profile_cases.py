@@ -6,12 +6,15 @@ between and exits, so a profiler can skip and capture launches by count:
     python -m radiance_b200.nvfp4.profile_cases quant --rows 16384 --cols 6144 --hadamard --sr
         one fused quantization (rowblock + colblock) per iteration
     python -m radiance_b200.nvfp4.profile_cases gemm --m 16384 --n 6144 --k 2048
-        one block-scaled GEMM (bf16 out) per iteration
+        one block-scaled GEMM (bf16 out) per iteration; ``--impl cublas`` runs cuBLASLt's NVFP4
+        GEMM (torch._scaled_mm_v2) on the same operands instead, for comparison
     python -m radiance_b200.nvfp4.profile_cases block-gemms
         the twelve GEMMs of one config-3 block step (four linears x fwd, dgrad, wgrad) per
         iteration, with the operand shapes and output types ``FP4Linear`` uses
 
-Inputs are seeded synthetic tensors (activations ~N(0, 1), weights ~N(0, 0.02)).
+Inputs are seeded synthetic tensors (activations ~N(0, 1), weights ~N(0, 0.02)).  The iterations
+run between cudaProfilerStart and cudaProfilerStop, so ``ncu --profile-from-start off`` captures
+only them (not the operand preparation).
 """
 
 from __future__ import annotations
@@ -38,10 +41,12 @@ def _quant_case(args, dev):
            torch.empty(col_scale_bytes(args.rows, args.cols), dtype=torch.uint8, device=dev))
     form = args.form
     torch.cuda.synchronize()
+    torch.cuda.profiler.start()
     for _ in range(args.iters):
         quantize_into_(x, global_scale=gs, row=row if form in ("row", "both") else None,
                        col=col if form in ("col", "both") else None, hadamard=h, stochastic=args.sr, seed=seed)
     torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
 
 
 def _operands(m, n, k, dev, g, a_scale=1.0, b_scale=0.02):
@@ -54,11 +59,25 @@ def _gemm_case(args, dev):
     g = torch.Generator(device="cpu").manual_seed(11)
     a, b = _operands(args.m, args.n, args.k, dev, g)
     out = torch.empty(args.m, args.n, dtype=torch.bfloat16, device=dev)
+    if args.impl == "cublas":
+        from torch._C import _ScalingType, _SwizzleType
+
+        blk = [_ScalingType.BlockWise1x16.value]
+        swz = [_SwizzleType.SWIZZLE_32_4_4.value]
+
+        def run():
+            torch._scaled_mm_v2(a.packed, b.packed.t(), scale_a=[a.scale], recipe_a=blk, swizzle_a=swz,
+                                scale_b=[b.scale], recipe_b=blk, swizzle_b=swz, bias=None, out_dtype=torch.bfloat16)
+    else:
+        def run():
+            _gemm(a.packed.view(torch.uint8), a.scale.view(torch.uint8), b.packed.view(torch.uint8),
+                  b.scale.view(torch.uint8), a.global_scale, b.global_scale, None, torch.bfloat16, out)
     torch.cuda.synchronize()
+    torch.cuda.profiler.start()
     for _ in range(args.iters):
-        _gemm(a.packed.view(torch.uint8), a.scale.view(torch.uint8), b.packed.view(torch.uint8),
-              b.scale.view(torch.uint8), a.global_scale, b.global_scale, None, torch.bfloat16, out)
+        run()
     torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
 
 
 def _block_gemms_case(args, dev):
@@ -74,11 +93,13 @@ def _block_gemms_case(args, dev):
             out = torch.empty(m_, n_, dtype=out_dtype, device=dev)
             calls.append((a, b, out, out_dtype))
     torch.cuda.synchronize()
+    torch.cuda.profiler.start()
     for _ in range(args.iters):
         for a, b, out, out_dtype in calls:
             _gemm(a.packed.view(torch.uint8), a.scale.view(torch.uint8), b.packed.view(torch.uint8),
                   b.scale.view(torch.uint8), a.global_scale, b.global_scale, None, out_dtype, out)
     torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
 
 
 def main(argv=None):
@@ -96,6 +117,7 @@ def main(argv=None):
     pg.add_argument("--n", type=int, default=6144)
     pg.add_argument("--k", type=int, default=2048)
     pg.add_argument("--iters", type=int, default=3)
+    pg.add_argument("--impl", choices=["ours", "cublas"], default="ours")
     pb = sub.add_parser("block-gemms")
     pb.add_argument("--tokens", type=int, default=16384)
     pb.add_argument("--iters", type=int, default=2)
