@@ -79,6 +79,18 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   return true;
 }
 
+// As mbar_wait, sleeping ~`ns` nanoseconds between polls: for long waits of warps that share a
+// scheduler with a latency-critical warp (the GEMM's epilogue warps beside its MMA issuer).
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long start = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - start > kWaitLimitCycles) return false;
+    __nanosleep(ns);
+  }
+  return true;
+}
+
 // ----------------------------------------------------------------------------------------------
 // TMA (no multicast anywhere in this library)
 // ----------------------------------------------------------------------------------------------

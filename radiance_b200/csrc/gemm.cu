@@ -452,7 +452,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int width = (int)min((int64_t)kBN, g.N - (int64_t)nt * kBN);
       const int buf = i & 1;
       const int base_col = buf ? kAcc1Col : 0;
-      if (!mbar_wait(&sm.acc_full, (uint32_t)(i & 1))) {
+      if (!mbar_wait_sleep(&sm.acc_full, (uint32_t)(i & 1), 64)) {
         record_status(&g_gemm_status, kStatusTimeoutMma);
         break;
       }
@@ -812,7 +812,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (g.alpha_b != nullptr) alpha = __fmul_rn(alpha, __ldg(g.alpha_b + T.group));
       const int buf = i & 1;
       const int base_col = buf ? kAcc1Col : 0;
-      if (!mbar_wait(&sm.acc_full, (uint32_t)(i & 1))) {
+      if (!mbar_wait_sleep(&sm.acc_full, (uint32_t)(i & 1), 64)) {
         record_status(&g_gemm_status, kStatusTimeoutMma);
         break;
       }
