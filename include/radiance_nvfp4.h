@@ -55,7 +55,9 @@ int rb_nvfp4_abi_version(void);
 
 /*
  * First non-zero status recorded by any kernel of this library on the current device since the
- * last clear (a bounded device-side wait that ran out); 0 if none.  Synchronises the device.
+ * last clear; 0 if none.  Synchronises the device.  Codes: 1-4 a bounded device-side wait ran out
+ * (TMA data, MMA completion, accumulator hand-off, free pipeline stage); 5 a grouped-GEMM record
+ * broke its contract; 6 the GEMM's whole-TMEM allocation did not start at address 0.
  * Test and debugging aid; no counterpart in the reference.
  */
 int rb_nvfp4_device_status(int clear);

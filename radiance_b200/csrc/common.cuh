@@ -27,6 +27,7 @@ enum : uint32_t {
   kStatusTimeoutEpilogue = 3,  // the epilogue waited too long for the accumulator
   kStatusTimeoutProducer = 4,  // a producer waited too long for a free stage
   kStatusBadGroup = 5,         // a grouped-GEMM group descriptor broke the contract (group skipped)
+  kStatusTmemBase = 6,         // a whole-TMEM allocation did not start at address 0 (GEMM skipped)
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

@@ -311,7 +311,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   GemmSmem& sm = *reinterpret_cast<GemmSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_my = ((int)blockIdx.x < g.n_tiles) ? (g.n_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -333,7 +332,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = sm.tmem_base;
+  // A 512-column allocation is all of the SM's tensor memory, so it starts at address 0.  Using
+  // the constant (with every descriptor derived from constants and the stage index) keeps the
+  // operands of the tcgen05 instructions in uniform registers, which the issue rate depends on.
+  // An allocation anywhere else is reported (status 6) and the CTA computes nothing.
+  constexpr uint32_t tmem = 0;
+  const bool tmem_ok = sm.tmem_base == 0;
+  if (!tmem_ok && threadIdx.x == 0) record_status(&g_gemm_status, kStatusTmemBase);
+  const int n_my = (tmem_ok && (int)blockIdx.x < g.n_tiles)
+                       ? (g.n_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
 
   if (warp == 0) {
     // ------------------------------------------------------------------ producer
@@ -383,6 +390,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      const uint64_t ad0 = sdesc_sw128(smem_u32(sm.a[0])), bd0 = sdesc_sw128(smem_u32(sm.b[0]));
+      const uint64_t sad0 = sdesc_scale(smem_u32(sm.sfa[0])), sbd0 = sdesc_scale(smem_u32(sm.sfb[0]));
       for (int i = 0; i < n_my && ok; ++i) {
         int mt, nt;
         tile_coords((int)blockIdx.x + i * (int)gridDim.x, g.tiles_m, g.tiles_n, mt, nt);
@@ -398,13 +407,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             break;
           }
           const int nkb = min(4, g.k_blocks - 4 * ks);
-          const uint32_t sfa_s = smem_u32(sm.sfa[stage]), sfb_s = smem_u32(sm.sfb[stage]);
-          const uint32_t a_s = smem_u32(sm.a[stage]), b_s = smem_u32(sm.b[stage]);
-          auto copy_scales = [&](int kb) {
-            tc_cp_scale(tmem + kSfaCol + 4 * kb, sdesc_scale(sfa_s + kb * 512));
-            tc_cp_scale(tmem + kSfbCol + 8 * kb, sdesc_scale(sfb_s + kb * 512));
-            if (width > 128) tc_cp_scale(tmem + kSfbCol + 8 * kb + 4, sdesc_scale(sfb_s + (4 + kb) * 512));
-          };
+          // Descriptors of this stage: the address field holds bytes >> 4.
+          const uint64_t ad = ad0 + (uint64_t)(stage * ((kBM * kStepBytes) >> 4));
+          const uint64_t bd = bd0 + (uint64_t)(stage * ((kBN * kStepBytes) >> 4));
+          const uint64_t sad = sad0 + (uint64_t)(stage * ((4 * 512) >> 4));
+          const uint64_t sbd = sbd0 + (uint64_t)(stage * ((8 * 512) >> 4));
           if (ks == 0 && i >= 1) {
             if (!mbar_wait_warp(&sm.acc_empty, (uint32_t)((i - 1) & 1))) {
               if (lane == 0) record_status(&g_gemm_status, kStatusTimeoutEpilogue);
@@ -417,10 +424,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             // An MMA starts only after every scale copy issued before it has landed, so each K
             // block's copies go directly before its own MMA (all copies of a step first costs ~20%,
             // copies one block ahead cost more, not less).
-            for (int kb = 0; kb < nkb; ++kb) {
-              copy_scales(kb);
-              tc_mma_nvf4(acc, sdesc_sw128(a_s + 32 * kb), sdesc_sw128(b_s + 32 * kb), idesc, tmem + kSfaCol + 4 * kb,
-                          tmem + kSfbCol + 8 * kb, (ks > 0 || kb > 0) ? 1u : 0u);
+#pragma unroll
+            for (int kb = 0; kb < 4; ++kb) {
+              if (kb < nkb) {
+                tc_cp_scale(tmem + kSfaCol + 4 * kb, sad + 32 * kb);
+                tc_cp_scale(tmem + kSfbCol + 8 * kb, sbd + 32 * kb);
+                if (width > 128) tc_cp_scale(tmem + kSfbCol + 8 * kb + 4, sbd + 32 * (4 + kb));
+                tc_mma_nvf4(acc, ad + 2 * kb, bd + 2 * kb, idesc, tmem + kSfaCol + 4 * kb, tmem + kSfbCol + 8 * kb,
+                            (ks > 0 || kb > 0) ? 1u : 0u);
+              }
             }
             tc_commit(&sm.empty[stage]);
           }
@@ -486,7 +498,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem, 512);
+  if (warp == 1) tmem_dealloc(sm.tmem_base, 512);
 }
 
 
@@ -700,9 +712,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_before();
   cluster_sync();
   tc_fence_after();
-  const uint32_t tmem = sm.tmem_base;
+  // A 512-column allocation is all of the SM's tensor memory (the same columns in both CTAs of the
+  // pair), so it starts at address 0.  Using the constant (with every descriptor derived from
+  // constants and the stage index) keeps the operands of the tcgen05 instructions in uniform
+  // registers, which the issue rate depends on (~10% of GEMM throughput).  An allocation anywhere
+  // else is reported (status 6) and the pair computes nothing.
+  constexpr uint32_t tmem = 0;
+  const bool tmem_ok = sm.tmem_base == 0;
+  if (!tmem_ok && threadIdx.x == 0) record_status(&g_gemm_status, kStatusTmemBase);
   const int n_tiles = (g.groups == nullptr) ? g.n_tiles : sm.tile_prefix[g.num_groups];
-  const int n_my = (cid < n_tiles) ? (n_tiles - cid + ncl - 1) / ncl : 0;  // 256x256 tiles of this pair
+  const int n_my = (tmem_ok && cid < n_tiles) ? (n_tiles - cid + ncl - 1) / ncl : 0;  // 256x256 tiles of this pair
 
   if (warp == 0) {
     // ------------------------------------------------------------------ producer (both CTAs)
@@ -749,6 +768,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      const uint64_t ad0 = sdesc_sw128(smem_u32(sm.a[0])), bd0 = sdesc_sw128(smem_u32(sm.b[0]));
+      const uint64_t sad0 = sdesc_scale(smem_u32(sm.sfa[0])), sbd0 = sdesc_scale(smem_u32(sm.sfb[0]));
       for (int i = 0; i < n_my && ok; ++i) {
         const Tile2 T = tile2_at(cid + i * ncl, g, sm.tile_prefix);
         const int width = T.width;
@@ -769,19 +790,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             break;
           }
           const int nkb = min(4, T.k_blocks - 4 * ks);
-          const uint32_t sfa_s = smem_u32(sm.sfa[stage]), sfb_s = smem_u32(sm.sfb[stage]);
-          const uint32_t a_s = smem_u32(sm.a[stage]), b_s = smem_u32(sm.b[stage]);
-          auto copy_scales = [&](int kb) {
-            tc_cp_scale2(tmem + kSfaCol + 4 * kb, sdesc_scale(sfa_s + kb * 512));
-            tc_cp_scale2(tmem + kSfbCol + 8 * kb, sdesc_scale(sfb_s + kb * 512));
-            if (width > 128) tc_cp_scale2(tmem + kSfbCol + 8 * kb + 4, sdesc_scale(sfb_s + kSfStep + kb * 512));
-          };
+          // Descriptors of this stage: the address field holds bytes >> 4.
+          const uint64_t ad = ad0 + (uint64_t)(stage * ((kBM * kStepBytes) >> 4));
+          const uint64_t bd = bd0 + (uint64_t)(stage * ((kBM * kStepBytes) >> 4));
+          const uint64_t sad = sad0 + (uint64_t)(stage * (kSfStep >> 4));
+          const uint64_t sbd = sbd0 + (uint64_t)(stage * ((2 * kSfStep) >> 4));
           if (elect_one()) {
             // As in the one-SM kernel, each K block's scale copies directly precede its MMA.
-            for (int kb = 0; kb < nkb; ++kb) {
-              copy_scales(kb);
-              tc_mma_nvf4_2sm(acc, sdesc_sw128(a_s + 32 * kb), sdesc_sw128(b_s + 32 * kb), idesc,
-                              tmem + kSfaCol + 4 * kb, tmem + kSfbCol + 8 * kb, (ks > 0 || kb > 0) ? 1u : 0u);
+#pragma unroll
+            for (int kb = 0; kb < 4; ++kb) {
+              if (kb < nkb) {
+                tc_cp_scale2(tmem + kSfaCol + 4 * kb, sad + 32 * kb);
+                tc_cp_scale2(tmem + kSfbCol + 8 * kb, sbd + 32 * kb);
+                if (width > 128) tc_cp_scale2(tmem + kSfbCol + 8 * kb + 4, sbd + ((kSfStep + kb * 512) >> 4));
+                tc_mma_nvf4_2sm(acc, ad + 2 * kb, bd + 2 * kb, idesc, tmem + kSfaCol + 4 * kb, tmem + kSfbCol + 8 * kb,
+                                (ks > 0 || kb > 0) ? 1u : 0u);
+              }
             }
             tc_commit2(&sm.empty[stage], 0x3);
           }
@@ -855,7 +879,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_before();
   cluster_sync();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc2(tmem, 512);
+  if (warp == 1) tmem_dealloc2(sm.tmem_base, 512);
 }
 
 }  // namespace rb
