@@ -6,6 +6,7 @@ everything on the hot path; the reference's pure-torch emulation (``quantize_ref
 ``ref_*`` helpers) defines the format and stays in radiance.
 """
 
+from .grouped import bmm
 from .linear import FP4Linear, FP4Recipe, refresh_fp4_weights
 from .quantize import (
     BLOCK,
@@ -43,6 +44,7 @@ __all__ = [
     "FP4Linear",
     "FP4Recipe",
     "blocked_offset",
+    "bmm",
     "col_scale_bytes",
     "global_scale_of",
     "hadamard_matrix",

@@ -203,6 +203,49 @@ def grouped_mm(
     return out if native == out_dtype else out.to(out_dtype)
 
 
+MAX_GROUPS = 256  # groups per rb_nvfp4_gemm_grouped launch
+_BMM_RECORDS: dict[tuple, torch.Tensor] = {}
+
+
+def bmm(a, b, batch: int, *, out_dtype: torch.dtype = torch.bfloat16, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Batched NVFP4 GEMM: ``out[i] = a[i] @ b[i].T`` for ``i < batch``, as one grouped launch per
+    256 batch entries.
+
+    radiance keeps attention's ``Q @ K^T`` and ``attn @ V`` in bf16 because ``torch._scaled_mm_v2``
+    is two-dimensional only (docs/results.md:287-293); the grouped tcgen05 GEMM has no such limit.
+    ``a`` and ``b`` are rowblock ``NVFP4Tensor``s of the stacked ``(batch * M, K)`` and
+    ``(batch * N, K)`` operands, each quantized as one tensor (one global scale);
+    M and N must be multiples of 128 and K of 64.  Returns ``(batch, M, N)``.
+    """
+    a_packed, b_packed = a.packed.view(torch.uint8), b.packed.view(torch.uint8)
+    _require_cuda(a_packed, "nvfp4.bmm")
+    rows_a, rows_b = a_packed.shape[0], b_packed.shape[0]
+    if batch < 1 or rows_a % batch or rows_b % batch:
+        raise ValueError(f"nvfp4.bmm: {rows_a} and {rows_b} rows do not split into {batch} batch entries")
+    m, n, k = rows_a // batch, rows_b // batch, a_packed.shape[1] * 2
+    if m % 128 or n % 128 or k % 64 or b_packed.shape[1] * 2 != k:
+        raise ValueError(f"nvfp4.bmm needs M % 128 == 0, N % 128 == 0 and a shared K % 64 == 0, got M={m}, "
+                         f"N={n}, K={k} and {b_packed.shape[1] * 2}")
+    dev = a_packed.device
+    native = out_dtype if out_dtype in _OUT_CODES else torch.float32
+    if out is None:
+        out = torch.empty(batch * m, n, dtype=native, device=dev)
+    for start in range(0, batch, MAX_GROUPS):
+        cnt = min(MAX_GROUPS, batch - start)
+        key = (dev, start, cnt, m, n, k)
+        recs = _BMM_RECORDS.get(key)
+        if recs is None:
+            g = torch.arange(start, start + cnt, dtype=torch.int64)
+            recs = torch.stack([g * m, g * n, g * m, torch.full_like(g, m), torch.zeros_like(g),
+                                torch.full_like(g, k)], dim=1).to(dev)
+            _BMM_RECORDS[key] = recs
+        grouped_mm((a_packed, a.scale.view(torch.uint8)), (b_packed, b.scale.view(torch.uint8)), recs, n=n,
+                   k_total=k, out_rows=batch * m, alpha_a=a.global_scale.reshape(1).expand(cnt),
+                   alpha_b=b.global_scale.reshape(1).expand(cnt), out_dtype=native, out=out)
+    out = out.view(batch, m, n)
+    return out if native == out_dtype else out.to(out_dtype)
+
+
 def groups_over_rows(offsets: torch.Tensor, b_rows_per_group: int, k: int) -> torch.Tensor:
     """Group records for a forward or dgrad GEMM: group g multiplies token rows
     ``offsets[g]:offsets[g+1]`` by expert operand rows ``g * b_rows_per_group ...`` over the full
