@@ -24,6 +24,7 @@
 #ifndef RADIANCE_NVFP4_H_
 #define RADIANCE_NVFP4_H_
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -151,6 +152,23 @@ int rb_nvfp4_gemm_allgather(const void* a_packed, const void* a_scale, const voi
                             int64_t m, int64_t n, int64_t k, const float* alpha_a, const float* alpha_b,
                             const void* bias, int bias_dtype, void* out, int out_dtype, int64_t ldo,
                             void* const* peer_out, int npeers, void* stream);
+
+/*
+ * Global scale and column sums of x in one read: *gs_out as rb_nvfp4_global_scale computes it, and
+ * colsum_out[c] = sum over rows of x[r, c] (fp32 accumulation in a fixed order, so repeated calls
+ * agree bit for bit).  For the upstream gradient of a linear with a bias, whose quantization needs
+ * gs and whose bias gradient is dY.sum(0) (linear.py:146-147 in jamespa16/radiance: a separate torch
+ * reduction there, a second full read of dY).
+ *   x          : rows x cols of `dtype`, row stride ld elements; 16-byte aligned base, cols*elemsize
+ *                and ld*elemsize multiples of 16.
+ *   colsum_out : device fp32[cols].
+ *   workspace  : rb_nvfp4_global_scale_colsum_workspace(dtype, rows, cols) bytes, 16-byte aligned;
+ *                its first 16 bytes zeroed before the first call (every call leaves them zeroed
+ *                again, so calls ordered on one stream can share it).
+ */
+size_t rb_nvfp4_global_scale_colsum_workspace(int dtype, int64_t rows, int64_t cols);
+int rb_nvfp4_global_scale_colsum(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld, float* gs_out,
+                                 float* colsum_out, void* workspace, void* stream);
 
 /*
  * Grouped (mixture-of-experts) GEMMs, global scales and quantization.  radiance runs its experts

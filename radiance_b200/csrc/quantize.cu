@@ -933,6 +933,92 @@ __global__ void __launch_bounds__(256) global_scale_grouped_kernel(const void* x
   }
 }
 
+// Global scale and column sums in one read (the upstream gradient of a linear with a bias needs
+// both: gs for its quantization and dY.sum(0) for the bias gradient, linear.py:146).  Block
+// (bx, by) covers the column chunk bx (8 bf16 or 4 fp32 columns per thread, one 16-byte load per
+// row) over the row range by; each thread keeps its columns' fp32 sums in registers and writes
+// them to partial-sum row `by` of the workspace.  The maximum goes through ws[0] and the last
+// block finalizes gs as global_scale_kernel does; colsum_finish_kernel then adds the partial rows
+// in order, so the sums are deterministic.
+template <bool F32IN>
+__global__ void __launch_bounds__(256) global_scale_colsum_kernel(const void* x, int64_t rows, int64_t cols,
+                                                                  int64_t ld, int64_t rows_per_block, uint32_t* ws,
+                                                                  float* partial, float* gs_out) {
+  constexpr int kPer = F32IN ? 4 : 8;
+  const int64_t c0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * kPer;
+  const int64_t r0 = (int64_t)blockIdx.y * rows_per_block;
+  const int64_t r1 = min(rows, r0 + rows_per_block);
+  float acc[kPer];
+#pragma unroll
+  for (int e = 0; e < kPer; ++e) acc[e] = 0.0f;
+  uint32_t m = 0;
+  if (c0 < cols) {
+    const size_t esize = F32IN ? 4 : 2;
+    const uint8_t* base = reinterpret_cast<const uint8_t*>(x) + (size_t)c0 * esize;
+    const size_t pitch = (size_t)ld * esize;
+    int64_t r = r0;
+    auto add = [&](const uint4 v) {
+      if constexpr (F32IN) {
+        acc[0] += __uint_as_float(v.x); acc[1] += __uint_as_float(v.y);
+        acc[2] += __uint_as_float(v.z); acc[3] += __uint_as_float(v.w);
+        m = max(m, max(max(v.x & 0x7FFFFFFFu, v.y & 0x7FFFFFFFu), max(v.z & 0x7FFFFFFFu, v.w & 0x7FFFFFFFu)));
+      } else {
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          acc[2 * q] += __uint_as_float(w[q] << 16);
+          acc[2 * q + 1] += __uint_as_float(w[q] & 0xFFFF0000u);
+        }
+        m = __vmaxu2(m, __vmaxu2(__vmaxu2(v.x & 0x7FFF7FFFu, v.y & 0x7FFF7FFFu), __vmaxu2(v.z & 0x7FFF7FFFu, v.w & 0x7FFF7FFFu)));
+      }
+    };
+    for (; r + 4 <= r1; r += 4) {
+      uint4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[u] = __ldg(reinterpret_cast<const uint4*>(base + (size_t)(r + u) * pitch));
+#pragma unroll
+      for (int u = 0; u < 4; ++u) add(v[u]);
+    }
+    for (; r < r1; ++r) add(__ldg(reinterpret_cast<const uint4*>(base + (size_t)r * pitch)));
+    float* out = partial + (size_t)blockIdx.y * (size_t)cols + c0;
+#pragma unroll
+    for (int e = 0; e < kPer; ++e) out[e] = acc[e];
+  }
+  if constexpr (!F32IN) m = max(m & 0xFFFFu, m >> 16) << 16;  // bf16 bits -> fp32 bits
+  m = __reduce_max_sync(0xFFFFFFFFu, m);
+  __shared__ uint32_t red[8];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = m;
+  __syncthreads();
+  if (warp == 0) {
+    m = lane < (int)(blockDim.x >> 5) ? red[lane] : 0u;
+    m = __reduce_max_sync(0xFFFFFFFFu, m);
+    if (lane == 0) {
+      atomicMax(&ws[0], m);
+      __threadfence();
+      const uint32_t ticket = atomicAdd(&ws[1], 1u);
+      if (ticket == gridDim.x * gridDim.y - 1) {
+        __threadfence();
+        const uint32_t mb = atomicExch(&ws[0], 0u);
+        atomicExch(&ws[1], 0u);
+        float gs = __fdiv_rn(__uint_as_float(mb), 2688.0f);
+        gs = (gs < 1e-12f) ? 1e-12f : gs;
+        *gs_out = gs;
+      }
+    }
+  }
+}
+
+// colsum[c] = sum over the partial-sum rows y = 0 .. nparts-1 of partial[y][c], in that order.
+__global__ void __launch_bounds__(256) colsum_finish_kernel(const float* partial, int64_t nparts, int64_t cols,
+                                                            float* colsum) {
+  const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= cols) return;
+  float s = 0.0f;
+  for (int64_t y = 0; y < nparts; ++y) s += partial[y * cols + c];
+  colsum[c] = s;
+}
+
 __global__ void fill_float_kernel(float* p, float v) { *p = v; }
 
 __global__ void selftest_division_kernel(const float* x, const float* d, int64_t n, uint32_t* mismatches) {
@@ -1180,6 +1266,68 @@ int rb_nvfp4_quantize_grouped(const void* x, int dtype, int64_t rows, int64_t co
   }
   return quantize_impl(x, dtype, rows, cols, ld, group_gs, offsets, num_groups, hadamard, seed, row_packed,
                        row_scale, col_packed, col_scale, stream);
+}
+
+// Row splits of global_scale_colsum_kernel for a launch of `gx` column chunks: enough blocks to
+// fill the GPU four times over, and at most one per row.
+static int64_t colsum_parts(int64_t rows, int64_t gx) {
+  const int64_t want = (4 * (int64_t)rb_host::num_sms(rb_host::current_device()) + gx - 1) / gx;
+  return max((int64_t)1, min(rows, want));
+}
+
+size_t rb_nvfp4_global_scale_colsum_workspace(int dtype, int64_t rows, int64_t cols) {
+  if (rows <= 0 || cols <= 0) return 16;
+  const int64_t per_block = (dtype == RB_DTYPE_F32 ? 4 : 8) * 256;
+  const int64_t gx = (cols + per_block - 1) / per_block;
+  return 16 + (size_t)colsum_parts(rows, gx) * (size_t)cols * sizeof(float);
+}
+
+int rb_nvfp4_global_scale_colsum(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld, float* gs_out,
+                                 float* colsum_out, void* workspace, void* stream) {
+  if (x == nullptr || gs_out == nullptr || colsum_out == nullptr || workspace == nullptr) {
+    rb_host::set_error("nvfp4 global_scale_colsum: null pointer argument");
+    return RB_ERR_ARG;
+  }
+  if (dtype != RB_DTYPE_BF16 && dtype != RB_DTYPE_F32) {
+    rb_host::set_error("nvfp4 global_scale_colsum: unsupported dtype %d", dtype);
+    return RB_ERR_ARG;
+  }
+  const int esize = dtype == RB_DTYPE_BF16 ? 2 : 4;
+  if (rows <= 0 || cols <= 0 || ld < cols || (cols * esize) % 16 != 0 || ((uint64_t)ld * esize) % 16 != 0 ||
+      (reinterpret_cast<uintptr_t>(x) & 15) != 0 || (reinterpret_cast<uintptr_t>(workspace) & 15) != 0) {
+    rb_host::set_error("nvfp4 global_scale_colsum: needs 16-byte aligned rows of a multiple of 16 bytes and a "
+                       "16-byte aligned workspace (rows=%lld cols=%lld ld=%lld)", (long long)rows, (long long)cols,
+                       (long long)ld);
+    return RB_ERR_SHAPE;
+  }
+  if (!device_is_sm100()) {
+    rb_host::set_error("nvfp4 global_scale_colsum: the current device is not an sm_100 GPU");
+    return RB_ERR_DEVICE;
+  }
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int64_t per_block = (int64_t)(16 / esize) * 256;
+  const int64_t gx = (cols + per_block - 1) / per_block;
+  const int64_t parts = colsum_parts(rows, gx);
+  if (gx > 0x7FFFFFFF || parts > 65535) {
+    rb_host::set_error("nvfp4 global_scale_colsum: tensor too large");
+    return RB_ERR_SHAPE;
+  }
+  const int64_t rows_per_block = (rows + parts - 1) / parts;
+  const int64_t used = (rows + rows_per_block - 1) / rows_per_block;  // partial rows actually written
+  uint32_t* ws = reinterpret_cast<uint32_t*>(workspace);
+  float* partial = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) + 16);
+  const dim3 grid((unsigned)gx, (unsigned)used);
+  if (dtype == RB_DTYPE_BF16)
+    rb::global_scale_colsum_kernel<false><<<grid, 256, 0, s>>>(x, rows, cols, ld, rows_per_block, ws, partial, gs_out);
+  else
+    rb::global_scale_colsum_kernel<true><<<grid, 256, 0, s>>>(x, rows, cols, ld, rows_per_block, ws, partial, gs_out);
+  rb::colsum_finish_kernel<<<(unsigned)((cols + 255) / 256), 256, 0, s>>>(partial, used, cols, colsum_out);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    rb_host::set_error("nvfp4 global_scale_colsum launch failed: %s", cudaGetErrorString(e));
+    return RB_ERR_CUDA;
+  }
+  return RB_OK;
 }
 
 int rb_nvfp4_global_scale_grouped(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld,

@@ -17,6 +17,7 @@ from .quantize import (
     NVFP4Tensor,
     blocked_offset,
     col_scale_bytes,
+    global_scale_and_column_sums,
     global_scale_of,
     hadamard_matrix,
     mm,
@@ -46,6 +47,7 @@ __all__ = [
     "blocked_offset",
     "bmm",
     "col_scale_bytes",
+    "global_scale_and_column_sums",
     "global_scale_of",
     "hadamard_matrix",
     "mm",

@@ -26,6 +26,7 @@ from .quantize import (
     NVFP4Tensor,
     _supported_cached,
     col_scale_bytes,
+    global_scale_and_column_sums,
     global_scale_of,
     hadamard_matrix,
     mm,
@@ -93,7 +94,10 @@ class _FP4LinearFn(torch.autograd.Function):
         fp4_backward = recipe.grad_gemms and quantize_supported_shape(*grad_y.shape)
         if fp4_backward:
             rot = hadamard if recipe.hadamard and hadamard.numel() else None
-            gg = global_scale_of(grad_y)
+            if ctx.has_bias:  # the bias gradient's column sums come from the same read of dY
+                gg, colsum = global_scale_and_column_sums(grad_y)
+            else:
+                gg = global_scale_of(grad_y)
             if ctx.reduce_grad_scale is not None:  # e.g. the full gradient's scale for an N-split slice
                 ctx.reduce_grad_scale(gg)
             # dgrad operand (rowblock) and wgrad operand (colblock, rotated) from one read of dY,
@@ -109,7 +113,10 @@ class _FP4LinearFn(torch.autograd.Function):
         else:
             grad_x = grad_y @ weight.to(grad_y.dtype)
             grad_w = grad_y.t() @ x_or_packed
-        grad_b = grad_y.sum(0) if ctx.has_bias else None
+        grad_b = None
+        if ctx.has_bias:
+            # The reference's grad_y.sum(0) is a bf16 tensor (fp32 accumulation, one rounding).
+            grad_b = colsum.to(grad_y.dtype) if fp4_backward else grad_y.sum(0)
         return (
             grad_x.to(x_dtype),
             grad_w.to(weight.dtype),

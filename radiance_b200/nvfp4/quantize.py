@@ -237,6 +237,43 @@ def global_scale_of(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.T
     return out
 
 
+_COLSUM_WS: dict[tuple[torch.device, int], torch.Tensor] = {}
+
+
+def global_scale_and_column_sums(x: torch.Tensor, out: torch.Tensor | None = None,
+                                 colsum: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """``(global_scale_of(x), x.sum(0) in fp32)`` from one read of ``x`` (two kernels, no host
+    synchronisation).  The upstream gradient of a linear with a bias needs both: the global scale
+    for its quantization and ``grad_y.sum(0)`` for the bias gradient (linear.py:146), which the
+    reference computes with a second full pass over ``grad_y``.  The sums are fp32 accumulated in
+    a fixed order (deterministic)."""
+    _require_cuda(x, "nvfp4.global_scale_and_column_sums")
+    lib = _lib.load()
+    x2 = _prep_input(x.reshape(-1, x.shape[-1]) if x.dim() != 2 else x)
+    rows, cols = x2.shape
+    dev = x.device
+    if out is None:
+        out = torch.empty((), dtype=torch.float32, device=dev)
+    if colsum is None:
+        colsum = torch.empty(cols, dtype=torch.float32, device=dev)
+    need = int(lib.rb_nvfp4_global_scale_colsum_workspace(_dtype_code(x2), rows, cols))
+    key = (dev, _stream_ptr(dev))
+    ws = _COLSUM_WS.get(key)
+    if ws is None or ws.numel() < need:
+        ws = torch.zeros(need, dtype=torch.uint8, device=dev)  # the first 16 bytes start (and stay) zero
+        _COLSUM_WS[key] = ws
+    tok = _trace.begin("amax", rows * cols * x2.element_size())
+    _lib.check(
+        lib.rb_nvfp4_global_scale_colsum(
+            x2.data_ptr(), _dtype_code(x2), rows, cols, x2.stride(0), out.data_ptr(), colsum.data_ptr(),
+            ws.data_ptr(), _stream_ptr(dev),
+        ),
+        "nvfp4.global_scale_and_column_sums",
+    )
+    _trace.end(tok)
+    return out, colsum
+
+
 def _quantize_into(
     x: torch.Tensor,
     *,
