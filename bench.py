@@ -567,8 +567,13 @@ def run_config4(args):
             n = int(counts[s][e])
             dst.extend(range(fill[j], fill[j] + n))
             fill[j] += n
-    dst = torch.tensor(dst, dtype=torch.int64, device=device)
     routed = int(exp_counts.sum())
+    # The inverse map, for gathers: padded expert-major row p takes received row src[p], or the
+    # zero row appended after the received rows when p is padding.
+    src = torch.full((t_pad,), routed, dtype=torch.int64)
+    src[torch.tensor(dst, dtype=torch.int64)] = torch.arange(routed, dtype=torch.int64)
+    src = src.to(device)
+    dst = torch.tensor(dst, dtype=torch.int64, device=device)
     flops = 6.0 * routed * (C4_D * 2 * C4_FFN + C4_FFN * C4_D)
 
     torch.manual_seed(100 + rank)
@@ -576,33 +581,47 @@ def run_config4(args):
     down = FP4GroupedLinear(per, C4_FFN, C4_D, device=device)
     gate_up.refresh_fp4_cache()
     down.refresh_fp4_cache()
-    x_send = torch.randn(sum(send), C4_D, device=device).to(torch.bfloat16)
+    x_send_ext = torch.zeros(sum(send) + 1, C4_D, device=device, dtype=torch.bfloat16)
+    x_send = x_send_ext[:sum(send)]
+    x_send.copy_(torch.randn(sum(send), C4_D, device=device).to(torch.bfloat16))
     h_in = torch.zeros(t_pad, C4_FFN, device=device, dtype=torch.bfloat16)
     h_in[dst] = torch.randn(routed, C4_FFN, device=device).to(torch.bfloat16)
     dy_gu = torch.zeros(t_pad, 2 * C4_FFN, device=device, dtype=torch.bfloat16)
     dy_gu[dst] = (torch.randn(routed, 2 * C4_FFN, device=device) * 1e-3).to(torch.bfloat16)
-    dy_send = (torch.randn(sum(send), C4_D, device=device) * 1e-3).to(torch.bfloat16)
+    dy_send_ext = torch.zeros(sum(send) + 1, C4_D, device=device, dtype=torch.bfloat16)
+    dy_send = dy_send_ext[:sum(send)]
+    dy_send.copy_((torch.randn(sum(send), C4_D, device=device) * 1e-3).to(torch.bfloat16))
 
-    def a2a(t, out_rows, out_split, in_split):
+    def a2a(t, out_rows, out_split, in_split, out=None):
         if world == 1:
+            if out is not None:
+                out.copy_(t)
+                return out
             return t
-        out = torch.empty(out_rows, t.shape[1], device=device, dtype=t.dtype)
+        if out is None:
+            out = torch.empty(out_rows, t.shape[1], device=device, dtype=t.dtype)
         dist.all_to_all_single(out, t, out_split, in_split)
         return out
 
+    # Received rows plus one zero row (the source of the padding rows in the expert-major gathers).
+    # On one GPU the received rows are the rank's own, already in place.
+    xr_ext = x_send_ext if world == 1 else torch.zeros(routed + 1, C4_D, device=device, dtype=torch.bfloat16)
+    dyr_ext = dy_send_ext if world == 1 else torch.zeros(routed + 1, C4_D, device=device, dtype=torch.bfloat16)
+
     def step():
-        # dispatch: routed rows -> their experts' owner, then expert-major with zero padding
-        xr = a2a(x_send, sum(recv), recv, send)
-        x_exp = torch.zeros(t_pad, C4_D, device=device, dtype=torch.bfloat16)
-        x_exp[dst] = xr
+        # dispatch: routed rows -> their experts' owner, then expert-major with zero padding (one
+        # row gather)
+        if world > 1:
+            a2a(x_send, sum(recv), recv, send, out=xr_ext[:routed])
+        x_exp = xr_ext.index_select(0, src)
         x_exp.requires_grad_(True)
         y_gu = gate_up(x_exp, offsets)
         h = h_in.detach().requires_grad_(True)  # silu(gate) * up of y_gu, synthetic here
         y_d = down(h, offsets)
         a2a(y_d[dst], sum(send), send, recv)  # combine: outputs back to the tokens' ranks
-        dyr = a2a(dy_send, sum(recv), recv, send)  # gradients of the combined outputs
-        dy_d = torch.zeros(t_pad, C4_D, device=device, dtype=torch.bfloat16)
-        dy_d[dst] = dyr
+        if world > 1:  # gradients of the combined outputs
+            a2a(dy_send, sum(recv), recv, send, out=dyr_ext[:routed])
+        dy_d = dyr_ext.index_select(0, src)
         torch.autograd.grad(y_d, (h, down.weight), dy_d)
         gx, _gw = torch.autograd.grad(y_gu, (x_exp, gate_up.weight), dy_gu)
         a2a(gx[dst], sum(send), send, recv)  # input gradients back to the tokens' ranks
@@ -624,22 +643,49 @@ def run_config4(args):
     visible = os.environ.get("CUDA_VISIBLE_DEVICES")
     phys = visible.split(",")[torch.cuda.current_device()] if visible else str(torch.cuda.current_device())
     clocks = ClockSampler(phys)
+    # On one GPU the step (no collectives; routing offsets stay on the device) is captured once in a
+    # CUDA graph and replayed, as in config 3; with several ranks it runs eagerly around NCCL.
+    run_step = step
+    graph = None
+    if world == 1 and not args.eager:
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                step()
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+        torch.cuda.synchronize()
+        run_step = graph.replay
     clocks.start()
     for _ in range(20):
-        step()
-    with _trace.kernel_timer() as kt:
-        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        barrier()
-        torch.cuda.synchronize()
-        start.record()
-        for _ in range(args.steps):
-            step()
-        stop.record()
-        torch.cuda.synchronize()
-        barrier()
+        run_step()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    start.record()
+    for _ in range(args.steps):
+        run_step()
+    stop.record()
+    torch.cuda.synchronize()
+    barrier()
     clk = clocks.stop()
     ms = max_over_ranks(start.elapsed_time(stop)) / args.steps
-    per_kind = kt.summary()
+    # Per-kernel breakdown: the same steps again, eagerly, with CUDA events around every launch.
+    kt_steps = max(3, min(args.steps, 50))
+    with _trace.kernel_timer() as kt:
+        for _ in range(kt_steps):
+            step()
+        torch.cuda.synchronize()
+    per_kind = {k: {kk: (int(round(vv * args.steps / kt_steps)) if kk == "launches" else vv * args.steps / kt_steps)
+                    for kk, vv in v.items()} for k, v in kt.summary().items()}
+    timing_mode = ("the step captured in one CUDA graph, replayed K times (per-kernel times from an eager pass)"
+                   if graph is not None else "eager Python step loop around NCCL (per-kernel times from a second pass)")
+    if graph is not None:
+        del graph
     if rank == 0:
         peaks, peak_kind = _peaks()
         fp4_peak = 4.0 * peaks["bf16_tflops"]
@@ -668,6 +714,7 @@ def run_config4(args):
                 "parallelism": f"expert-parallel ep{world} (NCCL all-to-all dispatch/combine)" if world > 1
                 else "single GPU, all experts",
                 "flops_basis": "6 x routed rows x (2048 x 2816 + 1408 x 2048); padding rows are overhead",
+                "timing": timing_mode,
             },
             "kernels": {k: {"launches": v["launches"], "ms": round(v["ms"], 3)} for k, v in per_kind.items()},
             "roofline": {
