@@ -737,6 +737,155 @@ def run_config4(args):
 
 
 # --------------------------------------------------------------------------------------------------
+# Config 2: one NVFP4 linear forward, both operands quantized in the step
+# --------------------------------------------------------------------------------------------------
+C2_M, C2_K, C2_N = 8192, 4096, 4096
+C2_FLOPS = 2.0 * C2_M * C2_N * C2_K  # 274.9e9
+C2_ROT = 3
+C2_METRIC = "NVFP4 linear forward TFLOPS (BASELINE config 2: 8192 x 4096 x 4096, both operands quantized)"
+
+
+def run_config2(args):
+    """One step = global scales of X and W, rowblock quantization of both, the block-scaled GEMM with
+    bf16 output (the forward of radiance's FP4Linear with its weight quantized in the step).
+    X ~ N(0,1) with 0.1% of its channels scaled x20 (outlier columns); W ~ N(0, 1/sqrt(K)); seed 0.
+    One GPU (with N ranks, each runs its own copy: replicas)."""
+    import torch
+    import torch.distributed as dist
+
+    import radiance_b200.nvfp4 as nv
+    from radiance_b200.nvfp4 import _trace
+    from radiance_b200.nvfp4.quantize import _gemm
+
+    rank, world, local = _dist_setup(args)
+    device = torch.device("cuda", local if world > 1 else 0)
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(C2_M, C2_K, generator=g)
+    cols = torch.randperm(C2_K, generator=g)[: round(0.001 * C2_K)]
+    x[:, cols] *= 20.0
+    w = torch.randn(C2_N, C2_K, generator=g) / C2_K ** 0.5
+    # Three copies of the inputs (288 MiB, more than L2), used in turn: no step finds its inputs in L2.
+    xs = [x.to(device, torch.bfloat16) for _ in range(C2_ROT)]
+    ws = [w.to(device, torch.bfloat16) for _ in range(C2_ROT)]
+    gx = torch.empty((), device=device)
+    gw = torch.empty((), device=device)
+    xq = (torch.empty(C2_M, C2_K // 2, dtype=torch.uint8, device=device),
+          torch.empty(nv.row_scale_bytes(C2_M, C2_K), dtype=torch.uint8, device=device))
+    wq = (torch.empty(C2_N, C2_K // 2, dtype=torch.uint8, device=device),
+          torch.empty(nv.row_scale_bytes(C2_N, C2_K), dtype=torch.uint8, device=device))
+    out = torch.empty(C2_M, C2_N, dtype=torch.bfloat16, device=device)
+
+    def one(x, w):
+        nv.global_scale_of(x, out=gx)
+        nv.global_scale_of(w, out=gw)
+        nv.quantize_into_(x, global_scale=gx, row=xq)
+        nv.quantize_into_(w, global_scale=gw, row=wq)
+        _gemm(xq[0], xq[1], wq[0], wq[1], gx, gw, None, torch.bfloat16, out)
+
+    def step():  # C2_ROT forwards, one per input copy
+        for r in range(C2_ROT):
+            one(xs[r], ws[r])
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+    phys = visible.split(",")[torch.cuda.current_device()] if visible else str(torch.cuda.current_device())
+    clocks = ClockSampler(phys)
+    run_step = step
+    graph = None
+    if not args.eager:
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                step()
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+        torch.cuda.synchronize()
+        run_step = graph.replay
+    clocks.start()
+    for _ in range(20):
+        run_step()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = max(1, args.steps // C2_ROT)
+    start.record()
+    for _ in range(reps):
+        run_step()
+    stop.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = start.elapsed_time(stop) / (reps * C2_ROT)
+    if world > 1:
+        t = torch.tensor([ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    kt_reps = max(1, min(reps, 16))
+    with _trace.kernel_timer() as kt:
+        for _ in range(kt_reps):
+            step()
+        torch.cuda.synchronize()
+    n_fwd = reps * C2_ROT  # forwards timed; per-kernel totals are scaled to them
+    per_kind = {k: {"launches": int(round(v["launches"] * reps / kt_reps)),
+                    "ms": round(v["ms"] * reps / kt_reps, 3)} for k, v in kt.summary().items()}
+    if graph is not None:
+        del graph
+    if rank == 0:
+        peaks, peak_kind = _peaks()
+        fp4_peak = 4.0 * peaks["bf16_tflops"]
+        gemm_ms = per_kind.get("gemm", {"ms": 0.0})["ms"] / n_fwd
+        gemm_tflops = C2_FLOPS / (gemm_ms * 1e-3) / 1e12 if gemm_ms else None
+        qms = per_kind.get("quantize", {"ms": 0.0})["ms"] / n_fwd
+        qbytes = (C2_M + C2_N) * C2_K * 2.5625
+        line = {
+            "metric": C2_METRIC,
+            "value": round(world * C2_FLOPS / (ms * 1e-3) / 1e12, 2),
+            "unit": "TFLOPS",
+            "n_gpus": world,
+            "steps": n_fwd,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "nvfp4 (e2m1 x e4m3 block scales, fp32 accumulate; bf16 in/out)",
+            "data": "synthetic (seeded; X~N(0,1) with 0.1% channels x20, W~N(0,1/sqrt(K)))",
+            "config": {
+                "workload": "config2: one linear forward, amax + rowblock quantization of X and W + GEMM",
+                "m": C2_M, "k": C2_K, "n": C2_N,
+                "parallelism": "one GPU" if world == 1 else f"{world} independent replicas",
+                "timing": "the step captured in one CUDA graph, replayed K times (per-kernel times from an eager pass)"
+                if not args.eager else "eager Python step loop",
+                "l2": f"{C2_ROT} copies of X (64 MiB) and W (32 MiB) used in turn: each step's inputs are not in L2",
+            },
+            "kernels": per_kind,
+            "quantizer_GBps": round(qbytes / (qms * 1e-3) / 1e9, 1) if qms else None,
+            "roofline": {
+                "kernel": "nvfp4_gemm2_kernel (tcgen05 cta_group::2 block-scaled GEMM)",
+                "bound": "tensor",
+                "achieved": None if gemm_tflops is None else round(gemm_tflops, 1),
+                "peak": round(fp4_peak, 1),
+                "peak_basis": f"4 x {peak_kind} dense bf16 ({peaks['bf16_tflops']} TF/s)",
+                "unit": "TFLOP/s",
+                "frac": None if gemm_tflops is None else round(gemm_tflops / fp4_peak, 4),
+                "traffic": None,
+            },
+            "gpu_launches": kt.launches * reps // kt_reps,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# --------------------------------------------------------------------------------------------------
 # Config 5: large dense block, attention linears token-sharded, FFN N-split with output all-gather
 # --------------------------------------------------------------------------------------------------
 C5_TOKENS = 65536
@@ -894,14 +1043,16 @@ def main():
                     help="config 3: time the Python step loop instead of a captured CUDA graph of the step")
     ap.add_argument("--nsplit", choices=["fused", "nccl"], default="fused",
                     help="config 5: the N-split layer's output all-gather (fused into the GEMM, or NCCL)")
-    ap.add_argument("--config", choices=["3", "4", "5"], default="3",
-                    help="3: dense block linears (the headline line); 4: MoE expert linears; "
-                         "5: d_model 4096 block with the FFN N-split")
+    ap.add_argument("--config", choices=["2", "3", "4", "5"], default="3",
+                    help="2: one linear forward (8192 x 4096 x 4096); 3: dense block linears (the headline "
+                         "line); 4: MoE expert linears; 5: d_model 4096 block with the FFN N-split")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.config == "2":
+        run_config2(args)
     elif args.config == "4":
         run_config4(args)
     elif args.config == "5":
