@@ -104,7 +104,8 @@ int rb_nvfp4_global_scale_noalloc(const void* x, int dtype, int64_t rows, int64_
  *                nearest even.  With a seed both forms use stochastic rounding with the rule of
  *                quantize.py:122-138 (up with probability (a - lo) / (hi - lo)), resolved to
  *                2^-16 of a grid step by the hardware convert cvt.rs.satfinite.e2m1x4.f32 (up with
- *                probability floor(f * 2^16) / 2^16 for the fraction f).  Each 32-element unit
+ *                probability floor(f * 2^16) / 2^16 for the fraction f of q = RN(x * RN(1/D)),
+ *                the quotient within 1.5 ulp of x / D).  Each 32-element unit
  *                (rowblock: 32 columns of a row; colblock: a column pair's 16-row blocks) draws
  *                from its own counter-based stream keyed by the seed and the unit's index, so
  *                results depend on (seed, element position) only -- not on the launch shape --

@@ -243,7 +243,13 @@ def sr_stream_col(rows: int, cols: int, seed: int) -> np.ndarray:
 def sr_nibbles(q: np.ndarray, r16: np.ndarray) -> np.ndarray:
     """The device's stochastic rounding of quotients q (already clamped to +-6) with 16-bit random
     numbers r16: the rule of quantize.py:122-138 with the fraction truncated to 16 bits -- up when
-    floor(f * 2^16) + r16 >= 2^16, f = (a - lo) / (hi - lo).  Sign in bit 3 (q < 0)."""
+    floor(f * 2^16) + r16 >= 2^16, f = (a - lo) / (hi - lo).  Sign in bit 3 (q < 0).
+
+    The device's quotient here is RN(x * RN(1/d)) rather than the IEEE x / d (one ulp of it moves
+    the probability of rounding up by at most 2^-22, below the 2^-16 resolution above);
+    ``_quantize_blocks`` forms it that way when given random numbers.  On the Hadamard path the
+    device evaluates the same product as (4y) * (RN(1/d) / 4), identical unless RN(1/d) / 4 is
+    subnormal (divisors above 2^124)."""
     q = np.asarray(q, dtype=np.float32)
     a = np.minimum(np.abs(q), np.float32(6.0)).astype(np.float64)
     levels = np.array(FP4_VALUES + (6.0,), dtype=np.float64)
@@ -281,7 +287,11 @@ def _quantize_blocks(xb: np.ndarray, gs, axis: int, u: np.ndarray | None, r: np.
     amax = np.abs(xb).max(axis=axis, keepdims=True)
     byte, divisor = block_scale(amax, gs)
     with np.errstate(invalid="ignore", divide="ignore", over="ignore"):
-        q = np.clip(xb / (divisor * gs), -FP4_MAX, FP4_MAX).astype(np.float32)
+        d = (divisor * gs).astype(np.float32)
+        # The device's stochastic rounding takes q = RN(x * RN(1/d)), within 1.5 ulp of x / d: see
+        # sr_nibbles.  Round-to-nearest uses the IEEE quotient, exactly as the reference.
+        q = xb * (_F32(1.0) / d) if r is not None else xb / d
+        q = np.clip(q, -FP4_MAX, FP4_MAX).astype(np.float32)
     code = sr_nibbles(q, r) if r is not None else encode_e2m1(np.abs(q), q < 0, u)
     return code, byte
 

@@ -32,7 +32,8 @@
 //     normal number, i.e. for every quotient above ~1e-20 -- far below 0.25, the smallest quotient
 //     with a non-zero e2m1 code.  Smaller quotients only decide the sign bit of a zero code, and
 //     that sign is fixed up exactly (see underflow_mask8).  rb_nvfp4_selftest_division checks the
-//     identity against the IEEE divide on the GPU.
+//     identity against the IEEE divide on the GPU.  Stochastic rounding, which has to match the
+//     reference in distribution only, rounds q0 = RN(x*Y) itself (quot2_sr).
 //   * The block-scale byte: byte(amax) = ceil_e4m3(clamp(RN(amax / 6gs))) is monotone in amax, so
 //     it is e + [amax >= thr[e]], where e = RN_e4m3(amax * rup) (the hardware convert, with rup a
 //     hair above 1/(6gs)) is provably the byte or the one below it, and thr[e] is the smallest
@@ -232,14 +233,22 @@ __device__ __forceinline__ float amax16(const float* a, int st) {
   return fmax3(fmax3(m0, m1, m2), fmax3(m3, m4, fabsf(a[15 * st])), 0.0f);
 }
 
-// q = RN(x / d) for a float2, given nd = -d and y = RN(1/d) (Markstein, two corrections).
+// q = RN(x / d) for a float2, given nd = -d and y = RN(1/d) (Markstein, two corrections).  The
+// first product is x * y + 0, which turns a -0 numerator into +0 (the corrections keep it there):
+// the reference's code for q = -0 is 0, its sign being `q < 0`.
 __device__ __forceinline__ float2 div2(float2 x, float2 nd, float2 y) {
-  float2 q = __fmul2_rn(x, y);
+  float2 q = __ffma2_rn(x, y, make_float2(0.0f, 0.0f));
   float2 r = __ffma2_rn(q, nd, x);
   q = __ffma2_rn(r, y, q);
   r = __ffma2_rn(q, nd, x);
   return __ffma2_rn(r, y, q);
 }
+
+// The stochastic-rounding quotient: RN(x * y) with y = RN(1/d), within 1.5 ulp of x / d (+0 for a
+// -0 numerator, as above).  Stochastic rounding only has to match the reference in distribution,
+// and an ulp of the quotient moves the probability of rounding up by at most 2^-22, far below the
+// convert's 2^-16 resolution, so the two corrections of div2 are skipped.
+__device__ __forceinline__ float2 quot2_sr(float2 x, float2 y) { return __ffma2_rn(x, y, make_float2(0.0f, 0.0f)); }
 
 // Eight quotients -> one 32-bit word of packed e2m1 codes, e0 in the low nibble.
 __device__ __forceinline__ uint32_t e2m1x8(float e0, float e1, float e2, float e3, float e4, float e5, float e6,
@@ -331,6 +340,15 @@ __device__ __forceinline__ uint32_t underflow_mask8(const float* v, int stride, 
   return keep;
 }
 
+// The same for stochastic-rounding quotients (RN(x * y), not RN(x / d)): nibble 0 where q is +-0.
+__device__ __forceinline__ uint32_t zero_mask8(const float* q, int stride) {
+  uint32_t keep = 0xFFFFFFFFu;
+#pragma unroll
+  for (int e = 0; e < 8; ++e)
+    if (q[e * stride] == 0.0f) keep &= ~(0xFu << (4 * e));
+  return keep;
+}
+
 __device__ __forceinline__ float2 bf16x2_to_float2(uint32_t w) {
   return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
 }
@@ -407,15 +425,20 @@ __device__ __forceinline__ void row_part(const uint32_t (&rk)[8], const QCtx& c,
       const float d = bs[i].d, y = bs[i].y;
       // Quotients that underflow to +-0 (possible only for large divisors) must give nibble 0.
       const float risk = F32IN ? 1.0f : 65536.0f;  // smallest |x|: 2^-149 (fp32), 2^-133 (bf16)
+      const bool risky = __any_sync(0xFFFFFFFFu, d >= risk) && d >= risk;
       uint32_t keep0 = 0xFFFFFFFFu, keep1 = 0xFFFFFFFFu;
-      if (__any_sync(0xFFFFFFFFu, d >= risk) && d >= risk) {
+      if (!SR && risky) {
         keep0 = underflow_mask8(&v[i][0].x, 1, d);
         keep1 = underflow_mask8(&v[i][4].x, 1, d);
       }
       const float2 nd = make_float2(-d, -d), yy = make_float2(y, y);
       float2 q[8];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) q[e] = div2(v[i][e], nd, yy);
+      for (int e = 0; e < 8; ++e) q[e] = SR ? quot2_sr(v[i][e], yy) : div2(v[i][e], nd, yy);
+      if (SR && risky) {
+        keep0 = zero_mask8(&q[0].x, 1);
+        keep1 = zero_mask8(&q[4].x, 1);
+      }
       if constexpr (SR) {
         const uint32_t h0 = e2m1x4_rs(q[0].x, q[0].y, q[1].x, q[1].y, sr_rbits(seed, 4 * i));
         const uint32_t h1 = e2m1x4_rs(q[2].x, q[2].y, q[3].x, q[3].y, sr_rbits(seed, 4 * i + 1));
@@ -536,7 +559,8 @@ __device__ __forceinline__ ColOut col_unit(const uint32_t (&bk)[8], uint32_t box
   // Smallest non-zero |v|: 2^-133 for bf16 inputs and sums of them, 2^-149 otherwise.
   const float risk = (F32IN || HADM == 2) ? 1.0f : 65536.0f;
   uint32_t kx0 = 0xFFFFFFFFu, kx1 = 0xFFFFFFFFu, ky0 = 0xFFFFFFFFu, ky1 = 0xFFFFFFFFu;
-  if (__any_sync(0xFFFFFFFFu, dx >= risk || dyv >= risk)) {
+  const bool risky = __any_sync(0xFFFFFFFFu, dx >= risk || dyv >= risk);
+  if (!SR && risky) {
     if (dx >= risk) {
       kx0 = underflow_mask8(&v[0].x, 2, dx);
       kx1 = underflow_mask8(&v[8].x, 2, dx);
@@ -550,7 +574,17 @@ __device__ __forceinline__ ColOut col_unit(const uint32_t (&bk)[8], uint32_t box
   const float2 yy = make_float2(sx.y * unfold, sy.y * unfold);
   float2 q[16];
 #pragma unroll
-  for (int i = 0; i < 16; ++i) q[i] = div2(v[i], nd, yy);
+  for (int i = 0; i < 16; ++i) q[i] = SR ? quot2_sr(v[i], yy) : div2(v[i], nd, yy);
+  if (SR && risky) {
+    if (dx >= risk) {
+      kx0 = zero_mask8(&q[0].x, 2);
+      kx1 = zero_mask8(&q[8].x, 2);
+    }
+    if (dyv >= risk) {
+      ky0 = zero_mask8(&q[0].y, 2);
+      ky1 = zero_mask8(&q[8].y, 2);
+    }
+  }
   uint32_t wx0, wx1, wy0, wy1;
   if constexpr (SR) {
     // Unit: column pair k0/2 + cp, 16-row group m0/16 + rg; converts 0..3 take column 2cp's rows

@@ -103,6 +103,14 @@ def main(ref_root: str) -> None:
     x[5::13, 4::7] = -1e-39
     x[1::9, :] = torch.randn(1, 128) * 1e-36
     add_quant_case("edge", x.bfloat16())
+    # Negative zeros inside ordinary blocks (the reference's code for q = -0 is 0: its sign is
+    # q < 0), plus whole blocks and one column of -0.
+    torch.manual_seed(502)
+    x = torch.randn(256, 128)
+    x[0::3, 2::5] = -0.0
+    x[16:32, 40:56] = -0.0
+    x[:, 77] = -0.0
+    add_quant_case("negzero", x.bfloat16())
     torch.manual_seed(501)
     lv = torch.tensor([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0, 6.0, 0.5, 3.0])
     x = lv[torch.randint(0, len(lv), (256, 128))] * torch.where(torch.rand(256, 128) < 0.5, -1.0, 1.0)

@@ -408,3 +408,24 @@ def test_stochastic_rounding_wide_range_matches_oracle(nv):
     np.testing.assert_array_equal(u8(col.packed), pc)
     np.testing.assert_array_equal(u8(col.scale), sc)
     _status_ok()
+
+
+def test_negative_zeros_stochastic(nv):
+    """-0 inputs inside ordinary blocks give nibble 0 under stochastic rounding too (the
+    round-to-nearest forms are pinned by the golden case ``negzero``)."""
+    torch.manual_seed(12)
+    x = torch.randn(256, 384)
+    x[0::3, 2::5] = -0.0
+    x[16:32, 40:56] = -0.0
+    x = x.bfloat16().cuda()
+    gs = nv.global_scale_of(x)
+    gs_np = np.float32(gs.item())
+    seed = torch.tensor(5, device="cuda", dtype=torch.int64)
+    had = O.hadamard_matrix()
+    row, col = nv.quantize_both(x, global_scale=gs, hadamard=torch.from_numpy(had).cuda(), stochastic=True, seed=seed)
+    xn = to_numpy_f32(x)
+    pr, _, _ = O.quantize(xn, -1, gs=gs_np, r=O.sr_stream_row(256, 384, 5))
+    pc, _, _ = O.quantize(xn, 0, gs=gs_np, hadamard=had, r=O.sr_stream_col(256, 384, 5))
+    np.testing.assert_array_equal(u8(row.packed), pr)
+    np.testing.assert_array_equal(u8(col.packed), pc)
+    _status_ok()
