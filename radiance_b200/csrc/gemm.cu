@@ -595,10 +595,15 @@ __device__ __forceinline__ void tma_load_2d_to_leader(void* smem_dst, const CUte
       : "memory");
 }
 // Arrive on the barrier at the same offset in the leader CTA.
+// Arrives on the leader CTA's copy of `bar` without release semantics.  The one use is the peer
+// epilogue's "shared accumulator columns read": its tcgen05.ld have completed (tcgen05.wait::ld)
+// and been fenced (tcgen05.fence::before_thread_sync) before the arrive, and it orders no memory
+// writes.  A release.cluster arrive cost ~670 cycles more per tile on that path, which is the
+// hand-off from one tile's last MMA to the next tile's first (about 9% of a K = 2048 GEMM).
 __device__ __forceinline__ void mbar_arrive_leader(uint64_t* bar) {
   uint32_t remote;
   asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(remote) : "r"(smem_u32(bar)));
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote) : "memory");
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote) : "memory");
 }
 
 __host__ __device__ constexpr uint32_t idesc_nvf4_m256(int n) {
