@@ -31,7 +31,7 @@
 extern "C" {
 #endif
 
-#define RB_NVFP4_ABI_VERSION 4
+#define RB_NVFP4_ABI_VERSION 5
 
 /* Input element types. */
 #define RB_DTYPE_BF16 0
@@ -153,6 +153,39 @@ int rb_nvfp4_gemm_allgather(const void* a_packed, const void* a_scale, const voi
                             int64_t m, int64_t n, int64_t k, const float* alpha_a, const float* alpha_b,
                             const void* bias, int bias_dtype, void* out, int out_dtype, int64_t ldo,
                             void* const* peer_out, int npeers, void* stream);
+
+/*
+ * rb_nvfp4_gemm for a SwiGLU producer (bf16 output): the gate/up projection of radiance's
+ * FeedForward, h = F.silu(gate_proj(x)) * up_proj(x) (src/radiance/model/ffn.py:32), with the
+ * activation and the global scale of h -- the next linear's quantizer input -- computed in the
+ * epilogue, so neither h's elementwise pass nor its amax pass reads the output again.
+ *   b_packed/b_scale : the gate and up weights as one n-row operand whose rows come in blocks of
+ *                      64: [32 gate rows | the 32 up rows of the same hidden units]; bias (if any)
+ *                      interleaved the same way.  out (m x n, bf16, row stride ldo) holds the
+ *                      pre-activations in that order (kept for the SwiGLU backward).
+ *   h                : m x n/2 bf16, row stride ldh elements (16-byte aligned, ldh*2 % 16 == 0):
+ *                      h[i, 32c + j] = bf16(bf16(silu(g)) * u) for g = out[i, 64c + j],
+ *                      u = out[i, 64c + 32 + j], silu(g) = g / (1 + exp(-g)) in fp32 -- the
+ *                      roundings of the bf16 eager F.silu(g) * u.
+ *   workspace        : 8 bytes, 8-byte aligned, zeroed before the first call (every call leaves it
+ *                      zeroed again; calls ordered on one stream can share it).
+ *   h_global_scale   : device fp32, set to max(amax|h| / 2688, 1e-12) as rb_nvfp4_global_scale
+ *                      would compute it from h (quantize.py:205-213).
+ *   m % 128 == 0, n % 128 == 0, k % 64 == 0 as rb_nvfp4_gemm.
+ */
+int rb_nvfp4_gemm_swiglu(const void* a_packed, const void* a_scale, const void* b_packed, const void* b_scale,
+                         int64_t m, int64_t n, int64_t k, const float* alpha_a, const float* alpha_b, const void* bias,
+                         int bias_dtype, void* out, int64_t ldo, void* h, int64_t ldh, void* workspace,
+                         float* h_global_scale, void* stream);
+
+/*
+ * Test aid: the SwiGLU epilogue takes silu(g), rounded to bf16, from a table and three closed forms
+ * instead of evaluating g / (1 + exp(-g)) per element; this checks that mapping on all 65536 bf16
+ * bit patterns g against bf16 of the IEEE evaluation.  mismatches: 2 device uint32 (zeroed by the
+ * caller); [0] counts the inputs whose bf16 results differ, [1] is the largest failing bit pattern
+ * plus one (0 if none).
+ */
+int rb_nvfp4_selftest_silu(uint32_t* mismatches, void* stream);
 
 /*
  * Global scale and column sums of x in one read: *gs_out as rb_nvfp4_global_scale computes it, and

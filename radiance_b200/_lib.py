@@ -40,6 +40,11 @@ SIGNATURES: dict[str, tuple] = {
         [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _c_void_p, _c_void_p, _c_void_p, _int,
          _c_void_p, _int, _i64, ctypes.POINTER(_c_void_p), _int, _c_void_p],
     ),
+    "rb_nvfp4_gemm_swiglu": (
+        _int,
+        [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _c_void_p, _c_void_p, _c_void_p, _int,
+         _c_void_p, _i64, _c_void_p, _i64, _c_void_p, _c_void_p, _c_void_p],
+    ),
     "rb_nvfp4_global_scale_colsum_workspace": (ctypes.c_size_t, [_int, _i64, _i64]),
     "rb_nvfp4_global_scale_colsum": (_int, [_c_void_p, _int, _i64, _i64, _i64, _c_void_p, _c_void_p, _c_void_p,
                                             _c_void_p]),
@@ -58,9 +63,10 @@ SIGNATURES: dict[str, tuple] = {
     ),
     "rb_nvfp4_selftest_division": (_int, [_c_void_p, _c_void_p, _i64, _c_void_p, _c_void_p]),
     "rb_nvfp4_selftest_scale": (_int, [_c_void_p, _i64, _c_void_p, _c_void_p, _c_void_p]),
+    "rb_nvfp4_selftest_silu": (_int, [_c_void_p, _c_void_p]),
 }
 
-ABI_VERSION = 4
+ABI_VERSION = 5
 
 RB_DTYPE_BF16 = 0
 RB_DTYPE_F32 = 1

@@ -83,6 +83,14 @@ struct GemmArgs {
   // own; every element stored to `out` is also written to each of them.
   void* peer_out[7];
   int npeers;
+  // SwiGLU epilogue (the kernels' kSwiglu instantiation; bf16 output, no peers).  Each 64-column
+  // chunk of the output holds [32 gate | 32 up] columns of the same 32 hidden units; besides the
+  // output itself the epilogue writes h = silu(g) * u (bf16) at h + row * ldh + col / 2 and folds
+  // max |h| into h_ws[0]; the last epilogue warp to finish turns it into the global scale of h.
+  void* h;
+  int64_t ldh;
+  uint32_t* h_ws;  // {max |h| as bf16 bits, finished epilogue warps}: zero on entry, left zero
+  float* h_gs;
 };
 
 constexpr int kMaxPeers = 7;
@@ -213,9 +221,138 @@ constexpr int kOutBox = 4096;  // one staged output box: 32 rows x 128 B
 // bf16 pieces alternate between them, fp32 pieces (two boxes of 32 columns) use both.  Rows at or
 // past row_end (the upper half of a 256-row tile when M % 256 == 128, or past a group's end) are
 // not stored.
+// silu(g) = g / (1 + exp(-g)) with the IEEE fp32 quotient, as torch's silu kernel evaluates it.
+__device__ __forceinline__ float silu_ieee(float g) { return g / (1.0f + expf(-g)); }
+
+// silu(g) rounded to bf16, for a bf16 g, is a function of g's 16 bits, and most of them are easy:
+//   |g| < 2^-9 (biased exponent e < 118): d = 1 + exp(-g) is within |g| of 2, so g / d is within a
+//       relative |g| / 2 < 2^-10 of g / 2, which is a bf16 value (or half of a subnormal one,
+//       rounded the same way) -- the result is bf16(g / 2);
+//   g >= 128 (e >= 134): exp(-g) is far below half an ulp of 1, d = 1 and the result is g;
+//   g <= -128 and the non-finite: evaluated with silu_ieee (the warp takes that path together);
+//   the 4096 others (e in 118..133, both signs): a table of bf16 results built with silu_ieee.
+// The table replaces an exp, a division and their range handling per element (about 40
+// instructions), which the epilogue's one warp per scheduler could not hide behind the MMAs.
+// rb_nvfp4_selftest_silu compares the whole mapping with bf16(silu_ieee(g)) for all 65536 g.
+constexpr uint32_t kSiluE0 = 118, kSiluE1 = 134;  // table exponents [kSiluE0, kSiluE1)
+constexpr int kSiluTab = 2048;                     // entries per sign: 16 exponents x 128 significands
+
+// Fills the table (threads tid = 0..nthreads-1 of the caller): entry i of sign s is the bf16 result
+// for the g with sign s, exponent kSiluE0 + i / 128 and significand i % 128.
+__device__ __forceinline__ void silu_table_build(uint32_t tab_pos, uint32_t tab_neg, int tid, int nthreads) {
+  for (int t = tid; t < 2 * kSiluTab; t += nthreads) {
+    const uint32_t sgn = (uint32_t)t / kSiluTab, i = (uint32_t)t % kSiluTab;
+    const uint32_t b = (sgn << 15) | ((kSiluE0 + (i >> 7)) << 7) | (i & 127u);
+    const __nv_bfloat16 r = __float2bfloat16_rn(silu_ieee(__uint_as_float(b << 16)));
+    const uint16_t rb = *reinterpret_cast<const uint16_t*>(&r);
+    asm volatile("st.shared.u16 [%0], %1;" ::"r"((sgn ? tab_neg : tab_pos) + 2 * i), "h"(rb) : "memory");
+  }
+}
+
+// A bf16 g (bits b) whose silu the table path cannot give: g <= -128, or not finite.
+__device__ __forceinline__ bool silu_needs_ieee(uint32_t b) {
+  const uint32_t e = (b >> 7) & 0xFFu;
+  return e == 0xFFu || ((b & 0x8000u) && e >= kSiluE1);
+}
+
+// bf16 bits of silu(g) for a bf16 g (bits b) that silu_needs_ieee does not reject.
+__device__ __forceinline__ uint32_t silu_bits(uint32_t b, uint32_t tab_pos, uint32_t tab_neg) {
+  const uint32_t e = (b >> 7) & 0xFFu;
+  const uint32_t i = ((e - kSiluE0) << 7 | (b & 127u)) & (uint32_t)(kSiluTab - 1);  // any valid address
+  uint16_t tv;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(tv) : "r"(((b & 0x8000u) ? tab_neg : tab_pos) + 2 * i));
+  const __nv_bfloat16 half = __float2bfloat16_rn(__uint_as_float(b << 16) * 0.5f);
+  const uint32_t hb = *reinterpret_cast<const uint16_t*>(&half);
+  return e < kSiluE0 ? hb : (e >= kSiluE1 ? b : (uint32_t)tv);
+}
+
+// The SwiGLU half of a 64-column piece: v[j] (gate) and v[32 + j] (up), j < 32, are one row's
+// pre-activations of 32 consecutive hidden units.  Each h is rounded as radiance's bf16
+// F.silu(g) * u rounds it (src/radiance/model/ffn.py:32): g and u to bf16 (as stored in the
+// output), silu(g) to bf16 (silu_bits), the product (exact in fp32) to bf16.  The row's 32 values
+// are one 64-byte run of h.  Rows at or past row_end are neither stored nor counted in the maximum.
+// The whole warp runs this (the rare exact path is taken warp-wide).
+__device__ __forceinline__ void swiglu_piece(const float* v, const GemmArgs& g, int col0, int64_t row,
+                                             int64_t row_end, uint32_t& hmax, uint32_t tab_pos, uint32_t tab_neg) {
+  uint32_t gw[16];
+  bool far = false;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    gw[j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
+    far |= silu_needs_ieee(gw[j] & 0xFFFFu) || silu_needs_ieee(gw[j] >> 16);
+  }
+  uint32_t sw[16];  // silu(g) as packed bf16 pairs
+  if (__any_sync(0xFFFFFFFFu, far)) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      sw[j] = pack_bf16x2(silu_ieee(__uint_as_float(gw[j] << 16)), silu_ieee(__uint_as_float(gw[j] & 0xFFFF0000u)));
+  } else {
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      sw[j] = silu_bits(gw[j] & 0xFFFFu, tab_pos, tab_neg) | (silu_bits(gw[j] >> 16, tab_pos, tab_neg) << 16);
+  }
+  uint32_t w[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const uint32_t uw = pack_bf16x2(v[32 + 2 * j], v[32 + 2 * j + 1]);
+    w[j] = pack_bf16x2(__uint_as_float(sw[j] << 16) * __uint_as_float(uw << 16),
+                       __uint_as_float(sw[j] & 0xFFFF0000u) * __uint_as_float(uw & 0xFFFF0000u));
+  }
+  if (row >= row_end) return;
+#pragma unroll
+  for (int j = 0; j < 16; ++j)
+    hmax = max(hmax, max(w[j] & 0x7FFFu, (w[j] >> 16) & 0x7FFFu));  // |h| as bf16 bits (NaN above inf)
+  uint8_t* p = reinterpret_cast<uint8_t*>(g.h) + (row * g.ldh + (col0 >> 1)) * 2;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) st_global_v4(p + 16 * q, w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+}
+
+// Compares the epilogue's silu (silu_bits with the silu_needs_ieee fallback) with
+// bf16(silu_ieee(g)) on all 65536 bf16 inputs: mismatches[0] counts bf16 results that differ (NaNs
+// compare equal), mismatches[1] keeps the largest failing bit pattern plus one.
+__global__ void __launch_bounds__(256) selftest_silu_kernel(uint32_t* mismatches) {
+  __shared__ __align__(16) uint16_t tab[2 * kSiluTab];
+  const uint32_t tab_pos = smem_u32(tab), tab_neg = tab_pos + 2 * kSiluTab;
+  silu_table_build(tab_pos, tab_neg, threadIdx.x, blockDim.x);
+  __syncthreads();
+  for (uint32_t b = blockIdx.x * blockDim.x + threadIdx.x; b < 65536u; b += gridDim.x * blockDim.x) {
+    const __nv_bfloat16 r = __float2bfloat16_rn(silu_ieee(__uint_as_float(b << 16)));
+    const uint32_t want = *reinterpret_cast<const uint16_t*>(&r);
+    const uint32_t got = silu_needs_ieee(b) ? want : silu_bits(b, tab_pos, tab_neg);
+    const bool nan_w = (want & 0x7FFFu) > 0x7F80u, nan_g = (got & 0x7FFFu) > 0x7F80u;
+    if (got != want && !(nan_w && nan_g)) {
+      atomicAdd(&mismatches[0], 1u);
+      atomicMax(&mismatches[1], b + 1u);
+    }
+  }
+}
+
+// End of an epilogue warp's work in SwiGLU mode: fold the warp's max |h| into the workspace; the
+// last of the launch's `n_warps` epilogue warps converts it to the global scale of h
+// (max(amax / 2688, 1e-12), quantize.py:205-213, NaN passing through) and re-zeroes the workspace.
+__device__ __forceinline__ void swiglu_finish(const GemmArgs& g, uint32_t hmax, uint32_t n_warps, int lane) {
+  const uint32_t m = __reduce_max_sync(0xFFFFFFFFu, hmax);
+  if (lane == 0) {
+    atomicMax(&g.h_ws[0], m);
+    __threadfence();
+    if (atomicAdd(&g.h_ws[1], 1u) == n_warps - 1) {
+      __threadfence();
+      const uint32_t mb = atomicExch(&g.h_ws[0], 0u) << 16;
+      atomicExch(&g.h_ws[1], 0u);
+      float gs = __fdiv_rn(__uint_as_float(mb), 2688.0f);
+      gs = (gs < 1e-12f) ? 1e-12f : gs;
+      *g.h_gs = gs;
+    }
+  }
+}
+
+// In SwiGLU mode each warp stages through its first box only; the second boxes of warps 0 and 1 hold
+// the silu table (positive and negative g).
+template <bool kSwiglu>
 __device__ __forceinline__ void epilogue_piece(const uint32_t (&r)[kEpiChunk], float alpha, const GemmArgs& g,
                                                const CUtensorMap* tmO, uint32_t slots, int& slot, int col0,
-                                               int64_t row0, int64_t row_end, int lane) {
+                                               int64_t row0, int64_t row_end, int lane, uint32_t& hmax,
+                                               uint32_t tab_pos, uint32_t tab_neg) {
   float v[kEpiChunk];
 #pragma unroll
   for (int j = 0; j < kEpiChunk; ++j) v[j] = __fmul_rn(__uint_as_float(r[j]), alpha);
@@ -244,6 +381,7 @@ __device__ __forceinline__ void epilogue_piece(const uint32_t (&r)[kEpiChunk], f
       }
     }
   }
+  if constexpr (kSwiglu) swiglu_piece(v, g, col0, row0 + lane, row_end, hmax, tab_pos, tab_neg);
   const bool store = row0 < row_end;
   const uint32_t row_off = (uint32_t)lane * 128u, sw = (uint32_t)(lane & 7);
   // Copies a staged box (32 rows x 128 B) to every peer output with coalesced 16-byte stores:
@@ -283,9 +421,12 @@ __device__ __forceinline__ void epilogue_piece(const uint32_t (&r)[kEpiChunk], f
       to_peers(slots + kOutBox, (int64_t)(col0 + 32) * 4);
     }
   } else {
-    if (lane == 0) bulk_wait_read<1>();
+    if (lane == 0) {
+      if constexpr (kSwiglu) bulk_wait_read<0>();
+      else bulk_wait_read<1>();
+    }
     __syncwarp();
-    const uint32_t box = slots + (uint32_t)slot * kOutBox;
+    const uint32_t box = slots + (kSwiglu ? 0u : (uint32_t)slot * kOutBox);
 #pragma unroll
     for (int c = 0; c < 8; ++c)
       st_shared_v4(box + row_off + ((c ^ sw) << 4), pack_bf16x2(v[8 * c], v[8 * c + 1]),
@@ -305,6 +446,7 @@ __device__ __forceinline__ void epilogue_piece(const uint32_t (&r)[kEpiChunk], f
 // ---------------------------------------------------------------------------------------------
 // The kernel
 // ---------------------------------------------------------------------------------------------
+template <bool kSwiglu>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const __grid_constant__ CUtensorMap tmO, const GemmArgs g) {
@@ -455,6 +597,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int q = warp & 3;  // TMEM lanes 32q .. 32q+31
     const uint32_t slots = smem_u32(sm.out[q]);
     int slot = 0;
+    uint32_t hmax = 0;  // SwiGLU mode: this lane's max |h| (bf16 bits)
+    const uint32_t tab_pos = smem_u32(sm.out[0][1]), tab_neg = smem_u32(sm.out[1][1]);
+    if constexpr (kSwiglu) {  // the four epilogue warps (threads 64..191) build the silu table
+      silu_table_build(tab_pos, tab_neg, (int)threadIdx.x - 64, 128);
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+    }
     float alpha = 1.0f;
     if (g.alpha_a != nullptr) alpha = *g.alpha_a;
     if (g.alpha_b != nullptr) alpha = __fmul_rn(alpha, *g.alpha_b);
@@ -486,9 +634,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(&sm.acc_empty);
         }
-        epilogue_piece(r, alpha, g, &tmO, slots, slot, nt * kBN + c * kEpiChunk, row0, g.M, lane);
+        epilogue_piece<kSwiglu>(r, alpha, g, &tmO, slots, slot, nt * kBN + c * kEpiChunk, row0, g.M, lane, hmax,
+                                tab_pos, tab_neg);
       }
     }
+    if constexpr (kSwiglu) swiglu_finish(g, hmax, gridDim.x * 4u, lane);
     // The staged boxes must not be overwritten or freed while a TMA store still reads them.
     if (lane == 0) bulk_wait_all();
     if (g.npeers > 0) __threadfence_system();
@@ -660,6 +810,7 @@ __device__ __forceinline__ Tile2 tile2_at(int t, const GemmArgs& g, const int* p
   return T;
 }
 
+template <bool kSwiglu>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     nvfp4_gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                        const __grid_constant__ CUtensorMap tmSA, const __grid_constant__ CUtensorMap tmSB,
@@ -833,6 +984,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int q = warp & 3;  // TMEM lanes 32q .. 32q+31
     const uint32_t slots = smem_u32(sm.out[q]);
     int slot = 0;
+    uint32_t hmax = 0;  // SwiGLU mode: this lane's max |h| (bf16 bits)
+    const uint32_t tab_pos = smem_u32(sm.out[0][1]), tab_neg = smem_u32(sm.out[1][1]);
+    if constexpr (kSwiglu) {  // the four epilogue warps (threads 64..191) build the silu table
+      silu_table_build(tab_pos, tab_neg, (int)threadIdx.x - 64, 128);
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+    }
     for (int i = 0; i < n_my; ++i) {
       const Tile2 T = tile2_at(cid + i * ncl, g, sm.tile_prefix);
       const int width = T.width;
@@ -871,9 +1028,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           __syncwarp();
           if (lane == 0) release();
         }
-        epilogue_piece(r, alpha, g, &tmO, slots, slot, T.ncol0 + c * kEpiChunk, row0, T.row_end, lane);
+        epilogue_piece<kSwiglu>(r, alpha, g, &tmO, slots, slot, T.ncol0 + c * kEpiChunk, row0, T.row_end, lane,
+                                hmax, tab_pos, tab_neg);
       }
     }
+    if constexpr (kSwiglu) swiglu_finish(g, hmax, gridDim.x * 4u, lane);
     if (lane == 0) bulk_wait_all();
     if (g.npeers > 0) __threadfence_system();
     __syncwarp();
@@ -899,6 +1058,7 @@ namespace {
 // Launches the two-SM kernel on min(clusters_wanted, resident clusters) CTA pairs.  A and B scale
 // buffers are viewed as rows of 256 bytes (half a 512-byte atom): one K step of one 128-row tile
 // is 8 consecutive rows.
+template <bool kSwiglu>
 int launch_two_sm(GemmArgs& g, const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmO,
                   const void* a_scale, int64_t a_rows, const void* b_scale, int64_t b_rows, int clusters_wanted,
                   int dev, cudaStream_t st) {
@@ -925,14 +1085,14 @@ int launch_two_sm(GemmArgs& g, const CUtensorMap& tmA, const CUtensorMap& tmB, c
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   if (dev >= 0 && dev < 64 && max_clusters[dev] == 0) {
-    if (cudaFuncSetAttribute(nvfp4_gemm2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+    if (cudaFuncSetAttribute(nvfp4_gemm2_kernel<kSwiglu>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
         cudaSuccess) {
       rb_host::set_error("cudaFuncSetAttribute(gemm2) failed: %s", cudaGetErrorString(cudaGetLastError()));
       return RB_ERR_CUDA;
     }
     cfg.gridDim = dim3(2 * (sms / 2), 1, 1);
     int nc = 0;
-    if (cudaOccupancyMaxActiveClusters(&nc, nvfp4_gemm2_kernel, &cfg) != cudaSuccess || nc < 1) {
+    if (cudaOccupancyMaxActiveClusters(&nc, nvfp4_gemm2_kernel<kSwiglu>, &cfg) != cudaSuccess || nc < 1) {
       cudaGetLastError();
       nc = sms / 2;
     }
@@ -942,8 +1102,33 @@ int launch_two_sm(GemmArgs& g, const CUtensorMap& tmA, const CUtensorMap& tmB, c
   const int clusters = clusters_wanted < cap ? clusters_wanted : cap;
   if (clusters < 1) return RB_OK;
   cfg.gridDim = dim3(2 * clusters, 1, 1);
-  cudaError_t e = cudaLaunchKernelEx(&cfg, nvfp4_gemm2_kernel, tmA, tmB, tmSA, tmSB, tmO, g);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, nvfp4_gemm2_kernel<kSwiglu>, tmA, tmB, tmSA, tmSB, tmO, g);
   if (e == cudaSuccess) e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    rb_host::set_error("nvfp4 gemm launch failed: %s", cudaGetErrorString(e));
+    return RB_ERR_CUDA;
+  }
+  return RB_OK;
+}
+
+// Launches the one-SM kernel (m < 256) on min(tiles, SMs) CTAs.
+template <bool kSwiglu>
+int launch_one_sm(const GemmArgs& g, const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmO, int dev,
+                  cudaStream_t st) {
+  const int sms = rb_host::num_sms(dev);
+  const size_t smem = sizeof(GemmSmem) + 1024;
+  static bool configured[64] = {false};
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    if (cudaFuncSetAttribute(nvfp4_gemm_kernel<kSwiglu>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess) {
+      rb_host::set_error("cudaFuncSetAttribute(gemm) failed: %s", cudaGetErrorString(cudaGetLastError()));
+      return RB_ERR_CUDA;
+    }
+    configured[dev] = true;
+  }
+  const int grid = g.n_tiles < sms ? g.n_tiles : sms;
+  nvfp4_gemm_kernel<kSwiglu><<<grid, kGemmThreads, smem, st>>>(tmA, tmB, tmO, g);
+  const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     rb_host::set_error("nvfp4 gemm launch failed: %s", cudaGetErrorString(e));
     return RB_ERR_CUDA;
@@ -976,10 +1161,18 @@ uint32_t rb_internal_gemm_status(int clear) {
   return v;
 }
 
+// SwiGLU outputs of rb_nvfp4_gemm_swiglu (all null for the plain GEMM).
+struct SwigluOut {
+  void* h = nullptr;
+  int64_t ldh = 0;
+  uint32_t* ws = nullptr;
+  float* gs = nullptr;
+};
+
 static int gemm_impl(const void* a_packed, const void* a_scale, const void* b_packed, const void* b_scale, int64_t m,
                      int64_t n, int64_t k, const float* alpha_a, const float* alpha_b, const void* bias,
                      int bias_dtype, void* out, int out_dtype, int64_t ldo, void* const* peer_out, int npeers,
-                     void* stream) {
+                     void* stream, const SwigluOut& sw = SwigluOut()) {
   if (npeers < 0 || npeers > kMaxPeers || (npeers > 0 && peer_out == nullptr)) {
     rb_host::set_error("nvfp4 gemm: npeers must be in [0, %d] with a peer pointer array", kMaxPeers);
     return RB_ERR_ARG;
@@ -1014,9 +1207,21 @@ static int gemm_impl(const void* a_packed, const void* a_scale, const void* b_pa
     rb_host::set_error("nvfp4 gemm: operands, bias and output must be 16-byte aligned with 16-byte row strides");
     return RB_ERR_ARG;
   }
+  const bool swiglu = sw.h != nullptr;
+  if (swiglu && (out_dtype != RB_OUT_BF16 || npeers != 0 || n % 64 != 0 || sw.ws == nullptr || sw.gs == nullptr ||
+                 misaligned(sw.h) || sw.ldh < n / 2 || ((uint64_t)sw.ldh * 2) % 16 != 0 ||
+                 (reinterpret_cast<uintptr_t>(sw.ws) & 7) != 0)) {
+    rb_host::set_error("nvfp4 gemm_swiglu: needs a bf16 output, n %% 64 == 0, a 16-byte aligned h with ldh >= n/2 "
+                       "and a 16-byte row stride, an 8-byte aligned zeroed workspace and a global-scale pointer");
+    return RB_ERR_ARG;
+  }
   int dev = rb_host::current_device();
   if (!sm100_device(dev, "nvfp4 gemm")) return RB_ERR_DEVICE;
   GemmArgs g;
+  g.h = sw.h;
+  g.ldh = sw.ldh;
+  g.h_ws = sw.ws;
+  g.h_gs = sw.gs;
   g.groups = nullptr;
   g.num_groups = 0;
   g.out_rows = m;
@@ -1051,34 +1256,15 @@ static int gemm_impl(const void* a_packed, const void* a_scale, const void* b_pa
                              (uint64_t)n, (uint64_t)m, (uint64_t)ldo * oesize, 128 / oesize, 32,
                              CU_TENSOR_MAP_SWIZZLE_128B))
     return RB_ERR_CUDA;
-  cudaError_t e = cudaSuccess;
   if (two_sm) {
     g.tiles_m = (int)((m + 255) / 256);
     g.n_tiles = g.tiles_m * g.tiles_n;
-    return launch_two_sm(g, tmA, tmB, tmO, a_scale, m, b_scale, n, g.n_tiles, dev, st);
-  } else {
-    const int sms = rb_host::num_sms(dev);
-    g.tiles_m = (int)(m / kBM);
-    g.n_tiles = g.tiles_m * g.tiles_n;
-    const size_t smem = sizeof(GemmSmem) + 1024;
-    static bool configured[64] = {false};
-    if (dev >= 0 && dev < 64 && !configured[dev]) {
-      if (cudaFuncSetAttribute(nvfp4_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-          cudaSuccess) {
-        rb_host::set_error("cudaFuncSetAttribute(gemm) failed: %s", cudaGetErrorString(cudaGetLastError()));
-        return RB_ERR_CUDA;
-      }
-      configured[dev] = true;
-    }
-    const int grid = g.n_tiles < sms ? g.n_tiles : sms;
-    nvfp4_gemm_kernel<<<grid, kGemmThreads, smem, st>>>(tmA, tmB, tmO, g);
+    return swiglu ? launch_two_sm<true>(g, tmA, tmB, tmO, a_scale, m, b_scale, n, g.n_tiles, dev, st)
+                  : launch_two_sm<false>(g, tmA, tmB, tmO, a_scale, m, b_scale, n, g.n_tiles, dev, st);
   }
-  if (e == cudaSuccess) e = cudaGetLastError();
-  if (e != cudaSuccess) {
-    rb_host::set_error("nvfp4 gemm launch failed: %s", cudaGetErrorString(e));
-    return RB_ERR_CUDA;
-  }
-  return RB_OK;
+  g.tiles_m = (int)(m / kBM);
+  g.n_tiles = g.tiles_m * g.tiles_n;
+  return swiglu ? launch_one_sm<true>(g, tmA, tmB, tmO, dev, st) : launch_one_sm<false>(g, tmA, tmB, tmO, dev, st);
 }
 
 int rb_nvfp4_gemm(const void* a_packed, const void* a_scale, const void* b_packed, const void* b_scale, int64_t m,
@@ -1094,6 +1280,38 @@ int rb_nvfp4_gemm_allgather(const void* a_packed, const void* a_scale, const voi
                             void* const* peer_out, int npeers, void* stream) {
   return gemm_impl(a_packed, a_scale, b_packed, b_scale, m, n, k, alpha_a, alpha_b, bias, bias_dtype, out, out_dtype,
                    ldo, peer_out, npeers, stream);
+}
+
+int rb_nvfp4_gemm_swiglu(const void* a_packed, const void* a_scale, const void* b_packed, const void* b_scale,
+                         int64_t m, int64_t n, int64_t k, const float* alpha_a, const float* alpha_b, const void* bias,
+                         int bias_dtype, void* out, int64_t ldo, void* h, int64_t ldh, void* workspace,
+                         float* h_global_scale, void* stream) {
+  if (h == nullptr) {
+    rb_host::set_error("nvfp4 gemm_swiglu: null h");
+    return RB_ERR_ARG;
+  }
+  SwigluOut sw;
+  sw.h = h;
+  sw.ldh = ldh;
+  sw.ws = reinterpret_cast<uint32_t*>(workspace);
+  sw.gs = h_global_scale;
+  return gemm_impl(a_packed, a_scale, b_packed, b_scale, m, n, k, alpha_a, alpha_b, bias, bias_dtype, out,
+                   RB_OUT_BF16, ldo, nullptr, 0, stream, sw);
+}
+
+int rb_nvfp4_selftest_silu(uint32_t* mismatches, void* stream) {
+  if (mismatches == nullptr) {
+    rb_host::set_error("nvfp4 selftest_silu: null output");
+    return RB_ERR_ARG;
+  }
+  if (!sm100_device(rb_host::current_device(), "nvfp4 selftest_silu")) return RB_ERR_DEVICE;
+  rb::selftest_silu_kernel<<<64, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(mismatches);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    rb_host::set_error("selftest_silu launch failed: %s", cudaGetErrorString(e));
+    return RB_ERR_CUDA;
+  }
+  return RB_OK;
 }
 
 int rb_nvfp4_gemm_grouped(const void* a_packed, const void* a_scale, int64_t a_rows, const void* b_packed,
@@ -1138,6 +1356,10 @@ int rb_nvfp4_gemm_grouped(const void* a_packed, const void* a_scale, int64_t a_r
   int dev = rb_host::current_device();
   if (!sm100_device(dev, "nvfp4 grouped gemm")) return RB_ERR_DEVICE;
   GemmArgs g;
+  g.h = nullptr;
+  g.ldh = 0;
+  g.h_ws = nullptr;
+  g.h_gs = nullptr;
   g.M = out_rows;
   g.N = n;
   g.K = k_total;
@@ -1172,7 +1394,7 @@ int rb_nvfp4_gemm_grouped(const void* a_packed, const void* a_scale, int64_t a_r
     return RB_ERR_CUDA;
   // The group sizes live on the device: every resident cluster starts, reads the table and takes
   // its share of the tiles (clusters without one exit).
-  return launch_two_sm(g, tmA, tmB, tmO, a_scale, a_rows, b_scale, b_rows, 1 << 30, dev,
+  return launch_two_sm<false>(g, tmA, tmB, tmO, a_scale, a_rows, b_scale, b_rows, 1 << 30, dev,
                        reinterpret_cast<cudaStream_t>(stream));
 }
 

@@ -7,7 +7,7 @@ everything on the hot path; the reference's pure-torch emulation (``quantize_ref
 """
 
 from .grouped import bmm
-from .linear import FP4Linear, FP4Recipe, refresh_fp4_weights
+from .linear import FP4FeedForward, FP4Linear, FP4Recipe, FP4SwiGLU, refresh_fp4_weights
 from .quantize import (
     BLOCK,
     E4M3_MAX,
@@ -20,6 +20,8 @@ from .quantize import (
     global_scale_and_column_sums,
     global_scale_of,
     hadamard_matrix,
+    interleave_gate_up,
+    merge_gate_up,
     mm,
     nvfp4_linear_mm,
     nvfp4_mm,
@@ -32,6 +34,8 @@ from .quantize import (
     require_nvfp4,
     row_scale_bytes,
     scale_denominator,
+    split_gate_up,
+    swiglu_mm,
     unpack_nibbles,
 )
 
@@ -42,7 +46,9 @@ __all__ = [
     "FP4_VALUES",
     "TINY",
     "NVFP4Tensor",
+    "FP4FeedForward",
     "FP4Linear",
+    "FP4SwiGLU",
     "FP4Recipe",
     "blocked_offset",
     "bmm",
@@ -50,6 +56,8 @@ __all__ = [
     "global_scale_and_column_sums",
     "global_scale_of",
     "hadamard_matrix",
+    "interleave_gate_up",
+    "merge_gate_up",
     "mm",
     "nvfp4_linear_mm",
     "nvfp4_mm",
@@ -63,5 +71,7 @@ __all__ = [
     "require_nvfp4",
     "row_scale_bytes",
     "scale_denominator",
+    "split_gate_up",
+    "swiglu_mm",
     "unpack_nibbles",
 ]

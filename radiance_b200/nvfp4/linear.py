@@ -36,6 +36,11 @@ from .quantize import (
     quantize_supported_shape,
     require_nvfp4,
     row_scale_bytes,
+    SWIGLU_GROUP,
+    interleave_gate_up,
+    merge_gate_up,
+    split_gate_up,
+    swiglu_mm,
 )
 
 
@@ -57,8 +62,9 @@ class _FP4LinearFn(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, x, weight, bias, w_fwd_packed, w_fwd_scale, w_fwd_gs, w_dgrad_packed, w_dgrad_scale,
-                w_dgrad_gs, hadamard, seed, recipe, reduce_grad_scale=None, output_gemm=None):
-        gx = global_scale_of(x)
+                w_dgrad_gs, hadamard, seed, recipe, reduce_grad_scale=None, output_gemm=None, x_global_scale=None):
+        # The input's global scale, unless its producer already computed it (a SwiGLU epilogue).
+        gx = global_scale_of(x) if x_global_scale is None else x_global_scale
         rot = hadamard if recipe.hadamard and hadamard.numel() else None
         save_quantized = recipe.save_activations and recipe.grad_gemms and quantize_supported_shape(*x.shape)
         if save_quantized:
@@ -121,7 +127,7 @@ class _FP4LinearFn(torch.autograd.Function):
             grad_x.to(x_dtype),
             grad_w.to(weight.dtype),
             None if grad_b is None else grad_b.to(weight.dtype),
-            None, None, None, None, None, None, None, None, None, None, None,
+            None, None, None, None, None, None, None, None, None, None, None, None,
         )
 
 
@@ -184,23 +190,154 @@ class FP4Linear(nn.Linear):
     def _eligible(self, x: torch.Tensor) -> bool:
         return self._cache_valid and quantize_supported_shape(x.numel() // self.in_features, self.in_features)
 
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
+    def _check_device(self, x: torch.Tensor) -> None:
         if not x.is_cuda or not _supported_cached(x.device):
-            require_nvfp4("FP4Linear")
-            raise RuntimeError("FP4Linear: input must be a CUDA tensor on the sm_100 device (no CPU path)")
-        if not self._eligible(x):
-            _warn_fallback_once(self, x)
-            return F.linear(x, self.weight.to(x.dtype), None if self.bias is None else self.bias.to(x.dtype))
-        flat = x.reshape(-1, self.in_features).contiguous()
-        y = _FP4LinearFn.apply(
+            require_nvfp4(type(self).__name__)
+            raise RuntimeError(f"{type(self).__name__}: input must be a CUDA tensor on the sm_100 device (no CPU path)")
+
+    def _fn_args(self, flat: torch.Tensor) -> tuple:
+        return (
             flat, self.weight, self.bias,
             self._w_fwd_packed.view(torch.float4_e2m1fn_x2), self._w_fwd_scale.view(torch.float8_e4m3fn),
             self._w_fwd_gs,
             self._w_dgrad_packed.view(torch.float4_e2m1fn_x2), self._w_dgrad_scale.view(torch.float8_e4m3fn),
             self._w_dgrad_gs,
-            self._hadamard, self._seed, self.recipe, self.reduce_grad_scale, self.output_gemm,
+            self._hadamard, self._seed, self.recipe, self.reduce_grad_scale,
         )
+
+    def forward(self, x: torch.Tensor, global_scale: torch.Tensor | None = None) -> torch.Tensor:
+        """``global_scale``: the input's 0-d fp32 global scale when its producer has computed it
+        (``FP4SwiGLU``); by default the layer computes it (linear.py:79)."""
+        self._check_device(x)
+        if not self._eligible(x):
+            _warn_fallback_once(self, x)
+            return F.linear(x, self.weight.to(x.dtype), None if self.bias is None else self.bias.to(x.dtype))
+        flat = x.reshape(-1, self.in_features).contiguous()
+        y = _FP4LinearFn.apply(*self._fn_args(flat), self.output_gemm, global_scale)
         return y.view(*x.shape[:-1], self.out_features)
+
+
+def _swiglu_backward(grad_h: torch.Tensor, gu: torch.Tensor) -> torch.Tensor:
+    """Gradient of ``F.silu(g) * u`` with respect to the interleaved pre-activations, computed with
+    the same torch kernels (and roundings) eager autograd runs for ffn.py:32: the product's
+    backward (grad * u, grad * silu(g)) and ``silu_backward``."""
+    g, u = split_gate_up(gu)
+    grad_h = grad_h.reshape(g.shape)
+    grad_u = grad_h * F.silu(g)
+    grad_g = torch.ops.aten.silu_backward(grad_h * u, g)
+    return merge_gate_up(grad_g, grad_u)
+
+
+class _FP4SwiGLUFn(torch.autograd.Function):
+    """``h = F.silu(x Wg^T + bg) * (x Wu^T + bu)`` with the gate/up GEMM in NVFP4 and the activation
+    and h's global scale computed in the GEMM's epilogue.  Same inputs as ``_FP4LinearFn``; the
+    weight is the interleaved gate/up matrix.  Returns ``(h, global_scale(h))``.
+
+    Forward and the gate/up weight/input gradients are ``_FP4LinearFn``'s, with the output GEMM
+    replaced by ``swiglu_mm``; the pre-activations are kept for the SwiGLU backward.
+    """
+
+    @staticmethod
+    def forward(ctx, x, weight, bias, w_fwd_packed, w_fwd_scale, w_fwd_gs, w_dgrad_packed, w_dgrad_scale,
+                w_dgrad_gs, hadamard, seed, recipe, reduce_grad_scale=None, output_gemm=None, x_global_scale=None):
+        produced = {}
+
+        def gemm(xq, wq, b, out_dtype):
+            gu, h, gs = swiglu_mm(xq, wq, bias=b)
+            produced["h"], produced["gs"] = h, gs
+            return gu
+
+        gu = _FP4LinearFn.forward(ctx, x, weight, bias, w_fwd_packed, w_fwd_scale, w_fwd_gs, w_dgrad_packed,
+                                  w_dgrad_scale, w_dgrad_gs, hadamard, seed, recipe, reduce_grad_scale, gemm,
+                                  x_global_scale)
+        ctx.gu = gu  # an intermediate, kept on ctx for the SwiGLU backward
+        ctx.mark_non_differentiable(produced["gs"])
+        return produced["h"], produced["gs"]
+
+    @staticmethod
+    def backward(ctx, grad_h, _grad_gs):
+        grad_gu = _swiglu_backward(grad_h, ctx.gu)
+        del ctx.gu
+        return _FP4LinearFn.backward(ctx, grad_gu)
+
+
+class FP4SwiGLU(FP4Linear):
+    """The ``gate_proj`` / ``up_proj`` pair of radiance's ``FeedForward`` (src/radiance/model/ffn.py:21-22,
+    :32) as one NVFP4 linear of ``2 * hidden_features`` rows, interleaved in blocks of 32 hidden
+    units (``interleave_gate_up``).  ``forward(x)`` returns ``(h, gs)``: ``h = F.silu(gate_proj(x)) *
+    up_proj(x)`` and ``gs`` its global scale, both from the GEMM's epilogue, so the next
+    ``FP4Linear`` (``down_proj(h, global_scale=gs)``) skips its amax pass and nothing re-reads the
+    pre-activations in the forward.  ``gs`` is None on the bf16 fallback path."""
+
+    def __init__(self, in_features, hidden_features, bias=True, recipe: FP4Recipe | None = None, device=None,
+                 dtype=None):
+        if hidden_features % SWIGLU_GROUP:
+            raise ValueError(f"FP4SwiGLU: hidden_features must be a multiple of {SWIGLU_GROUP}")
+        super().__init__(in_features, 2 * hidden_features, bias=bias, recipe=recipe, device=device, dtype=dtype)
+        self.hidden_features = hidden_features
+
+    @classmethod
+    @torch.no_grad()
+    def from_gate_up(cls, gate_proj: nn.Linear, up_proj: nn.Linear, recipe: FP4Recipe | None = None) -> "FP4SwiGLU":
+        """Build from the two ``nn.Linear`` layers of a radiance ``FeedForward`` (weights copied)."""
+        w = gate_proj.weight
+        mod = cls(gate_proj.in_features, gate_proj.out_features, bias=gate_proj.bias is not None, recipe=recipe,
+                  device=w.device, dtype=w.dtype)
+        mod.weight.copy_(interleave_gate_up(gate_proj.weight, up_proj.weight))
+        if gate_proj.bias is not None:
+            mod.bias.copy_(interleave_gate_up(gate_proj.bias, up_proj.bias))
+        mod.invalidate_fp4_cache()
+        return mod
+
+    def gate_up_weights(self) -> tuple[torch.Tensor, torch.Tensor]:
+        """The gate and up projections' weights (copies, in their own row order)."""
+        g, u = split_gate_up(self.weight.detach().t())
+        return g.t().contiguous(), u.t().contiguous()
+
+    def _eligible(self, x: torch.Tensor) -> bool:
+        return super()._eligible(x) and x.dtype == torch.bfloat16
+
+    def forward(self, x: torch.Tensor, global_scale: torch.Tensor | None = None):
+        self._check_device(x)
+        if not self._eligible(x):
+            _warn_fallback_once(self, x)
+            gu = F.linear(x, self.weight.to(x.dtype), None if self.bias is None else self.bias.to(x.dtype))
+            g, u = split_gate_up(gu)
+            return F.silu(g) * u, None
+        flat = x.reshape(-1, self.in_features).contiguous()
+        h, gs = _FP4SwiGLUFn.apply(*self._fn_args(flat), None, global_scale)
+        return h.view(*x.shape[:-1], self.hidden_features), gs
+
+
+class FP4FeedForward(nn.Module):
+    """radiance's one-hidden-layer ``FeedForward`` (ffn.py:10-39, ``ffn_depth == 1``, no LoRA):
+    ``down_proj(F.silu(gate_proj(x)) * up_proj(x))``, with the gate/up pair as ``FP4SwiGLU`` and
+    ``down_proj`` an ``FP4Linear`` fed the global scale the SwiGLU epilogue computed."""
+
+    def __init__(self, d_model, ffn_dim, bias=True, dropout: float = 0.0, recipe: FP4Recipe | None = None,
+                 device=None, dtype=None):
+        super().__init__()
+        self.gate_up = FP4SwiGLU(d_model, ffn_dim, bias=bias, recipe=recipe, device=device, dtype=dtype)
+        self.down_proj = FP4Linear(ffn_dim, d_model, bias=bias, recipe=recipe, device=device, dtype=dtype)
+        self.dropout = nn.Dropout(dropout)
+
+    @classmethod
+    @torch.no_grad()
+    def from_feedforward(cls, ff: nn.Module, recipe: FP4Recipe | None = None) -> "FP4FeedForward":
+        """Build from a module with ``gate_proj``, ``up_proj`` and ``down_proj`` ``nn.Linear`` layers."""
+        w = ff.down_proj.weight
+        mod = cls(ff.gate_proj.in_features, ff.gate_proj.out_features, bias=ff.down_proj.bias is not None,
+                  recipe=recipe, device=w.device, dtype=w.dtype)
+        mod.gate_up = FP4SwiGLU.from_gate_up(ff.gate_proj, ff.up_proj, recipe=recipe)
+        mod.down_proj.weight.copy_(ff.down_proj.weight)
+        if ff.down_proj.bias is not None:
+            mod.down_proj.bias.copy_(ff.down_proj.bias)
+        mod.down_proj.invalidate_fp4_cache()
+        return mod
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        h, gs = self.gate_up(x)
+        return self.dropout(self.down_proj(h, global_scale=gs))
 
 
 _warned_fp4_fallback = False

@@ -525,6 +525,89 @@ def _nvfp4_linear_mm_fake(a_packed, a_scale, a_gs, b_packed, b_scale, b_gs, bias
     return a_packed.new_empty((a_packed.shape[0], b_packed.shape[0]), dtype=out_dtype)
 
 
+# ------------------------------------------------------------------------------------------------
+# SwiGLU producer: the gate/up GEMM whose epilogue also emits h and its global scale
+# ------------------------------------------------------------------------------------------------
+
+SWIGLU_GROUP = 32  # hidden units per [gate | up] block of the interleaved layout
+
+
+def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """Stack the gate and up projections' rows (weights ``(H, in)`` or biases ``(H,)``) into the
+    ``(2H, ...)`` order ``swiglu_mm`` reads: blocks of 64 rows, [32 gate rows | the 32 up rows of
+    the same hidden units]."""
+    if gate.shape != up.shape or gate.shape[0] % SWIGLU_GROUP:
+        raise ValueError(f"interleave_gate_up: gate {tuple(gate.shape)} and up {tuple(up.shape)} must match, "
+                         f"with rows % {SWIGLU_GROUP} == 0")
+    h, rest = gate.shape[0], gate.shape[1:]
+    blocks = (h // SWIGLU_GROUP, SWIGLU_GROUP, *rest)
+    return torch.stack([gate.reshape(blocks), up.reshape(blocks)], dim=1).reshape(2 * h, *rest)
+
+
+def split_gate_up(gu: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """The interleaved order along the last dimension -> gate, up ``(..., H)`` (contiguous copies)."""
+    two_h = gu.shape[-1]
+    v = gu.reshape(*gu.shape[:-1], two_h // (2 * SWIGLU_GROUP), 2, SWIGLU_GROUP)
+    return (v[..., 0, :].reshape(*gu.shape[:-1], two_h // 2), v[..., 1, :].reshape(*gu.shape[:-1], two_h // 2))
+
+
+def merge_gate_up(g: torch.Tensor, u: torch.Tensor) -> torch.Tensor:
+    """Inverse of ``split_gate_up``: gate and up ``(..., H)`` -> the interleaved ``(..., 2H)``."""
+    lead, h = g.shape[:-1], g.shape[-1]
+    blocks = (*lead, h // SWIGLU_GROUP, SWIGLU_GROUP)
+    return torch.stack([g.reshape(blocks), u.reshape(blocks)], dim=-2).reshape(*lead, 2 * h)
+
+
+def swiglu_mm(a: NVFP4Tensor, b: NVFP4Tensor, *, bias=None, out: torch.Tensor | None = None,
+              h: torch.Tensor | None = None, h_global_scale: torch.Tensor | None = None):
+    """The gate/up projection of a SwiGLU FFN and its activation in one GEMM.
+
+    ``b`` holds the gate and up weights interleaved (``interleave_gate_up``).  Returns
+    ``(gu, h, gs)``: ``gu = (a @ b.T) * (ga * gb) + bias`` in bf16 (the pre-activations, in the
+    interleaved order), ``h = F.silu(g) * u`` in bf16 with the roundings of radiance's eager
+    ``F.silu(gate_proj(x)) * up_proj(x)`` (src/radiance/model/ffn.py:32), and
+    ``gs = global_scale_of(h)``, all from the GEMM's epilogue -- the next linear's quantizer takes
+    ``gs`` and reads ``h`` once.
+    """
+    _require_cuda(a.packed, "nvfp4.swiglu_mm")
+    lib = _lib.load()
+    ap, asc = a.packed.view(torch.uint8), a.scale.view(torch.uint8)
+    bp, bsc = b.packed.view(torch.uint8), b.scale.view(torch.uint8)
+    m, k2 = ap.shape
+    n, k2b = bp.shape
+    if k2 != k2b:
+        raise ValueError(f"nvfp4.swiglu_mm: contraction mismatch {2 * k2} vs {2 * k2b}")
+    if n % (2 * SWIGLU_GROUP):
+        raise ValueError(f"nvfp4.swiglu_mm: the interleaved gate/up operand needs rows % 64 == 0, got {n}")
+    dev = ap.device
+    if out is None:
+        out = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
+    if h is None:
+        h = torch.empty(m, n // 2, device=dev, dtype=torch.bfloat16)
+    if h_global_scale is None:
+        h_global_scale = torch.empty((), device=dev, dtype=torch.float32)
+    bias_code = 0
+    if bias is not None:
+        if bias.dtype not in (torch.bfloat16, torch.float32):
+            bias = bias.to(torch.float32)
+        bias = bias.contiguous()
+        if bias.data_ptr() % 16:
+            bias = bias.clone()
+        bias_code = _lib.RB_DTYPE_BF16 if bias.dtype == torch.bfloat16 else _lib.RB_DTYPE_F32
+    tok = _trace.begin("gemm", 2.0 * m * n * 2 * k2)
+    _lib.check(
+        lib.rb_nvfp4_gemm_swiglu(
+            ap.data_ptr(), asc.data_ptr(), bp.data_ptr(), bsc.data_ptr(), m, n, 2 * k2,
+            a.global_scale.data_ptr(), b.global_scale.data_ptr(),
+            None if bias is None else bias.data_ptr(), bias_code, out.data_ptr(), out.stride(0),
+            h.data_ptr(), h.stride(0), _workspace(dev).data_ptr(), h_global_scale.data_ptr(), _stream_ptr(dev),
+        ),
+        "nvfp4.swiglu_mm",
+    )
+    _trace.end(tok)
+    return out, h, h_global_scale
+
+
 def mm(a: NVFP4Tensor, b: NVFP4Tensor, *, out_dtype: torch.dtype = torch.bfloat16, bias=None) -> torch.Tensor:
     """``a @ b.T`` with the global scales folded back in (quantize.py:400-409).
 

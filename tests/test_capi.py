@@ -80,3 +80,36 @@ def test_grouped_record_builders():
         [0, 0, 0, 128, 0, 320], [128, 64, 128, 0, 0, 320], [128, 128, 128, 256, 0, 320]]
     assert groups_over_contraction(offs, 256).tolist() == [
         [0, 0, 0, 256, 0, 128], [0, 0, 256, 256, 128, 0], [0, 0, 512, 256, 128, 256]]
+
+
+def test_swiglu_gemm_contract_is_checked_on_the_host():
+    """rb_nvfp4_gemm_swiglu refuses shapes and outputs it cannot serve before touching memory."""
+    lib = _lib.load()
+    buf = ctypes.c_void_p(256)
+    # n = 192 is not a multiple of 128.
+    rc = lib.rb_nvfp4_gemm_swiglu(buf, buf, buf, buf, 256, 192, 128, None, None, None, 0, buf, 192, buf, 96, buf,
+                                  buf, None)
+    assert rc in (1, 2) and lib.rb_nvfp4_last_error().decode()
+    # h row stride shorter than n / 2.
+    rc = lib.rb_nvfp4_gemm_swiglu(buf, buf, buf, buf, 256, 256, 128, None, None, None, 0, buf, 256, buf, 64, buf,
+                                  buf, None)
+    assert rc == 2 and "ldh" in lib.rb_nvfp4_last_error().decode()
+    rc = lib.rb_nvfp4_gemm_swiglu(buf, buf, buf, buf, 256, 256, 128, None, None, None, 0, buf, 256, None, 128, buf,
+                                  buf, None)
+    assert rc == 2
+
+
+def test_gate_up_interleave_round_trip():
+    """The [32 gate | 32 up] row order the SwiGLU epilogue reads (CPU, pure torch)."""
+    import torch
+
+    import radiance_b200.nvfp4 as nv
+
+    wg, wu = torch.randn(96, 8), torch.randn(96, 8)
+    w = nv.interleave_gate_up(wg, wu)
+    assert torch.equal(w[:32], wg[:32]) and torch.equal(w[32:64], wu[:32]) and torch.equal(w[64:96], wg[32:64])
+    x = torch.randn(5, 8)
+    g, u = nv.split_gate_up(x @ w.t())
+    torch.testing.assert_close(g, x @ wg.t())
+    torch.testing.assert_close(u, x @ wu.t())
+    assert torch.equal(nv.merge_gate_up(g, u), x @ w.t())
