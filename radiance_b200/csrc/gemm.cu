@@ -229,7 +229,8 @@ __device__ __forceinline__ float silu_ieee(float g) { return g / (1.0f + expf(-g
 //       relative |g| / 2 < 2^-10 of g / 2, which is a bf16 value (or half of a subnormal one,
 //       rounded the same way) -- the result is bf16(g / 2);
 //   g >= 128 (e >= 134): exp(-g) is far below half an ulp of 1, d = 1 and the result is g;
-//   g <= -128 and the non-finite: evaluated with silu_ieee (the warp takes that path together);
+//   +inf and NaN: g as well;  g <= -128 (and -inf): evaluated with silu_ieee (the warp takes that
+//       path together);
 //   the 4096 others (e in 118..133, both signs): a table of bf16 results built with silu_ieee.
 // The table replaces an exp, a division and their range handling per element (about 40
 // instructions), which the epilogue's one warp per scheduler could not hide behind the MMAs.
@@ -237,66 +238,67 @@ __device__ __forceinline__ float silu_ieee(float g) { return g / (1.0f + expf(-g
 constexpr uint32_t kSiluE0 = 118, kSiluE1 = 134;  // table exponents [kSiluE0, kSiluE1)
 constexpr int kSiluTab = 2048;                     // entries per sign: 16 exponents x 128 significands
 
-// Fills the table (threads tid = 0..nthreads-1 of the caller): entry i of sign s is the bf16 result
-// for the g with sign s, exponent kSiluE0 + i / 128 and significand i % 128.
-__device__ __forceinline__ void silu_table_build(uint32_t tab_pos, uint32_t tab_neg, int tid, int nthreads) {
+// Fills the table at `tab` (threads tid = 0..nthreads-1 of the caller): entry s * 2048 + i is the
+// bf16 result for the g with sign s, exponent kSiluE0 + i / 128 and significand i % 128.
+__device__ __forceinline__ void silu_table_build(uint32_t tab, int tid, int nthreads) {
   for (int t = tid; t < 2 * kSiluTab; t += nthreads) {
     const uint32_t sgn = (uint32_t)t / kSiluTab, i = (uint32_t)t % kSiluTab;
     const uint32_t b = (sgn << 15) | ((kSiluE0 + (i >> 7)) << 7) | (i & 127u);
     const __nv_bfloat16 r = __float2bfloat16_rn(silu_ieee(__uint_as_float(b << 16)));
     const uint16_t rb = *reinterpret_cast<const uint16_t*>(&r);
-    asm volatile("st.shared.u16 [%0], %1;" ::"r"((sgn ? tab_neg : tab_pos) + 2 * i), "h"(rb) : "memory");
+    asm volatile("st.shared.u16 [%0], %1;" ::"r"(tab + 2 * (uint32_t)t), "h"(rb) : "memory");
   }
 }
 
-// A bf16 g (bits b) whose silu the table path cannot give: g <= -128, or not finite.
-__device__ __forceinline__ bool silu_needs_ieee(uint32_t b) {
-  const uint32_t e = (b >> 7) & 0xFFu;
-  return e == 0xFFu || ((b & 0x8000u) && e >= kSiluE1);
-}
-
-// bf16 bits of silu(g) for a bf16 g (bits b) that silu_needs_ieee does not reject.
-__device__ __forceinline__ uint32_t silu_bits(uint32_t b, uint32_t tab_pos, uint32_t tab_neg) {
-  const uint32_t e = (b >> 7) & 0xFFu;
-  const uint32_t i = ((e - kSiluE0) << 7 | (b & 127u)) & (uint32_t)(kSiluTab - 1);  // any valid address
+// silu(g) as a float holding a bf16 value, for a bf16 g (bits b, value gf) above -128 (finite or
+// not: +-inf and NaN above the table range give g itself, as the IEEE evaluation does for +inf and
+// NaN).  One table read and two selects; rb_nvfp4_selftest_silu checks it on every bf16 input.
+__device__ __forceinline__ float silu_lookup(uint32_t b, float gf, uint32_t tab) {
+  const uint32_t idx = ((b - (kSiluE0 << 7)) & 0x7FFu) | ((b >> 4) & 0x800u);  // any valid entry
   uint16_t tv;
-  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(tv) : "r"(((b & 0x8000u) ? tab_neg : tab_pos) + 2 * i));
-  const __nv_bfloat16 half = __float2bfloat16_rn(__uint_as_float(b << 16) * 0.5f);
-  const uint32_t hb = *reinterpret_cast<const uint16_t*>(&half);
-  return e < kSiluE0 ? hb : (e >= kSiluE1 ? b : (uint32_t)tv);
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(tv) : "r"(tab + 2 * idx));
+  const float a = fabsf(gf);
+  const float half = __bfloat162float(__float2bfloat16_rn(gf * 0.5f));
+  const float t = __uint_as_float((uint32_t)tv << 16);
+  return a < 0.001953125f /* 2^-9 */ ? half : (a >= 128.0f || a != a ? gf : t);
 }
 
 // The SwiGLU half of a 64-column piece: v[j] (gate) and v[32 + j] (up), j < 32, are one row's
 // pre-activations of 32 consecutive hidden units.  Each h is rounded as radiance's bf16
 // F.silu(g) * u rounds it (src/radiance/model/ffn.py:32): g and u to bf16 (as stored in the
-// output), silu(g) to bf16 (silu_bits), the product (exact in fp32) to bf16.  The row's 32 values
-// are one 64-byte run of h.  Rows at or past row_end are neither stored nor counted in the maximum.
-// The whole warp runs this (the rare exact path is taken warp-wide).
+// output), silu(g) to bf16, the product (exact in fp32) to bf16.  The row's 32 values are one
+// 64-byte run of h.  Rows at or past row_end are neither stored nor counted in the maximum.  The
+// whole warp runs this: a gate value at or below -128 anywhere in it sends the warp down the
+// IEEE evaluation (rare).
 __device__ __forceinline__ void swiglu_piece(const float* v, const GemmArgs& g, int col0, int64_t row,
-                                             int64_t row_end, uint32_t& hmax, uint32_t tab_pos, uint32_t tab_neg) {
+                                             int64_t row_end, uint32_t& hmax, uint32_t tab) {
   uint32_t gw[16];
-  bool far = false;
+  __nv_bfloat162 mn = __float2bfloat162_rn(0.0f);
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
     gw[j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
-    far |= silu_needs_ieee(gw[j] & 0xFFFFu) || silu_needs_ieee(gw[j] >> 16);
+    mn = __hmin2(mn, *reinterpret_cast<const __nv_bfloat162*>(&gw[j]));
   }
-  uint32_t sw[16];  // silu(g) as packed bf16 pairs
+  const bool far = fminf(__low2float(mn), __high2float(mn)) <= -128.0f;
+  float sl[32];
   if (__any_sync(0xFFFFFFFFu, far)) {
 #pragma unroll
-    for (int j = 0; j < 16; ++j)
-      sw[j] = pack_bf16x2(silu_ieee(__uint_as_float(gw[j] << 16)), silu_ieee(__uint_as_float(gw[j] & 0xFFFF0000u)));
+    for (int j = 0; j < 32; ++j) {
+      const uint32_t b = (j & 1) ? (gw[j >> 1] >> 16) : (gw[j >> 1] & 0xFFFFu);
+      sl[j] = __bfloat162float(__float2bfloat16_rn(silu_ieee(__uint_as_float(b << 16))));
+    }
   } else {
 #pragma unroll
-    for (int j = 0; j < 16; ++j)
-      sw[j] = silu_bits(gw[j] & 0xFFFFu, tab_pos, tab_neg) | (silu_bits(gw[j] >> 16, tab_pos, tab_neg) << 16);
+    for (int j = 0; j < 32; ++j) {
+      const uint32_t b = (j & 1) ? (gw[j >> 1] >> 16) : (gw[j >> 1] & 0xFFFFu);
+      sl[j] = silu_lookup(b, __uint_as_float(b << 16), tab);
+    }
   }
   uint32_t w[16];
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
     const uint32_t uw = pack_bf16x2(v[32 + 2 * j], v[32 + 2 * j + 1]);
-    w[j] = pack_bf16x2(__uint_as_float(sw[j] << 16) * __uint_as_float(uw << 16),
-                       __uint_as_float(sw[j] & 0xFFFF0000u) * __uint_as_float(uw & 0xFFFF0000u));
+    w[j] = pack_bf16x2(sl[2 * j] * __uint_as_float(uw << 16), sl[2 * j + 1] * __uint_as_float(uw & 0xFFFF0000u));
   }
   if (row >= row_end) return;
 #pragma unroll
@@ -307,18 +309,20 @@ __device__ __forceinline__ void swiglu_piece(const float* v, const GemmArgs& g, 
   for (int q = 0; q < 4; ++q) st_global_v4(p + 16 * q, w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
 }
 
-// Compares the epilogue's silu (silu_bits with the silu_needs_ieee fallback) with
+// Compares the epilogue's silu (silu_lookup, and the IEEE evaluation at or below -128) with
 // bf16(silu_ieee(g)) on all 65536 bf16 inputs: mismatches[0] counts bf16 results that differ (NaNs
 // compare equal), mismatches[1] keeps the largest failing bit pattern plus one.
 __global__ void __launch_bounds__(256) selftest_silu_kernel(uint32_t* mismatches) {
   __shared__ __align__(16) uint16_t tab[2 * kSiluTab];
-  const uint32_t tab_pos = smem_u32(tab), tab_neg = tab_pos + 2 * kSiluTab;
-  silu_table_build(tab_pos, tab_neg, threadIdx.x, blockDim.x);
+  const uint32_t tab_addr = smem_u32(tab);
+  silu_table_build(tab_addr, threadIdx.x, blockDim.x);
   __syncthreads();
   for (uint32_t b = blockIdx.x * blockDim.x + threadIdx.x; b < 65536u; b += gridDim.x * blockDim.x) {
-    const __nv_bfloat16 r = __float2bfloat16_rn(silu_ieee(__uint_as_float(b << 16)));
+    const float gf = __uint_as_float(b << 16);
+    const __nv_bfloat16 r = __float2bfloat16_rn(silu_ieee(gf));
     const uint32_t want = *reinterpret_cast<const uint16_t*>(&r);
-    const uint32_t got = silu_needs_ieee(b) ? want : silu_bits(b, tab_pos, tab_neg);
+    const float sv = gf <= -128.0f ? __bfloat162float(r) : silu_lookup(b, gf, tab_addr);
+    const uint32_t got = __float_as_uint(sv) >> 16;
     const bool nan_w = (want & 0x7FFFu) > 0x7F80u, nan_g = (got & 0x7FFFu) > 0x7F80u;
     if (got != want && !(nan_w && nan_g)) {
       atomicAdd(&mismatches[0], 1u);
@@ -346,13 +350,13 @@ __device__ __forceinline__ void swiglu_finish(const GemmArgs& g, uint32_t hmax, 
   }
 }
 
-// In SwiGLU mode each warp stages through its first box only; the second boxes of warps 0 and 1 hold
-// the silu table (positive and negative g).
+// In SwiGLU mode each warp stages through one box: its first, except warp 1, which uses its second;
+// the 8 KB from warp 0's second box through warp 1's first hold the silu table.
 template <bool kSwiglu>
 __device__ __forceinline__ void epilogue_piece(const uint32_t (&r)[kEpiChunk], float alpha, const GemmArgs& g,
                                                const CUtensorMap* tmO, uint32_t slots, int& slot, int col0,
                                                int64_t row0, int64_t row_end, int lane, uint32_t& hmax,
-                                               uint32_t tab_pos, uint32_t tab_neg) {
+                                               uint32_t tab) {
   float v[kEpiChunk];
 #pragma unroll
   for (int j = 0; j < kEpiChunk; ++j) v[j] = __fmul_rn(__uint_as_float(r[j]), alpha);
@@ -381,7 +385,7 @@ __device__ __forceinline__ void epilogue_piece(const uint32_t (&r)[kEpiChunk], f
       }
     }
   }
-  if constexpr (kSwiglu) swiglu_piece(v, g, col0, row0 + lane, row_end, hmax, tab_pos, tab_neg);
+  if constexpr (kSwiglu) swiglu_piece(v, g, col0, row0 + lane, row_end, hmax, tab);
   const bool store = row0 < row_end;
   const uint32_t row_off = (uint32_t)lane * 128u, sw = (uint32_t)(lane & 7);
   // Copies a staged box (32 rows x 128 B) to every peer output with coalesced 16-byte stores:
@@ -426,7 +430,8 @@ __device__ __forceinline__ void epilogue_piece(const uint32_t (&r)[kEpiChunk], f
       else bulk_wait_read<1>();
     }
     __syncwarp();
-    const uint32_t box = slots + (kSwiglu ? 0u : (uint32_t)slot * kOutBox);
+    const uint32_t box =
+        slots + (kSwiglu ? (((threadIdx.x >> 5) & 3) == 1 ? (uint32_t)kOutBox : 0u) : (uint32_t)slot * kOutBox);
 #pragma unroll
     for (int c = 0; c < 8; ++c)
       st_shared_v4(box + row_off + ((c ^ sw) << 4), pack_bf16x2(v[8 * c], v[8 * c + 1]),
@@ -598,9 +603,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const uint32_t slots = smem_u32(sm.out[q]);
     int slot = 0;
     uint32_t hmax = 0;  // SwiGLU mode: this lane's max |h| (bf16 bits)
-    const uint32_t tab_pos = smem_u32(sm.out[0][1]), tab_neg = smem_u32(sm.out[1][1]);
+    const uint32_t tab = smem_u32(sm.out[0][1]);  // SwiGLU mode: 8 KB, through sm.out[1][0]
     if constexpr (kSwiglu) {  // the four epilogue warps (threads 64..191) build the silu table
-      silu_table_build(tab_pos, tab_neg, (int)threadIdx.x - 64, 128);
+      silu_table_build(tab, (int)threadIdx.x - 64, 128);
       asm volatile("bar.sync 1, 128;" ::: "memory");
     }
     float alpha = 1.0f;
@@ -635,7 +640,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (lane == 0) mbar_arrive(&sm.acc_empty);
         }
         epilogue_piece<kSwiglu>(r, alpha, g, &tmO, slots, slot, nt * kBN + c * kEpiChunk, row0, g.M, lane, hmax,
-                                tab_pos, tab_neg);
+                                tab);
       }
     }
     if constexpr (kSwiglu) swiglu_finish(g, hmax, gridDim.x * 4u, lane);
@@ -985,9 +990,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const uint32_t slots = smem_u32(sm.out[q]);
     int slot = 0;
     uint32_t hmax = 0;  // SwiGLU mode: this lane's max |h| (bf16 bits)
-    const uint32_t tab_pos = smem_u32(sm.out[0][1]), tab_neg = smem_u32(sm.out[1][1]);
+    const uint32_t tab = smem_u32(sm.out[0][1]);  // SwiGLU mode: 8 KB, through sm.out[1][0]
     if constexpr (kSwiglu) {  // the four epilogue warps (threads 64..191) build the silu table
-      silu_table_build(tab_pos, tab_neg, (int)threadIdx.x - 64, 128);
+      silu_table_build(tab, (int)threadIdx.x - 64, 128);
       asm volatile("bar.sync 1, 128;" ::: "memory");
     }
     for (int i = 0; i < n_my; ++i) {
@@ -1029,7 +1034,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (lane == 0) release();
         }
         epilogue_piece<kSwiglu>(r, alpha, g, &tmO, slots, slot, T.ncol0 + c * kEpiChunk, row0, T.row_end, lane,
-                                hmax, tab_pos, tab_neg);
+                                hmax, tab);
       }
     }
     if constexpr (kSwiglu) swiglu_finish(g, hmax, gridDim.x * 4u, lane);
