@@ -177,6 +177,15 @@ __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity) {
   return __all_sync(0xFFFFFFFFu, mbar_wait(bar, parity));
 }
 
+// The producer's and MMA issuer's waits.  In the SwiGLU instantiation the epilogue bounds the
+// kernel and these warps mostly wait for it; they poll with a short sleep so that their polling
+// does not take issue slots from the epilogue warps on their schedulers.
+template <bool kSwiglu>
+__device__ __forceinline__ bool pipe_wait_warp(uint64_t* bar, uint32_t parity) {
+  if constexpr (kSwiglu) return __all_sync(0xFFFFFFFFu, mbar_wait_sleep(bar, parity, 32));
+  else return mbar_wait_warp(bar, parity);
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<const uint32_t*>(&v);
@@ -260,7 +269,7 @@ __device__ __forceinline__ float silu_lookup(uint32_t b, float gf, uint32_t tab)
   const float a = fabsf(gf);
   const float half = __bfloat162float(__float2bfloat16_rn(gf * 0.5f));
   const float t = __uint_as_float((uint32_t)tv << 16);
-  return a < 0.001953125f /* 2^-9 */ ? half : (a >= 128.0f || a != a ? gf : t);
+  return a < 0.001953125f /* 2^-9 */ ? half : (a < 128.0f ? t : gf);  // NaN fails a < 128: gf
 }
 
 // The SwiGLU half of a 64-column piece: v[j] (gate) and v[32 + j] (up), j < 32, are one row's
@@ -501,7 +510,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tile_coords((int)blockIdx.x + i * (int)gridDim.x, g.tiles_m, g.tiles_n, mt, nt);
         const bool two_halves = (int64_t)nt * kBN + 128 < g.N;
         for (int ks = 0; ks < g.k_steps; ++ks) {
-          if (!mbar_wait_warp(&sm.empty[stage], phase ^ 1u)) {
+          if (!pipe_wait_warp<kSwiglu>(&sm.empty[stage], phase ^ 1u)) {
             if (lane == 0) record_status(&g_gemm_status, kStatusTimeoutProducer);
             ok = false;
             break;
@@ -560,7 +569,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const uint64_t sad = sad0 + (uint64_t)(stage * ((4 * 512) >> 4));
           const uint64_t sbd = sbd0 + (uint64_t)(stage * ((8 * 512) >> 4));
           if (ks == 0 && i >= 1) {
-            if (!mbar_wait_warp(&sm.acc_empty, (uint32_t)((i - 1) & 1))) {
+            if (!pipe_wait_warp<kSwiglu>(&sm.acc_empty, (uint32_t)((i - 1) & 1))) {
               if (lane == 0) record_status(&g_gemm_status, kStatusTimeoutEpilogue);
               ok = false;
               break;
@@ -900,7 +909,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int64_t sa_row = (arow / kBM) * g.kb_total + T.kb0, sb_row = (T.brow / kBM) * g.kb_total + T.kb0;
         const int k_steps = (T.k_blocks + 3) / 4;
         for (int ks = 0; ks < k_steps; ++ks) {
-          if (!mbar_wait_warp(&sm.empty[stage], phase ^ 1u)) {
+          if (!pipe_wait_warp<kSwiglu>(&sm.empty[stage], phase ^ 1u)) {
             if (lane == 0) record_status(&g_gemm_status, kStatusTimeoutProducer);
             ok = false;
             break;
