@@ -113,3 +113,23 @@ def test_gate_up_interleave_round_trip():
     torch.testing.assert_close(g, x @ wg.t())
     torch.testing.assert_close(u, x @ wu.t())
     assert torch.equal(nv.merge_gate_up(g, u), x @ w.t())
+
+
+def test_swiglu_silu_closed_forms_match_torch():
+    """The SwiGLU epilogue takes silu(g), rounded to bf16, as bf16(g / 2) for |g| < 2^-9 and as g
+    for g >= 128 (and +inf, NaN), reading a table only in between (rb_nvfp4_selftest_silu checks the
+    whole mapping on the GPU).  Here the two closed forms are checked against torch's own bf16
+    F.silu on the CPU for every bf16 bit pattern they cover."""
+    import torch
+    import torch.nn.functional as F
+
+    bits = torch.arange(65536, dtype=torch.int32).to(torch.int16)
+    g = bits.view(torch.bfloat16)
+    gf = g.float()
+    ref = F.silu(g)
+    small = gf.abs() < 2.0 ** -9
+    big = gf >= 128.0
+    assert int(small.sum()) > 30000 and int(big.sum()) > 100
+    half = (gf * 0.5).bfloat16()
+    assert torch.equal(ref[small].view(torch.int16), half[small].view(torch.int16))
+    assert torch.equal(ref[big].view(torch.int16), g[big].view(torch.int16))
