@@ -946,7 +946,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const uint32_t idesc = idesc_nvf4_m256(width);
         const uint32_t acc = tmem + ((i & 1) ? kAcc1Col : 0);
         if (i >= 1) {
-          if (!mbar_wait_warp(&sm.acc_empty, (uint32_t)((i - 1) & 1))) {
+          if (!pipe_wait_warp<kSwiglu>(&sm.acc_empty, (uint32_t)((i - 1) & 1))) {
             if (lane == 0) record_status(&g_gemm_status, kStatusTimeoutEpilogue);
             break;
           }
