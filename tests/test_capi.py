@@ -133,3 +133,26 @@ def test_swiglu_silu_closed_forms_match_torch():
     half = (gf * 0.5).bfloat16()
     assert torch.equal(ref[small].view(torch.int16), half[small].view(torch.int16))
     assert torch.equal(ref[big].view(torch.int16), g[big].view(torch.int16))
+
+
+def test_feedforward_module_construction_on_cpu():
+    """FP4FeedForward.from_feedforward interleaves radiance's gate_proj / up_proj weights and biases
+    and copies down_proj; the gate/up pair splits back unchanged; a CPU input is refused (there is no
+    CPU path)."""
+    import torch
+    import torch.nn as nn
+
+    import radiance_b200.nvfp4 as nv
+
+    torch.manual_seed(0)
+    src = nn.Module()
+    src.gate_proj, src.up_proj, src.down_proj = nn.Linear(64, 96), nn.Linear(64, 96), nn.Linear(96, 64)
+    ff = nv.FP4FeedForward.from_feedforward(src)
+    assert ff.gate_up.weight.shape == (192, 64) and ff.gate_up.hidden_features == 96
+    g, u = ff.gate_up.gate_up_weights()
+    assert torch.equal(g, src.gate_proj.weight) and torch.equal(u, src.up_proj.weight)
+    assert torch.equal(ff.gate_up.bias, nv.interleave_gate_up(src.gate_proj.bias, src.up_proj.bias))
+    assert torch.equal(ff.down_proj.weight, src.down_proj.weight)
+    # Without an sm_100 GPU the reference's actionable message comes first; with one, the CPU input.
+    with pytest.raises(RuntimeError, match="needs NVFP4 support|no CPU path"):
+        ff(torch.randn(128, 64))
