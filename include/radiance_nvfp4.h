@@ -155,6 +155,20 @@ int rb_nvfp4_gemm_allgather(const void* a_packed, const void* a_scale, const voi
                             void* const* peer_out, int npeers, void* stream);
 
 /*
+ * The optimizer's last in-place step on a weight fused with the start of its cache refresh:
+ * w <- w + alpha * u elementwise (radiance's Muon step ends with target.add_(orthogonalize(u),
+ * alpha=-lr*scale), src/radiance/optim.py:518, and linear.py:193-210 then re-quantizes the weight),
+ * and *gs_out = the updated weight's global scale as rb_nvfp4_global_scale computes it.  Each element
+ * is one fp32 fused multiply-add of the widened operands, rounded once to w's dtype.
+ *   w, u      : n contiguous elements each of w_dtype / u_dtype (RB_DTYPE_BF16 or RB_DTYPE_F32);
+ *               w is updated in place.
+ *   workspace : the 8-byte workspace of rb_nvfp4_global_scale (zeroed before the first call, left
+ *               zeroed; calls ordered on one stream can share it).
+ */
+int rb_nvfp4_update_global_scale(void* w, int w_dtype, const void* u, int u_dtype, int64_t n, float alpha,
+                                 float* gs_out, void* workspace, void* stream);
+
+/*
  * rb_nvfp4_gemm for a SwiGLU producer (bf16 output): the gate/up projection of radiance's
  * FeedForward, h = F.silu(gate_proj(x)) * up_proj(x) (src/radiance/model/ffn.py:32), with the
  * activation and the global scale of h -- the next linear's quantizer input -- computed in the

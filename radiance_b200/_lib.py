@@ -45,6 +45,9 @@ SIGNATURES: dict[str, tuple] = {
         [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _c_void_p, _c_void_p, _c_void_p, _int,
          _c_void_p, _i64, _c_void_p, _i64, _c_void_p, _c_void_p, _c_void_p],
     ),
+    "rb_nvfp4_update_global_scale": (
+        _int, [_c_void_p, _int, _c_void_p, _int, _i64, ctypes.c_float, _c_void_p, _c_void_p, _c_void_p],
+    ),
     "rb_nvfp4_global_scale_colsum_workspace": (ctypes.c_size_t, [_int, _i64, _i64]),
     "rb_nvfp4_global_scale_colsum": (_int, [_c_void_p, _int, _i64, _i64, _i64, _c_void_p, _c_void_p, _c_void_p,
                                             _c_void_p]),

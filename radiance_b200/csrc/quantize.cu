@@ -1091,6 +1091,59 @@ __global__ void __launch_bounds__(256) selftest_scale_kernel(const float* amax, 
   if ((threadIdx.x & 31) == 0 && bad) atomicAdd(mismatches, bad);
 }
 
+// The optimizer's last in-place step on a weight, w <- w + alpha * u (radiance's Muon step ends
+// with target.add_(orthogonalize(u), alpha=-lr*scale), src/radiance/optim.py:518), with the global
+// scale of the updated weight (quantize.py:205-213) from the same pass.  The weight's cache refresh
+// can then quantize both layouts without a separate amax read.  Each element: one fp32 fused
+// multiply-add of the widened operands, rounded once to w's dtype.  n elements, contiguous; ws is the
+// global-scale workspace ({max bits, ticket}, zero on entry, left zero).
+template <bool W_F32, bool U_F32>
+__global__ void __launch_bounds__(512) update_global_scale_kernel(void* w, const void* u, int64_t n, float alpha,
+                                                                  uint32_t* ws, float* gs_out) {
+  uint32_t m = 0;  // max of |w'| as fp32 bit patterns
+  const int64_t gtid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  auto load = [](const void* p, int64_t e, bool f32) -> float {
+    return f32 ? reinterpret_cast<const float*>(p)[e]
+               : __uint_as_float((uint32_t)reinterpret_cast<const uint16_t*>(p)[e] << 16);
+  };
+  for (int64_t e = gtid; e < n; e += stride) {
+    const float r = __fmaf_rn(alpha, load(u, e, U_F32), load(w, e, W_F32));
+    uint32_t rb;
+    if constexpr (W_F32) {
+      reinterpret_cast<float*>(w)[e] = r;
+      rb = __float_as_uint(r);
+    } else {
+      const __nv_bfloat16 h = __float2bfloat16_rn(r);
+      const uint16_t hb = *reinterpret_cast<const uint16_t*>(&h);
+      reinterpret_cast<uint16_t*>(w)[e] = hb;
+      rb = (uint32_t)hb << 16;
+    }
+    m = max(m, rb & 0x7FFFFFFFu);
+  }
+  m = __reduce_max_sync(0xFFFFFFFFu, m);
+  __shared__ uint32_t red[16];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = m;
+  __syncthreads();
+  if (warp == 0) {
+    m = lane < (int)(blockDim.x >> 5) ? red[lane] : 0u;
+    m = __reduce_max_sync(0xFFFFFFFFu, m);
+    if (lane == 0) {
+      atomicMax(&ws[0], m);
+      __threadfence();
+      if (atomicAdd(&ws[1], 1u) == gridDim.x - 1) {
+        __threadfence();
+        const uint32_t mb = atomicExch(&ws[0], 0u);
+        atomicExch(&ws[1], 0u);
+        float gs = __fdiv_rn(__uint_as_float(mb), 2688.0f);
+        gs = (gs < 1e-12f) ? 1e-12f : gs;  // clamp(min=1e-12); NaN passes through as in torch
+        *gs_out = gs;
+      }
+    }
+  }
+}
+
 }  // namespace rb
 
 // =============================================================================================
@@ -1209,6 +1262,42 @@ int rb_nvfp4_global_scale(const void* x, int dtype, int64_t rows, int64_t cols, 
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     rb_host::set_error("nvfp4 global_scale launch failed: %s", cudaGetErrorString(e));
+    return RB_ERR_CUDA;
+  }
+  return RB_OK;
+}
+
+int rb_nvfp4_update_global_scale(void* w, int w_dtype, const void* u, int u_dtype, int64_t n, float alpha,
+                                 float* gs_out, void* workspace, void* stream) {
+  if (gs_out == nullptr || workspace == nullptr || (n > 0 && (w == nullptr || u == nullptr)) || n < 0) {
+    rb_host::set_error("nvfp4 update_global_scale: null pointer or negative size");
+    return RB_ERR_ARG;
+  }
+  if ((w_dtype != RB_DTYPE_BF16 && w_dtype != RB_DTYPE_F32) || (u_dtype != RB_DTYPE_BF16 && u_dtype != RB_DTYPE_F32)) {
+    rb_host::set_error("nvfp4 update_global_scale: unsupported dtypes %d, %d", w_dtype, u_dtype);
+    return RB_ERR_ARG;
+  }
+  if (!device_is_sm100()) {
+    rb_host::set_error("nvfp4 update_global_scale: the current device is not an sm_100 GPU");
+    return RB_ERR_DEVICE;
+  }
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (n == 0) {
+    rb::fill_float_kernel<<<1, 1, 0, s>>>(gs_out, 1e-12f);
+  } else {
+    const int sms = rb_host::num_sms(rb_host::current_device());
+    int64_t grid = (n + 4 * 512 - 1) / (4 * 512);
+    if (grid > 8 * sms) grid = 8 * sms;
+    uint32_t* ws = reinterpret_cast<uint32_t*>(workspace);
+    const bool wf = w_dtype == RB_DTYPE_F32, uf = u_dtype == RB_DTYPE_F32;
+    if (wf && uf) rb::update_global_scale_kernel<true, true><<<(int)grid, 512, 0, s>>>(w, u, n, alpha, ws, gs_out);
+    else if (wf) rb::update_global_scale_kernel<true, false><<<(int)grid, 512, 0, s>>>(w, u, n, alpha, ws, gs_out);
+    else if (uf) rb::update_global_scale_kernel<false, true><<<(int)grid, 512, 0, s>>>(w, u, n, alpha, ws, gs_out);
+    else rb::update_global_scale_kernel<false, false><<<(int)grid, 512, 0, s>>>(w, u, n, alpha, ws, gs_out);
+  }
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    rb_host::set_error("nvfp4 update_global_scale launch failed: %s", cudaGetErrorString(e));
     return RB_ERR_CUDA;
   }
   return RB_OK;

@@ -37,6 +37,7 @@ from .quantize import (
     split_gate_up,
     swiglu_mm,
     unpack_nibbles,
+    update_and_global_scale_,
 )
 
 __all__ = [
@@ -74,4 +75,5 @@ __all__ = [
     "split_gate_up",
     "swiglu_mm",
     "unpack_nibbles",
+    "update_and_global_scale_",
 ]

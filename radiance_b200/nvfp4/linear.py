@@ -41,6 +41,7 @@ from .quantize import (
     merge_gate_up,
     split_gate_up,
     swiglu_mm,
+    update_and_global_scale_,
 )
 
 
@@ -180,6 +181,21 @@ class FP4Linear(nn.Linear):
         global_scale_of(w, out=self._w_fwd_gs)
         if reduce_global_scale is not None:
             reduce_global_scale(self._w_fwd_gs)
+        self._w_dgrad_gs.copy_(self._w_fwd_gs)
+        quantize_into_(
+            w, global_scale=self._w_fwd_gs,
+            row=(self._w_fwd_packed, self._w_fwd_scale), col=(self._w_dgrad_packed, self._w_dgrad_scale),
+        )
+        self._cache_valid = True
+
+    @torch.no_grad()
+    def apply_update_and_refresh_(self, update: torch.Tensor, alpha: float) -> None:
+        """The optimizer's last in-place step on this weight, ``weight.add_(update, alpha=alpha)``
+        (radiance's Muon step, optim.py:518), fused with the cache refresh: one kernel applies the
+        update and computes the new weight's global scale, then one pass quantizes both layouts.
+        Same cache contents as ``refresh_fp4_cache()`` after the update, without its amax read."""
+        w = self.weight.data
+        update_and_global_scale_(w, update, alpha, out=self._w_fwd_gs)
         self._w_dgrad_gs.copy_(self._w_fwd_gs)
         quantize_into_(
             w, global_scale=self._w_fwd_gs,

@@ -237,6 +237,37 @@ def global_scale_of(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.T
     return out
 
 
+def update_and_global_scale_(w: torch.Tensor, update: torch.Tensor, alpha: float,
+                             out: torch.Tensor | None = None) -> torch.Tensor:
+    """``w.add_(update, alpha=alpha)`` and ``global_scale_of(w)`` of the result in one pass.
+
+    The last in-place step of radiance's Muon update (``target.add_(orthogonalize(u),
+    alpha=-lr*scale)``, src/radiance/optim.py:518) fused with the amax the weight's cache refresh
+    needs (linear.py:193-210).  Each element is one fp32 fused multiply-add of the widened operands,
+    rounded once to ``w``'s dtype.  ``w`` (bf16 or fp32) and ``update`` (bf16 or fp32, same shape)
+    must be contiguous CUDA tensors; returns the 0-d fp32 global scale (``out`` when given).
+    """
+    _require_cuda(w, "nvfp4.update_and_global_scale_")
+    if update.shape != w.shape:
+        raise ValueError(f"nvfp4.update_and_global_scale_: update {tuple(update.shape)} vs weight {tuple(w.shape)}")
+    if not w.is_contiguous():
+        raise ValueError("nvfp4.update_and_global_scale_: the weight must be contiguous (it is updated in place)")
+    lib = _lib.load()
+    u = update.contiguous()
+    if u.dtype not in (torch.bfloat16, torch.float32):
+        u = u.float()
+    if out is None:
+        out = torch.empty((), dtype=torch.float32, device=w.device)
+    _lib.check(
+        lib.rb_nvfp4_update_global_scale(
+            w.data_ptr(), _dtype_code(w), u.data_ptr(), _dtype_code(u), w.numel(), float(alpha), out.data_ptr(),
+            _workspace(w.device).data_ptr(), _stream_ptr(w.device),
+        ),
+        "nvfp4.update_and_global_scale_",
+    )
+    return out
+
+
 _COLSUM_WS: dict[tuple[torch.device, int], torch.Tensor] = {}
 
 

@@ -156,3 +156,12 @@ def test_feedforward_module_construction_on_cpu():
     # Without an sm_100 GPU the reference's actionable message comes first; with one, the CPU input.
     with pytest.raises(RuntimeError, match="needs NVFP4 support|no CPU path"):
         ff(torch.randn(128, 64))
+
+
+def test_update_global_scale_contract_is_checked_on_the_host():
+    lib = _lib.load()
+    buf = ctypes.c_void_p(256)
+    assert lib.rb_nvfp4_update_global_scale(buf, 7, buf, 0, 16, ctypes.c_float(1.0), buf, buf, None) == 2
+    assert "dtypes" in lib.rb_nvfp4_last_error().decode()
+    assert lib.rb_nvfp4_update_global_scale(None, 0, buf, 0, 16, ctypes.c_float(1.0), buf, buf, None) == 2
+    assert lib.rb_nvfp4_update_global_scale(buf, 0, buf, 0, -1, ctypes.c_float(1.0), buf, buf, None) == 2
