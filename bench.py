@@ -3,13 +3,14 @@
 Workload: one dense transformer block's linears -- QKV 2048->6144,
 O 2048->2048, gate/up 2048->11264, down 5632->2048 -- forward + dgrad + wgrad through
 ``radiance_b200.nvfp4.FP4Linear`` with the default recipe (stochastic rounding and Hadamard on,
-packed activation saving on), 16384 tokens per GPU, weights ~N(0, 0.02), activations ~N(0, 1),
-upstream gradients ~N(0, 1e-3).  A step = one micro-batch forward + backward of the four linears.
-Token rows shard across ranks with no data-path collective (weak scaling: every rank runs its own
-16384-token micro-batch; the data-parallel gradient all-reduce belongs to the optimizer, not to
-this path).
+packed activation saving on), weights ~N(0, 0.02), activations ~N(0, 1), upstream gradients
+~N(0, 1e-3).  A step = the job's 16384 tokens (batch 8 x seq 2048): the four forwards, then the four
+backwards.  With N ranks the tokens are sharded (16384/N per rank, strong scaling) and each linear's
+fp32 weight gradient is reduce-scattered over the ranks inside the step, as data-parallel training
+needs; the weak-scaled replica number (16384 tokens on every rank, no reduction) is reported beside
+it.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 2|3|4|5]
 
 Prints one JSON line (rank 0).  ``--impl reference`` times the reference's CPU implementation of
 the path (the NumPy restatement of radiance's pure-torch NVFP4 emulation in ``oracle/``) on the
@@ -32,10 +33,11 @@ if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
 D_MODEL = 2048
-TOKENS_PER_GPU = 16384
+TOKENS = 16384  # tokens per step of the whole job (batch 8 x seq 2048)
 LAYERS = [("qkv", 2048, 6144), ("o", 2048, 2048), ("gate_up", 2048, 11264), ("down", 5632, 2048)]
-STEP_FLOPS = 6.0 * TOKENS_PER_GPU * sum(k * n for _, k, n in LAYERS)  # 5.051e12
-METRIC = "NVFP4 linear fwd+bwd TFLOPS (BASELINE config 3 block linears, 16384 tokens/GPU)"
+LAYER_KN = sum(k * n for _, k, n in LAYERS)
+STEP_FLOPS = 6.0 * TOKENS * LAYER_KN  # 5.051e12 per step of the job
+METRIC = "NVFP4 linear fwd+bwd TFLOPS (BASELINE config 3 block linears, 16384 tokens per step, token-sharded)"
 
 # Average DRAM bytes (read + write) per GEMM launch of this workload's twelve GEMMs, from one `ncu`
 # capture (profiles/gemm_block_step_traffic.md).
@@ -135,13 +137,14 @@ def _dist_setup(args):
     return rank, world, local
 
 
-def _make_layers(device, seed):
+def _make_layers(device):
+    """The block's four linears, identical on every rank (data-parallel replicas of one model)."""
     import torch
 
     from radiance_b200 import nvfp4 as nv
 
-    g = torch.Generator(device="cpu").manual_seed(seed)
-    layers, xs, dys = [], [], []
+    g = torch.Generator(device="cpu").manual_seed(1234)
+    layers = []
     for name, k, n in LAYERS:
         lin = nv.FP4Linear(k, n, bias=False, recipe=nv.FP4Recipe())
         with torch.no_grad():
@@ -149,33 +152,163 @@ def _make_layers(device, seed):
         lin = lin.to(device)
         lin.refresh_fp4_cache()
         layers.append(lin)
-        xs.append((torch.randn(TOKENS_PER_GPU, k, generator=g)).to(torch.bfloat16))
-        dys.append((torch.randn(TOKENS_PER_GPU, n, generator=g) * 1e-3).to(torch.bfloat16))
-    return layers, xs, dys
+    return layers
 
 
-def _step(layers, xs, dys, outs=None):
+def _make_inputs(tokens, seed):
+    """This rank's token shard: activations ~N(0,1) and upstream gradients ~N(0,1e-3), bf16, on the host."""
     import torch
 
-    for i, lin in enumerate(layers):
-        x = xs[i].detach().requires_grad_(True)
-        y = lin(x)
-        gx, gw = torch.autograd.grad(y, (x, lin.weight), dys[i])
-        if outs is not None:
-            outs.append((gx, gw))
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    xs, dys = [], []
+    for name, k, n in LAYERS:
+        xs.append(torch.randn(tokens, k, generator=g).to(torch.bfloat16))
+        dys.append((torch.randn(tokens, n, generator=g) * 1e-3).to(torch.bfloat16))
+    return xs, dys
+
+
+class BlockStep:
+    """One training step of the block's linears on this rank's token shard: the four forwards, then
+    the four backwards in reverse order (as a block's backward runs).  With several ranks, each
+    linear's fp32 dW is reduce-scattered over the ranks (ZeRO-style: rank r keeps the summed rows
+    r*N/g .. (r+1)*N/g) on a side stream, issued from the layer's wgrad hook the moment its wgrad GEMM
+    has produced dW, so the reduction overlaps that layer's dgrad and the layers still to come."""
+
+    def __init__(self, layers, world, device, reduce=True):
+        import torch
+
+        self.layers, self.world = layers, world
+        self.reduce = reduce and world > 1
+        self.side = torch.cuda.Stream(device)
+        self.shards = [torch.empty(lin.out_features // world, lin.in_features, device=device) for lin in layers]
+        self.reduce_bytes = sum(lin.weight.numel() * 4 for lin in layers) if self.reduce else 0
+        self._pending = []
+
+    def _hook(self, i):
+        import torch
+        import torch.distributed as dist
+
+        from radiance_b200.nvfp4 import _trace
+
+        def hook(grad_w):
+            self.side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(self.side):
+                tok = _trace.begin("reduce_scatter", grad_w.numel() * 4)
+                dist.reduce_scatter_tensor(self.shards[i], grad_w)
+                _trace.end(tok)
+            self._pending.append(grad_w)  # keeps dW alive until the side stream has consumed it
+        return hook
+
+    def __call__(self, xs, dys, outs=None):
+        import torch
+
+        if self.reduce:
+            for i, lin in enumerate(self.layers):
+                lin.wgrad_hook = self._hook(i)
+        ins, ys = [], []
+        for i, lin in enumerate(self.layers):
+            x = xs[i].detach().requires_grad_(True)
+            ins.append(x)
+            ys.append(lin(x))
+        for i in reversed(range(len(self.layers))):
+            gx, gw = torch.autograd.grad(ys[i], (ins[i], self.layers[i].weight), dys[i])
+            if outs is not None:
+                outs.append((i, gx, self.shards[i] if self.reduce else gw))
+        if self.reduce:
+            torch.cuda.current_stream().wait_stream(self.side)
+            self._pending.clear()
+            for lin in self.layers:
+                lin.wgrad_hook = None
+
+
+def _capture(fn):
+    """Capture fn() in a CUDA graph after two warm-up calls on a side stream; returns the graph."""
+    import torch
+
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(2):
+            fn()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        fn()
+    torch.cuda.synchronize()
+    return graph
+
+
+def _graph_kernel_times(fn, replays):
+    """Per-kind device time of one step, measured inside a CUDA graph of the step: the step is
+    captured with timing events around every library launch (and every reduce-scatter), replayed,
+    and the event pairs of each replay are summed.  Returns (per-kind totals averaged per step,
+    launches per step)."""
+    import torch
+
+    from radiance_b200.nvfp4 import _trace
+
+    with _trace.kernel_timer() as kt:
+        graph = _capture(fn)
+        # The two warm-up calls inside _capture recorded events too; keep only the captured ones.
+        per_step = kt.launches // 3
+        kt.records = kt.records[-per_step:]
+    totals: dict = {}
+    for _ in range(replays):
+        graph.replay()
+        torch.cuda.synchronize()
+        for kind, v in kt.summary().items():
+            t = totals.setdefault(kind, {"launches": 0, "ms": 0.0, "work": 0.0})
+            t["launches"] += v["launches"]
+            t["ms"] += v["ms"]
+            t["work"] += v["work"]
+    del graph
+    out = {k: {"launches": v["launches"] / replays, "ms": v["ms"] / replays, "work": v["work"] / replays}
+           for k, v in totals.items()}
+    launches = sum(v["launches"] for k, v in out.items() if k != "reduce_scatter")
+    return out, int(round(launches))
+
+
+def _timed_replays(run_step, steps, barrier, clocks=None):
+    """K replays between CUDA events, bracketed by a barrier and a synchronize on both sides."""
+    import torch
+
+    if clocks is not None:
+        clocks.start()
+    for _ in range(20):  # keep the GPU loaded while the clock sampler starts (untimed)
+        run_step()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    start.record()
+    for _ in range(steps):
+        run_step()
+    stop.record()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    clk = clocks.stop() if clocks is not None else None
+    return start.elapsed_time(stop), clk
 
 
 def run_ours(args):
     import torch
     import torch.distributed as dist
 
-    from radiance_b200.nvfp4 import _trace
-
     rank, world, local = _dist_setup(args)
     device = torch.device("cuda", local if world > 1 else 0)
-    layers, xs_host, dys_host = _make_layers(device, seed=1234 + rank)
+    if args.tokens_per_rank:
+        tokens, scaling = args.tokens_per_rank, "weak"
+    else:
+        if TOKENS % (128 * world):
+            raise SystemExit(f"{TOKENS} tokens do not shard into multiples of 128 over {world} ranks")
+        tokens, scaling = TOKENS // world, "strong"
+    step_flops = 6.0 * tokens * LAYER_KN  # this rank's GEMM work per step
+    layers = _make_layers(device)
+    xs_host, dys_host = _make_inputs(tokens, seed=1000 + rank)
     xs = [x.to(device) for x in xs_host]
     dys = [d.to(device) for d in dys_host]
+    step = BlockStep(layers, world, device)
 
     def barrier():
         if world > 1:
@@ -190,157 +323,73 @@ def run_ours(args):
 
     # ---- device-resident timing (value) ------------------------------------------------------
     for _ in range(args.warmup):
-        _step(layers, xs, dys)
+        step(xs, dys)
     torch.cuda.synchronize()
     visible = os.environ.get("CUDA_VISIBLE_DEVICES")
     phys = visible.split(",")[torch.cuda.current_device()] if visible else str(torch.cuda.current_device())
-    clocks = ClockSampler(phys)
-    barrier()
-    torch.cuda.synchronize()
-    # The step is captured once in a CUDA graph and replayed: every kernel of the step runs on every
-    # replay; the graph removes the host's per-launch overhead, which with eight processes sharing
-    # the host's cores leaves gaps between kernels.  --eager times the Python loop instead.
-    run_step = (lambda: _step(layers, xs, dys))
+    # The step is captured once in a CUDA graph and replayed: every kernel and every reduce-scatter
+    # of the step runs on every replay; the graph removes the host's per-launch overhead, which with
+    # eight processes sharing the host's cores leaves gaps between kernels.  --eager times the
+    # Python loop instead.
     graph = None
+    run_step = (lambda: step(xs, dys))
     if not args.eager:
-        side = torch.cuda.Stream()
-        side.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(side):
-            for _ in range(2):
-                _step(layers, xs, dys)
-        torch.cuda.current_stream().wait_stream(side)
-        torch.cuda.synchronize()
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            _step(layers, xs, dys)
-        torch.cuda.synchronize()
+        graph = _capture(run_step)
         run_step = graph.replay
-    clocks.start()
-    for _ in range(20):  # keep the GPU loaded while the sampler starts up (untimed)
-        run_step()
-    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
-    torch.cuda.synchronize()
-    start.record()
-    for _ in range(args.steps):
-        run_step()
-    stop.record()
-    torch.cuda.synchronize()
-    barrier()
-    torch.cuda.synchronize()
-    clk = clocks.stop()
-    ms = start.elapsed_time(stop)
+    ms, clk = _timed_replays(run_step, args.steps, barrier, ClockSampler(phys))
     ms_max = max_over_ranks(ms)
-    # Per-kernel breakdown (the roofline's live timing): the same steps again, eagerly, with CUDA
-    # events around every launch.  Not part of `value`.
-    kt_steps = max(3, min(args.steps, 50))
-    with _trace.kernel_timer() as kt:
-        for _ in range(kt_steps):
-            _step(layers, xs, dys)
-        torch.cuda.synchronize()
-    per_kind = {k: {kk: (int(round(vv * args.steps / kt_steps)) if kk == "launches" else vv * args.steps / kt_steps)
-                    for kk, vv in v.items()} for k, v in kt.summary().items()}
-    launches = kt.launches * args.steps // kt_steps
+    per_kind, launches_per_step = _graph_kernel_times(lambda: step(xs, dys), replays=max(3, min(args.steps, 20)))
+    del graph, run_step
 
-    # ---- with the data-parallel weight-gradient reduction (N > 1) -----------------------------
-    # Token sharding needs no collective on the fwd/dgrad path, but wgrad contracts over tokens:
-    # a data-parallel job sums each linear's fp32 dW across ranks.  Measured separately, the way
-    # DDP overlaps it (one async all-reduce per linear, issued as its dW is produced).
-    dp = None
-    if world > 1:
-        def step_allreduce():
-            works = []
-            for i, lin in enumerate(layers):
-                x = xs[i].detach().requires_grad_(True)
-                y = lin(x)
-                _gx, gw = torch.autograd.grad(y, (x, lin.weight), dys[i])
-                works.append(dist.all_reduce(gw, async_op=True))
-            for w in works:
-                w.wait()
-
-        dp_steps = max(3, min(args.steps, 50))
+    # ---- weak-scaled replicas (N > 1): every rank a whole 16384-token micro-batch, no collective
+    weak = None
+    if world > 1 and not args.tokens_per_rank:
+        wx_host, wdy_host = _make_inputs(TOKENS, seed=2000 + rank)
+        wxs = [x.to(device) for x in wx_host]
+        wdys = [d.to(device) for d in wdy_host]
+        wstep = BlockStep(layers, world, device, reduce=False)
         for _ in range(3):
-            step_allreduce()
+            wstep(wxs, wdys)
+        wgraph = _capture(lambda: wstep(wxs, wdys))
+        wms, _ = _timed_replays(wgraph.replay, args.steps, barrier)
+        wms_max = max_over_ranks(wms) / args.steps
+        weak = {"value": round(world * 6.0 * TOKENS * LAYER_KN / (wms_max * 1e-3) / 1e12, 2), "unit": "TFLOPS",
+                "ms_per_step": round(wms_max, 4), "tokens_per_gpu": TOKENS, "scaling": "weak",
+                "what": "every rank runs its own 16384-token micro-batch, no gradient reduction (replicas)"}
+        del wgraph, wxs, wdys
         torch.cuda.synchronize()
-        barrier()
-        torch.cuda.synchronize()
-        ds, de = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        ds.record()
-        for _ in range(dp_steps):
-            step_allreduce()
-        de.record()
-        torch.cuda.synchronize()
-        dp_ms = max_over_ranks(ds.elapsed_time(de)) / dp_steps
-        dp_bytes = sum(lin.weight.numel() * 4 for lin in layers)
-        dp = {"value": round(world * STEP_FLOPS / (dp_ms * 1e-3) / 1e12, 2), "unit": "TFLOPS",
-              "ms_per_step": round(dp_ms, 4), "allreduce_bytes_per_step": dp_bytes,
-              "what": "same step plus an async NCCL all-reduce of each linear's fp32 dW (overlapped)"}
 
     # ---- end-to-end through the public API with host buffers (e2e) --------------------------
-    pinned_x = [x.pin_memory() for x in xs_host]
-    pinned_dy = [d.pin_memory() for d in dys_host]
-    dev_x = [torch.empty_like(x, device=device) for x in xs_host]
-    dev_dy = [torch.empty_like(d, device=device) for d in dys_host]
-    result_host = torch.empty(D_MODEL, dtype=torch.float32).pin_memory()
-    h2d = sum(t.numel() * t.element_size() for t in pinned_x + pinned_dy)
-    d2h = result_host.numel() * result_host.element_size()
+    e2e = _e2e(layers, xs_host, dys_host, step, device, world, args, barrier, max_over_ranks)
+    reducing, reduce_bytes = step.reduce, step.reduce_bytes
+    del xs, dys, step
 
-    # Two sets of device inputs: while step s computes on one set, the copy stream uploads step
-    # s+1's inputs into the other (the way a data loader feeds a training loop), so a step costs
-    # the larger of its host-to-device copy and its compute.
-    dev_sets = [(dev_x, dev_dy), ([torch.empty_like(x, device=device) for x in xs_host],
-                                  [torch.empty_like(d, device=device) for d in dys_host])]
-    copy_stream = torch.cuda.Stream(device)
-    copied = [torch.cuda.Event(), torch.cuda.Event()]
-    consumed = [torch.cuda.Event(), torch.cuda.Event()]
-    used = [False, False]
-
-    def issue_copy(b):
-        with torch.cuda.stream(copy_stream):
-            if used[b]:
-                copy_stream.wait_event(consumed[b])
-            for i in range(len(layers)):
-                dev_sets[b][0][i].copy_(pinned_x[i], non_blocking=True)
-                dev_sets[b][1][i].copy_(pinned_dy[i], non_blocking=True)
-            copied[b].record(copy_stream)
-
-    def e2e_run(n):
-        copy_stream.wait_stream(torch.cuda.current_stream())  # the first copy starts inside the timing
-        issue_copy(0)
-        for s_ in range(n):
-            b = s_ % 2
-            if s_ + 1 < n:
-                issue_copy(1 - b)
-            torch.cuda.current_stream().wait_event(copied[b])
-            outs = []
-            _step(layers, dev_sets[b][0], dev_sets[b][1], outs)
-            consumed[b].record()
-            used[b] = True
-            result_host.copy_(outs[0][1][0], non_blocking=True)  # first row of dW(qkv)
-
-    e2e_steps = max(3, min(args.steps, 20))
-    e2e_run(max(3, args.warmup))
-    torch.cuda.synchronize()
-    barrier()
-    torch.cuda.synchronize()
-    es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    es.record()
-    e2e_run(e2e_steps)
-    ee.record()
-    torch.cuda.synchronize()
-    e2e_ms = max_over_ranks(es.elapsed_time(ee)) / e2e_steps
+    # ---- configs 4 and 5 as sub-records (with their parity checks at N > 1) --------------------
+    subs = {}
+    if not args.no_subrecords and not args.tokens_per_rank:
+        for name, fn, n_steps in (("config4", measure_config4, max(3, min(args.steps, 50))),
+                                  ("config5", measure_config5, max(3, min(args.steps, 10)))):
+            torch.cuda.empty_cache()
+            try:
+                rec = fn(args, rank, world, device, barrier, max_over_ranks, n_steps)
+            except Exception as e:  # a sub-record must not take the headline line down with it
+                rec = {"error": f"{type(e).__name__}: {e}"[:400]}
+            if rank == 0:
+                subs[name] = rec
 
     if rank == 0:
         peaks, peak_kind = _peaks()
         ms_step = ms_max / args.steps
-        value = world * STEP_FLOPS / (ms_step * 1e-3) / 1e12
+        job_flops = step_flops * world
+        value = job_flops / (ms_step * 1e-3) / 1e12
         gemm = per_kind.get("gemm", {"launches": 0, "ms": 0.0, "work": 0.0})
         quant = per_kind.get("quantize", {"launches": 0, "ms": 0.0, "work": 0.0})
         amax = per_kind.get("amax", {"launches": 0, "ms": 0.0, "work": 0.0})
+        rs = per_kind.get("reduce_scatter")
         fp4_peak = 4.0 * peaks["bf16_tflops"]
-        gemm_ms_launch = gemm["ms"] / max(gemm["launches"], 1)
         gemm_tflops = gemm["work"] / (gemm["ms"] * 1e-3) / 1e12 if gemm["ms"] else None
-        traffic = GEMM_DRAM_BYTES_PER_LAUNCH
+        quant_gbs = quant["work"] / (quant["ms"] * 1e-3) / 1e9 if quant["ms"] else None
+        hbm = peaks["hbm_gbs"]
         line = {
             "metric": METRIC,
             "value": round(value, 2),
@@ -350,7 +399,7 @@ def run_ours(args):
             "warmup": args.warmup,
             "ms_per_step": round(ms_step, 4),
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": scaling,
             "vs_baseline": None,
             "dtype": "nvfp4 (e2m1 x e4m3 block scales, fp32 accumulate; bf16 in/out, fp32 dW)",
             "data": "synthetic (seeded; W~N(0,0.02), X~N(0,1), dY~N(0,1e-3))",
@@ -358,22 +407,26 @@ def run_ours(args):
                 "workload": "config3: dense block linears fwd+dgrad+wgrad via FP4Linear",
                 "d_model": D_MODEL,
                 "layers": {n: [k, o] for n, k, o in LAYERS},
-                "tokens_per_gpu": TOKENS_PER_GPU,
-                "global_batch_tokens": TOKENS_PER_GPU * world,
+                "global_batch_tokens": tokens * world,
+                "tokens_per_gpu": tokens,
                 "recipe": "grad_gemms, stochastic_rounding, hadamard, save_activations",
-                "parallelism": f"token-sharded dp{world} (no data-path collective)",
-                "l2": "inputs larger than L2 (about 1 GB of activations and gradients per step)",
+                "parallelism": (f"token-sharded dp{world}: 16384 tokens per step split over the ranks, each linear's "
+                                "fp32 dW reduce-scattered (NCCL, overlapped from the wgrad hook) inside the step")
+                if world > 1 and reducing else "one GPU" if world == 1 else f"{world} replicas",
+                "grad_reduce_bytes_per_step": reduce_bytes,
+                "l2": "inputs larger than L2 (about 1 GB of activations and gradients per 16384 tokens)",
                 "timing": "eager Python step loop" if args.eager else
-                          "the step captured in one CUDA graph, replayed K times (per-kernel times from an eager pass)",
+                          "the step captured in one CUDA graph, replayed K times; per-kernel times from event pairs "
+                          "captured in a second graph of the same step",
             },
-            "tokens_per_s": round(world * TOKENS_PER_GPU / (ms_step * 1e-3), 1),
-            "gpu_launches": launches,
+            "tokens_per_s": round(tokens * world / (ms_step * 1e-3), 1),
+            "gpu_launches": launches_per_step * args.steps,
             "kernels": {
-                "gemm": {"launches": gemm["launches"], "ms": round(gemm["ms"], 3),
+                "gemm": {"launches_per_step": gemm["launches"], "ms_per_step": round(gemm["ms"], 4),
                          "TFLOPS": None if gemm_tflops is None else round(gemm_tflops, 1)},
-                "quantize": {"launches": quant["launches"], "ms": round(quant["ms"], 3),
-                             "GBps": round(quant["work"] / (quant["ms"] * 1e-3) / 1e9, 1) if quant["ms"] else None},
-                "amax": {"launches": amax["launches"], "ms": round(amax["ms"], 3),
+                "quantize": {"launches_per_step": quant["launches"], "ms_per_step": round(quant["ms"], 4),
+                             "GBps": None if quant_gbs is None else round(quant_gbs, 1)},
+                "amax": {"launches_per_step": amax["launches"], "ms_per_step": round(amax["ms"], 4),
                          "GBps": round(amax["work"] / (amax["ms"] * 1e-3) / 1e9, 1) if amax["ms"] else None},
             },
             "roofline": {
@@ -381,33 +434,125 @@ def run_ours(args):
                 "bound": "tensor",
                 "achieved": None if gemm_tflops is None else round(gemm_tflops, 1),
                 "peak": round(fp4_peak, 1),
-                "peak_basis": f"4 x {peak_kind} dense bf16 ({peaks['bf16_tflops']} TF/s): B200 NVFP4 dense rate is 4x bf16; nominal 9000",
+                "peak_basis": f"4 x {peak_kind} dense bf16 ({peaks['bf16_tflops']} TF/s): B200 NVFP4 dense rate is 4x "
+                              "bf16; nominal 9000",
                 "unit": "TFLOP/s",
                 "frac": None if gemm_tflops is None else round(gemm_tflops / fp4_peak, 4),
-                "traffic": traffic,
+                "frac_of_nominal_9000": None if gemm_tflops is None else round(gemm_tflops / 9000.0, 4),
+                "traffic": GEMM_DRAM_BYTES_PER_LAUNCH if tokens == TOKENS else None,
                 "flops_per_launch": round(gemm["work"] / max(gemm["launches"], 1)),
-                "ms_per_launch": round(gemm_ms_launch, 4),
+                "ms_per_launch": round(gemm["ms"] / max(gemm["launches"], 1), 5),
             },
-            "e2e": {
-                "value": round(world * STEP_FLOPS / (e2e_ms * 1e-3) / 1e12, 2),
-                "unit": "TFLOPS",
-                "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h,
-                "ms_per_step": round(e2e_ms, 3),
-                "path": "FP4Linear forward/backward (public API), inputs copied from pinned host memory each step "
-                        "(step s+1's copies overlap step s's compute on a second stream)",
+            "roofline_quantizer": {
+                "kernel": "nvfp4_quantize_kernel (both layouts; Hadamard colblock; SR on gradients)",
+                "bound": "hbm",
+                "achieved": None if quant_gbs is None else round(quant_gbs, 1),
+                "peak": hbm,
+                "unit": "GB/s",
+                "frac": None if quant_gbs is None else round(quant_gbs / hbm, 4),
+                "peak_basis": f"{peak_kind} HBM copy bandwidth",
+                "traffic": None,
+                "bytes_per_launch": round(quant["work"] / max(quant["launches"], 1)),
+                "ms_per_launch": round(quant["ms"] / max(quant["launches"], 1), 5),
             },
+            "e2e": e2e,
             "clocks": clk,
         }
-        if dp is not None:
-            line["with_dp_grad_allreduce"] = dp
+        if rs is not None:
+            line["kernels"]["reduce_scatter"] = {
+                "calls_per_step": rs["launches"], "ms_per_step": round(rs["ms"], 4),
+                "GBps_algbw": round(rs["work"] / (rs["ms"] * 1e-3) / 1e9, 1) if rs["ms"] else None,
+                "note": "NCCL on a side stream, overlapped with the GEMMs; its time is not additive"}
+        if weak is not None:
+            line["weak_replicas"] = weak
+        for name, rec in subs.items():
+            line[name] = rec
+        flags = [rec.get("parity_ok") for rec in subs.values() if "parity_ok" in rec]
+        if flags:
+            line["parity_ok"] = all(flags)
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(budget_s=args.cpu_budget)
         print(json.dumps(line), flush=True)
-    del graph, run_step
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def _e2e(layers, xs_host, dys_host, step, device, world, args, barrier, max_over_ranks):
+    """The same step through the public API with host buffers: every step copies its inputs from
+    pinned host memory and copies its results (dX of every linear, and this rank's dW rows -- the
+    reduce-scattered shard with several ranks) back to pinned host memory, inside the timed region.
+    Step s+1's uploads run on a copy stream during step s (double-buffered inputs, the way a data
+    loader feeds a training loop), and step s's downloads on another while step s+1 computes."""
+    import torch
+
+    pinned_x = [x.pin_memory() for x in xs_host]
+    pinned_dy = [d.pin_memory() for d in dys_host]
+    tokens = xs_host[0].shape[0]
+    out_dx = [torch.empty(tokens, k, dtype=torch.bfloat16).pin_memory() for _, k, _ in LAYERS]
+    out_dw = [torch.empty(n // world if step.reduce else n, k, dtype=torch.float32).pin_memory() for _, k, n in LAYERS]
+    h2d = sum(t.numel() * t.element_size() for t in pinned_x + pinned_dy)
+    d2h = sum(t.numel() * t.element_size() for t in out_dx + out_dw)
+    dev_sets = [([torch.empty_like(x, device=device) for x in xs_host],
+                 [torch.empty_like(d, device=device) for d in dys_host]) for _ in range(2)]
+    up, down = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    copied = [torch.cuda.Event(), torch.cuda.Event()]
+    consumed = [torch.cuda.Event(), torch.cuda.Event()]
+    used = [False, False]
+
+    def issue_copy(b):
+        with torch.cuda.stream(up):
+            if used[b]:
+                up.wait_event(consumed[b])
+            for i in range(len(LAYERS)):
+                dev_sets[b][0][i].copy_(pinned_x[i], non_blocking=True)
+                dev_sets[b][1][i].copy_(pinned_dy[i], non_blocking=True)
+            copied[b].record(up)
+
+    def run(n):
+        cur = torch.cuda.current_stream()
+        up.wait_stream(cur)  # the first upload starts inside the timing
+        issue_copy(0)
+        for s_ in range(n):
+            b = s_ % 2
+            if s_ + 1 < n:
+                issue_copy(1 - b)
+            cur.wait_event(copied[b])
+            step.side.wait_stream(down)  # the reduce-scatter reuses the dW shards the last download reads
+            outs = []
+            step(dev_sets[b][0], dev_sets[b][1], outs)
+            consumed[b].record()
+            used[b] = True
+            down.wait_stream(cur)
+            with torch.cuda.stream(down):
+                for i, gx, gw in outs:
+                    out_dx[i].copy_(gx, non_blocking=True)
+                    out_dw[i].copy_(gw, non_blocking=True)
+                    gx.record_stream(down)
+                    gw.record_stream(down)
+        cur.wait_stream(down)
+
+    e2e_steps = max(3, min(args.steps, 20))
+    run(max(3, args.warmup))
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    es.record()
+    run(e2e_steps)
+    ee.record()
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(es.elapsed_time(ee)) / e2e_steps
+    return {
+        "value": round(world * 6.0 * tokens * LAYER_KN / (e2e_ms * 1e-3) / 1e12, 2),
+        "unit": "TFLOPS",
+        "h2d_bytes_per_step": h2d,
+        "d2h_bytes_per_step": d2h,
+        "ms_per_step": round(e2e_ms, 3),
+        "path": "FP4Linear forward/backward (public API) per rank; inputs from pinned host memory each step "
+                "(uploads of step s+1 overlap step s), results (every dX and this rank's dW rows) copied back to "
+                "pinned host memory each step; eager launches",
+    }
 
 
 # --------------------------------------------------------------------------------------------------
@@ -520,111 +665,176 @@ def run_reference(args):
 # Config 4: MoE expert FFN (grouped NVFP4 GEMMs), experts partitioned across ranks
 # --------------------------------------------------------------------------------------------------
 C4_D, C4_E, C4_FFN, C4_TOKENS, C4_TOPK = 2048, 8, 1408, 16384, 2
-C4_FLOPS = 6.0 * C4_TOKENS * C4_TOPK * (C4_D * 2 * C4_FFN + C4_FFN * C4_D)  # 1.701e12 per rank
-C4_METRIC = "NVFP4 MoE expert linears fwd+bwd TFLOPS (BASELINE config 4: 8 experts, top-2, 16384 tokens/GPU)"
+C4_ROUTED = C4_TOKENS * C4_TOPK
+C4_FLOPS = 6.0 * C4_ROUTED * (C4_D * 2 * C4_FFN + C4_FFN * C4_D)  # 1.701e12 per step of the job
+C4_METRIC = "NVFP4 MoE expert FFN fwd+bwd TFLOPS (BASELINE config 4: 8 experts, top-2 over 16384 tokens)"
 
 
-def _c4_counts(src_rank: int):
-    """Tokens of source rank s routed to each expert: router logits ~N(0,1) (seed s), softmax, top-2."""
+def _c4_routing():
+    """The job's routing: router logits ~N(0,1) (seed 0) for 16384 tokens, softmax, top-2."""
     import torch
 
-    g = torch.Generator().manual_seed(src_rank)
-    logits = torch.randn(C4_TOKENS, C4_E, generator=g)
-    top = logits.softmax(-1).topk(C4_TOPK, dim=-1).indices
-    return torch.bincount(top.flatten(), minlength=C4_E)
+    logits = torch.randn(C4_TOKENS, C4_E, generator=torch.Generator().manual_seed(0))
+    return logits.softmax(-1).topk(C4_TOPK, dim=-1).indices
 
 
-def run_config4(args):
-    """One step = the expert FFN's two grouped linears (gate+up fused 2048->2816, down 1408->2048),
-    forward + dgrad + wgrad, on the rows this rank's experts receive.  With N ranks each rank owns
-    E/N experts and routes its own 16384 tokens; the routed rows travel to their expert's owner and
-    back with NCCL all-to-alls (dispatch before gate/up, combine after down, and the reverse pair for
-    the gradients), inside the timed region.  Work per rank is fixed as N grows (weak scaling)."""
+def _c4_source_pairs(top, s, world):
+    """(token, expert) pairs of source rank s (tokens s*T/N ..), sorted expert-major then by token:
+    the order of the source's send buffer."""
     import torch
-    import torch.distributed as dist
+
+    per = C4_TOKENS // world
+    tok = torch.arange(s * per, (s + 1) * per).repeat_interleave(C4_TOPK)
+    ex = top[s * per:(s + 1) * per].flatten()
+    order = torch.argsort(ex * C4_TOKENS + tok)
+    return tok[order], ex[order]
+
+
+class _MoEFFN:
+    """The expert FFN of config 4 for the experts of one rank: dispatch -> gate/up (grouped NVFP4)
+    -> SwiGLU (torch) -> down (grouped NVFP4) -> combine, the expert half of radiance's MoE layer
+    (BatchedExperts.forward, src/radiance/model/ffn.py:148-153, with its [gate | up] split)."""
+
+    def __init__(self, plan, w_gu, w_dn, device, recipe=None):
+        import torch
+
+        from radiance_b200.nvfp4.grouped import FP4GroupedLinear
+
+        per = len(plan.experts)
+        self.plan = plan
+        self.gate_up = FP4GroupedLinear(per, C4_D, 2 * C4_FFN, recipe=recipe, device=device)
+        self.down = FP4GroupedLinear(per, C4_FFN, C4_D, recipe=recipe, device=device)
+        with torch.no_grad():
+            self.gate_up.weight.copy_(w_gu[plan.experts])
+            self.down.weight.copy_(w_dn[plan.experts])
+        self.gate_up.refresh_fp4_cache()
+        self.down.refresh_fp4_cache()
+
+    def __call__(self, x_send, group=None):
+        import torch.nn.functional as F
+
+        from radiance_b200.nvfp4.expert_parallel import combine, dispatch
+
+        x_exp = dispatch(x_send, self.plan, group)
+        y_gu = self.gate_up(x_exp, self.plan.offsets)
+        h = F.silu(y_gu[:, :C4_FFN]) * y_gu[:, C4_FFN:]
+        return combine(self.down(h, self.plan.offsets), self.plan, group)
+
+
+def measure_config4(args, rank, world, device, barrier, max_over_ranks, steps):
+    """Config 4 for a fixed job of 16384 tokens: rank r routes tokens r*16384/N .. and owns experts
+    r*8/N ..; the routed rows go to their expert's owner and back with all-to-alls (dispatch before
+    gate/up, combine after down, the reverse pair for the gradients) inside the timed step.  With
+    N > 1, rank 0 also checks that its tokens' forward output through the expert-parallel exchange
+    equals the single-GPU expert FFN on the whole job, bit for bit.  Returns the record (rank 0)."""
+    import torch
 
     from radiance_b200.nvfp4 import _trace
-    from radiance_b200.nvfp4.grouped import FP4GroupedLinear, align_offsets
+    from radiance_b200.nvfp4.expert_parallel import ExpertParallelPlan
 
-    rank, world, local = _dist_setup(args)
-    if C4_E % world:
-        raise SystemExit(f"config 4 needs the {C4_E} experts to divide evenly over {world} ranks")
-    device = torch.device("cuda", local if world > 1 else 0)
-    per = C4_E // world
-    mine = list(range(rank * per, (rank + 1) * per))
-    counts = [_c4_counts(s) for s in range(world)]  # every rank knows every rank's routing (seeded)
-    send = [int(counts[rank][d * per:(d + 1) * per].sum()) for d in range(world)]
-    recv = [int(counts[s][mine].sum()) for s in range(world)]
-    # Received rows arrive source-major (each source's rows sorted by expert); the experts need them
-    # expert-major and padded to 128-row groups: a fixed gather index, built once.
-    exp_counts = torch.stack([counts[s][mine] for s in range(world)]).sum(0)
-    offsets = align_offsets(exp_counts).to(device)
-    t_pad = int(offsets[-1])
-    dst = []
-    fill = [int(o) for o in offsets[:-1].tolist()]
-    for s in range(world):
-        for j, e in enumerate(mine):
-            n = int(counts[s][e])
-            dst.extend(range(fill[j], fill[j] + n))
-            fill[j] += n
-    routed = int(exp_counts.sum())
-    # The inverse map, for gathers: padded expert-major row p takes received row src[p], or the
-    # zero row appended after the received rows when p is padding.
-    src = torch.full((t_pad,), routed, dtype=torch.int64)
-    src[torch.tensor(dst, dtype=torch.int64)] = torch.arange(routed, dtype=torch.int64)
-    src = src.to(device)
-    dst = torch.tensor(dst, dtype=torch.int64, device=device)
-    flops = 6.0 * routed * (C4_D * 2 * C4_FFN + C4_FFN * C4_D)
-
-    torch.manual_seed(100 + rank)
-    gate_up = FP4GroupedLinear(per, C4_D, 2 * C4_FFN, device=device)
-    down = FP4GroupedLinear(per, C4_FFN, C4_D, device=device)
-    gate_up.refresh_fp4_cache()
-    down.refresh_fp4_cache()
-    x_send_ext = torch.zeros(sum(send) + 1, C4_D, device=device, dtype=torch.bfloat16)
-    x_send = x_send_ext[:sum(send)]
-    x_send.copy_(torch.randn(sum(send), C4_D, device=device).to(torch.bfloat16))
-    h_in = torch.zeros(t_pad, C4_FFN, device=device, dtype=torch.bfloat16)
-    h_in[dst] = torch.randn(routed, C4_FFN, device=device).to(torch.bfloat16)
-    dy_gu = torch.zeros(t_pad, 2 * C4_FFN, device=device, dtype=torch.bfloat16)
-    dy_gu[dst] = (torch.randn(routed, 2 * C4_FFN, device=device) * 1e-3).to(torch.bfloat16)
-    dy_send_ext = torch.zeros(sum(send) + 1, C4_D, device=device, dtype=torch.bfloat16)
-    dy_send = dy_send_ext[:sum(send)]
-    dy_send.copy_((torch.randn(sum(send), C4_D, device=device) * 1e-3).to(torch.bfloat16))
-
-    def a2a(t, out_rows, out_split, in_split, out=None):
-        if world == 1:
-            if out is not None:
-                out.copy_(t)
-                return out
-            return t
-        if out is None:
-            out = torch.empty(out_rows, t.shape[1], device=device, dtype=t.dtype)
-        dist.all_to_all_single(out, t, out_split, in_split)
-        return out
-
-    # Received rows plus one zero row (the source of the padding rows in the expert-major gathers).
-    # On one GPU the received rows are the rank's own, already in place.
-    xr_ext = x_send_ext if world == 1 else torch.zeros(routed + 1, C4_D, device=device, dtype=torch.bfloat16)
-    dyr_ext = dy_send_ext if world == 1 else torch.zeros(routed + 1, C4_D, device=device, dtype=torch.bfloat16)
+    if C4_E % world or C4_TOKENS % world:
+        raise SystemExit(f"config 4 needs the {C4_E} experts and {C4_TOKENS} tokens to divide over {world} ranks")
+    top = _c4_routing()
+    counts = [torch.bincount(_c4_source_pairs(top, s, world)[1], minlength=C4_E) for s in range(world)]
+    plan = ExpertParallelPlan(counts, rank, world, device)
+    gen = torch.Generator(device=device).manual_seed(404)  # every rank draws every expert's weights
+    w_gu = torch.randn(C4_E, C4_D, 2 * C4_FFN, generator=gen, device=device) * 0.02
+    w_dn = torch.randn(C4_E, C4_FFN, C4_D, generator=gen, device=device) * 0.02
+    ffn = _MoEFFN(plan, w_gu, w_dn, device)
+    x_job = torch.randn(C4_TOKENS, C4_D, generator=gen, device=device).to(torch.bfloat16)
+    tok, _ex = _c4_source_pairs(top, rank, world)
+    x_send = x_job[tok.to(device)]
+    g_rank = torch.Generator(device=device).manual_seed(500 + rank)
+    dy_send = (torch.randn(x_send.shape[0], C4_D, generator=g_rank, device=device) * 1e-3).to(torch.bfloat16)
+    weights = (ffn.gate_up.weight, ffn.down.weight)
 
     def step():
-        # dispatch: routed rows -> their experts' owner, then expert-major with zero padding (one
-        # row gather)
-        if world > 1:
-            a2a(x_send, sum(recv), recv, send, out=xr_ext[:routed])
-        x_exp = xr_ext.index_select(0, src)
-        x_exp.requires_grad_(True)
-        y_gu = gate_up(x_exp, offsets)
-        h = h_in.detach().requires_grad_(True)  # silu(gate) * up of y_gu, synthetic here
-        y_d = down(h, offsets)
-        a2a(y_d[dst], sum(send), send, recv)  # combine: outputs back to the tokens' ranks
-        if world > 1:  # gradients of the combined outputs
-            a2a(dy_send, sum(recv), recv, send, out=dyr_ext[:routed])
-        dy_d = dyr_ext.index_select(0, src)
-        torch.autograd.grad(y_d, (h, down.weight), dy_d)
-        gx, _gw = torch.autograd.grad(y_gu, (x_exp, gate_up.weight), dy_gu)
-        a2a(gx[dst], sum(send), send, recv)  # input gradients back to the tokens' ranks
+        xs = x_send.detach().requires_grad_(True)
+        y = ffn(xs)
+        torch.autograd.grad(y, (xs, *weights), dy_send)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    graph = None
+    run_step = step
+    if world == 1 and not args.eager:
+        graph = _capture(step)
+        run_step = graph.replay
+    ms, _clk = _timed_replays(run_step, steps, barrier)
+    ms = max_over_ranks(ms) / steps
+    with _trace.kernel_timer() as kt:
+        step()
+        per_kind = kt.summary()
+    del graph
+
+    parity = None
+    if world > 1:
+        with torch.no_grad():
+            y_ep = ffn(x_send)
+        if rank == 0:
+            all_counts = [torch.bincount(top.flatten(), minlength=C4_E)]
+            plan1 = ExpertParallelPlan(all_counts, 0, 1, device)
+            ref = _MoEFFN(plan1, w_gu, w_dn, device)
+            tok1, ex1 = _c4_source_pairs(top, 0, 1)
+            with torch.no_grad():
+                y_ref = ref(x_job[tok1.to(device)])
+            keys1 = ex1 * C4_TOKENS + tok1  # sorted: the single-GPU row order
+            tok0, ex0 = _c4_source_pairs(top, 0, world)
+            rows = torch.searchsorted(keys1, ex0 * C4_TOKENS + tok0).to(device)
+            parity = bool(torch.equal(y_ep, y_ref.index_select(0, rows)))
+            del y_ep
+            del ref, y_ref
+        barrier()
+    if rank != 0:
+        return None
+    peaks, peak_kind = _peaks()
+    fp4_peak = 4.0 * peaks["bf16_tflops"]
+    gemm = per_kind.get("gemm", {"launches": 0, "ms": 0.0, "work": 0.0})
+    gemm_tflops = gemm["work"] / (gemm["ms"] * 1e-3) / 1e12 if gemm["ms"] else None
+    rec = {
+        "metric": C4_METRIC,
+        "value": round(C4_FLOPS / (ms * 1e-3) / 1e12, 2),
+        "unit": "TFLOPS",
+        "n_gpus": world,
+        "steps": steps,
+        "ms_per_step": round(ms, 4),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "config": {
+            "workload": "config4: MoE expert FFN (dispatch, grouped gate+up 2048->2816, SwiGLU, grouped down "
+                        "1408->2048, combine) fwd+dgrad+wgrad via FP4GroupedLinear",
+            "experts": C4_E, "experts_per_rank": C4_E // world, "top_k": C4_TOPK, "tokens_per_job": C4_TOKENS,
+            "routed_rows_rank0": plan.routed, "padded_rows_rank0": plan.rows, "rank0_expert_rows": plan.expert_rows,
+            "parallelism": f"expert-parallel ep{world} (NCCL all-to-all dispatch/combine)" if world > 1
+            else "single GPU, all experts",
+            "flops_basis": "6 x 32768 routed rows x (2048 x 2816 + 1408 x 2048) per job step; padding is overhead",
+            "timing": "the step captured in one CUDA graph, replayed" if world == 1 and not args.eager
+            else "eager Python step loop around NCCL",
+        },
+        "kernels": {k: {"launches": v["launches"], "ms": round(v["ms"], 4)} for k, v in per_kind.items()},
+        "roofline": {
+            "kernel": "nvfp4_gemm2_kernel (grouped)",
+            "bound": "tensor",
+            "achieved": None if gemm_tflops is None else round(gemm_tflops, 1),
+            "peak": round(fp4_peak, 1),
+            "peak_basis": f"4 x {peak_kind} dense bf16 ({peaks['bf16_tflops']} TF/s)",
+            "unit": "TFLOP/s",
+            "frac": None if gemm_tflops is None else round(gemm_tflops / fp4_peak, 4),
+            "traffic": None,
+        },
+        "gpu_launches": kt.launches * steps,
+    }
+    if parity is not None:
+        rec["parity_ok"] = parity
+        rec["parity"] = ("rank 0's tokens: forward output through dispatch/experts/combine equals the single-GPU "
+                         "expert FFN over the whole job, bit for bit")
+    return rec
+
+
+def _dist_helpers(world, device):
+    import torch
+    import torch.distributed as dist
 
     def barrier():
         if world > 1:
@@ -637,100 +847,28 @@ def run_config4(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
+    return barrier, max_over_ranks
+
+
+def run_config4(args):
+    import torch
+    import torch.distributed as dist
+
+    rank, world, local = _dist_setup(args)
+    device = torch.device("cuda", local if world > 1 else 0)
+    barrier, max_over_ranks = _dist_helpers(world, device)
     visible = os.environ.get("CUDA_VISIBLE_DEVICES")
     phys = visible.split(",")[torch.cuda.current_device()] if visible else str(torch.cuda.current_device())
     clocks = ClockSampler(phys)
-    # On one GPU the step (no collectives; routing offsets stay on the device) is captured once in a
-    # CUDA graph and replayed, as in config 3; with several ranks it runs eagerly around NCCL.
-    run_step = step
-    graph = None
-    if world == 1 and not args.eager:
-        side = torch.cuda.Stream()
-        side.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(side):
-            for _ in range(2):
-                step()
-        torch.cuda.current_stream().wait_stream(side)
-        torch.cuda.synchronize()
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            step()
-        torch.cuda.synchronize()
-        run_step = graph.replay
     clocks.start()
-    for _ in range(20):
-        run_step()
-    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
-    torch.cuda.synchronize()
-    start.record()
-    for _ in range(args.steps):
-        run_step()
-    stop.record()
-    torch.cuda.synchronize()
-    barrier()
+    rec = measure_config4(args, rank, world, device, barrier, max_over_ranks, max(3, min(args.steps, 50)))
     clk = clocks.stop()
-    ms = max_over_ranks(start.elapsed_time(stop)) / args.steps
-    # Per-kernel breakdown: the same steps again, eagerly, with CUDA events around every launch.
-    kt_steps = max(3, min(args.steps, 50))
-    with _trace.kernel_timer() as kt:
-        for _ in range(kt_steps):
-            step()
-        torch.cuda.synchronize()
-    per_kind = {k: {kk: (int(round(vv * args.steps / kt_steps)) if kk == "launches" else vv * args.steps / kt_steps)
-                    for kk, vv in v.items()} for k, v in kt.summary().items()}
-    timing_mode = ("the step captured in one CUDA graph, replayed K times (per-kernel times from an eager pass)"
-                   if graph is not None else "eager Python step loop around NCCL (per-kernel times from a second pass)")
-    if graph is not None:
-        del graph
     if rank == 0:
-        peaks, peak_kind = _peaks()
-        fp4_peak = 4.0 * peaks["bf16_tflops"]
-        gemm = per_kind.get("gemm", {"launches": 0, "ms": 0.0})
-        gemm_ms = gemm["ms"] / args.steps
-        gemm_tflops = flops / (gemm_ms * 1e-3) / 1e12 if gemm_ms else None
-        line = {
-            "metric": C4_METRIC,
-            "value": round(world * C4_FLOPS / (ms * 1e-3) / 1e12, 2),
-            "unit": "TFLOPS",
-            "n_gpus": world,
-            "steps": args.steps,
-            "warmup": args.warmup,
-            "ms_per_step": round(ms, 4),
-            "higher_is_better": True,
-            "scaling": "weak",
-            "vs_baseline": None,
-            "dtype": "nvfp4 (e2m1 x e4m3 block scales, fp32 accumulate; bf16 in/out, fp32 dW)",
-            "data": "synthetic (seeded; router logits ~N(0,1), W~N(0,0.02), X~N(0,1), dY~N(0,1e-3))",
-            "config": {
-                "workload": "config4: MoE expert FFN linears (gate+up 2048->2816, down 1408->2048) fwd+dgrad+wgrad "
-                            "via FP4GroupedLinear",
-                "experts": C4_E, "experts_per_rank": per, "top_k": C4_TOPK, "tokens_per_gpu": C4_TOKENS,
-                "routed_rows_rank0": routed, "padded_rows_rank0": t_pad,
-                "rank0_expert_rows": exp_counts.tolist(),
-                "parallelism": f"expert-parallel ep{world} (NCCL all-to-all dispatch/combine)" if world > 1
-                else "single GPU, all experts",
-                "flops_basis": "6 x routed rows x (2048 x 2816 + 1408 x 2048); padding rows are overhead",
-                "timing": timing_mode,
-            },
-            "kernels": {k: {"launches": v["launches"], "ms": round(v["ms"], 3)} for k, v in per_kind.items()},
-            "roofline": {
-                "kernel": "nvfp4_gemm2_kernel (grouped)",
-                "bound": "tensor",
-                "achieved": None if gemm_tflops is None else round(gemm_tflops, 1),
-                "peak": round(fp4_peak, 1),
-                "peak_basis": f"4 x {peak_kind} dense bf16 ({peaks['bf16_tflops']} TF/s)",
-                "unit": "TFLOP/s",
-                "frac": None if gemm_tflops is None else round(gemm_tflops / fp4_peak, 4),
-                "traffic": None,
-            },
-            "gpu_launches": kt.launches,
-            "clocks": clk,
-        }
-        print(json.dumps(line), flush=True)
+        rec.update({"warmup": args.warmup, "vs_baseline": None,
+                    "dtype": "nvfp4 (e2m1 x e4m3 block scales, fp32 accumulate; bf16 in/out, fp32 dW)",
+                    "data": "synthetic (seeded; router logits ~N(0,1), W~N(0,0.02), X~N(0,1), dY~N(0,1e-3))",
+                    "clocks": clk})
+        print(json.dumps(rec), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -895,13 +1033,16 @@ C5_FLOPS = 6.0 * C5_TOKENS * sum(k * n for _, k, n in C5_TOKEN_SHARDED + C5_NSPL
 C5_METRIC = "NVFP4 linear fwd+bwd TFLOPS (BASELINE config 5: d_model 4096 block, 65536 tokens per job)"
 
 
-def run_config5(args):
+def measure_config5(args, rank, world, device, barrier, max_over_ranks, steps):
     """One step = the block's four linears fwd + dgrad + wgrad for a fixed 65536-token job.  QKV,
-    O and down are token-sharded (65536/N rows per rank, no collective).  The largest layer,
-    gate/up (4096 -> 28672), is split along N: every rank holds 28672/N rows of the weight
-    (quantized with the full weight's global scale), computes its column slice for all 65536 rows
-    and all-gathers the bf16 output; the partial input gradients are all-reduced.  Total work is
-    fixed as N grows (strong scaling)."""
+    O and down are token-sharded (65536/N rows per rank); their fp32 weight gradients are
+    reduce-scattered over the ranks inside the step (NCCL on a side stream, from the wgrad hooks).
+    The largest layer, gate/up (4096 -> 28672), is split along N: every rank holds 28672/N rows of
+    the weight (quantized with the full weight's global scale), computes its column slice for all
+    65536 rows and all-gathers the bf16 output (fused into the GEMM epilogue, or NCCL); the partial
+    input gradients are all-reduced.  Total work is fixed as N grows (strong scaling).  With N > 1,
+    rank 0 checks that the N-split layer's output rows equal the unsplit FP4Linear's (same full-input
+    global scale), bit for bit.  Returns the record (rank 0)."""
     import torch
     import torch.distributed as dist
 
@@ -909,8 +1050,6 @@ def run_config5(args):
     from radiance_b200.nvfp4 import _trace
     from radiance_b200.nvfp4.nsplit import FP4ColumnParallelLinear
 
-    rank, world, local = _dist_setup(args)
-    device = torch.device("cuda", local if world > 1 else 0)
     if C5_TOKENS % (128 * world):
         raise SystemExit(f"config 5 needs 65536 tokens to shard into multiples of 128 over {world} ranks")
     m_local = C5_TOKENS // world
@@ -919,18 +1058,32 @@ def run_config5(args):
     m_ffn = C5_TOKENS
     gen = torch.Generator(device=device).manual_seed(777)  # same on every rank: replicated weights/rows
     layers, inputs, grads = [], [], []
+    side = torch.cuda.Stream(device)
+    shards, pending = [], []
     for name, k, n in C5_TOKEN_SHARDED:
         lin = nv.FP4Linear(k, n, bias=False, device=device)
         with torch.no_grad():
             lin.weight.copy_(torch.randn(n, k, device=device, generator=gen) * 0.02)
         lin.refresh_fp4_cache()
+        if world > 1:
+            shard = torch.empty(n // world, k, device=device)
+            shards.append(shard)
+
+            def hook(grad_w, shard=shard):
+                side.wait_stream(torch.cuda.current_stream())
+                with torch.cuda.stream(side):
+                    dist.reduce_scatter_tensor(shard, grad_w)
+                pending.append(grad_w)
+            lin.wgrad_hook = hook
         layers.append((lin, lin.weight))
         g_local = torch.Generator(device=device).manual_seed(1000 + rank)
         inputs.append(torch.randn(m_local, k, device=device, generator=g_local).to(torch.bfloat16))
         grads.append((torch.randn(m_local, n, device=device, generator=g_local) * 1e-3).to(torch.bfloat16))
+    full_w = None
     for name, k, n in C5_NSPLIT:
         lin = FP4ColumnParallelLinear(k, n, device=device, fused_gather=args.nsplit == "fused")
-        lin.load_full_weight(torch.randn(n, k, device=device, generator=gen) * 0.02)
+        full_w = torch.randn(n, k, device=device, generator=gen) * 0.02
+        lin.load_full_weight(full_w)
         lin.refresh_fp4_cache()
         layers.append((lin, lin.local.weight))
         inputs.append(torch.randn(m_ffn, k, device=device, generator=gen).to(torch.bfloat16))
@@ -939,32 +1092,21 @@ def run_config5(args):
                         + m_ffn * sum(k * n for _, k, n in C5_NSPLIT) / world)
     gather_bytes = sum(m_ffn * n * 2 * (world - 1) // world for _, k, n in C5_NSPLIT) if world > 1 else 0
     reduce_bytes = sum(m_ffn * k * 2 for _, k, n in C5_NSPLIT) if world > 1 else 0
+    wgrad_rs_bytes = sum(n * k * 4 for _, k, n in C5_TOKEN_SHARDED) if world > 1 else 0
 
     def step():
         for (lin, w), x0, dy in zip(layers, inputs, grads):
             x = x0.detach().requires_grad_(True)
             y = lin(x)
             torch.autograd.grad(y, (x, w), dy)
-
-    def barrier():
+            del y
         if world > 1:
-            dist.barrier()
+            torch.cuda.current_stream().wait_stream(side)
+            pending.clear()
 
-    def max_over_ranks(v: float) -> float:
-        if world == 1:
-            return v
-        t = torch.tensor([v], device=device, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
-    steps = max(3, min(args.steps, 20))
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
-    visible = os.environ.get("CUDA_VISIBLE_DEVICES")
-    phys = visible.split(",")[torch.cuda.current_device()] if visible else str(torch.cuda.current_device())
-    clocks = ClockSampler(phys)
-    clocks.start()
     for _ in range(3):
         step()
     with _trace.kernel_timer() as kt:
@@ -977,55 +1119,98 @@ def run_config5(args):
         stop.record()
         torch.cuda.synchronize()
         barrier()
-    clk = clocks.stop()
     ms = max_over_ranks(start.elapsed_time(stop)) / steps
     per_kind = kt.summary()
+    parity = None
+    if world > 1:
+        lin = layers[-1][0]
+        with torch.no_grad():
+            y_split = lin(inputs[-1])
+            if rank == 0:
+                k, n = C5_NSPLIT[0][1], C5_NSPLIT[0][2]
+                ref = nv.FP4Linear(k, n, bias=False, device=device)
+                ref.weight.copy_(full_w)
+                ref.refresh_fp4_cache()
+                gs = nv.global_scale_of(inputs[-1])
+                y_ref = ref(inputs[-1][:4096], global_scale=gs)
+                parity = bool(torch.equal(y_split[:4096], y_ref))
+                del ref, y_ref
+            del y_split
+        barrier()
+        for lin, _w in layers:
+            if isinstance(lin, FP4ColumnParallelLinear):
+                lin.close()
+            else:
+                lin.wgrad_hook = None
+    if rank != 0:
+        return None
+    peaks, peak_kind = _peaks()
+    fp4_peak = 4.0 * peaks["bf16_tflops"]
+    gemm = per_kind.get("gemm", {"launches": 0, "ms": 0.0, "work": 0.0})
+    gemm_tflops = gemm["work"] / (gemm["ms"] * 1e-3) / 1e12 if gemm["ms"] else None
+    rec = {
+        "metric": C5_METRIC,
+        "value": round(C5_FLOPS / (ms * 1e-3) / 1e12, 2),
+        "unit": "TFLOPS",
+        "n_gpus": world,
+        "steps": steps,
+        "ms_per_step": round(ms, 3),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "config": {
+            "workload": "config5: d_model 4096 block linears fwd+dgrad+wgrad; QKV/O/down token-sharded with their "
+                        "fp32 dW reduce-scattered in the step, gate_up (the largest) N-split with an all-gather of "
+                        "its bf16 output",
+            "tokens_per_job": C5_TOKENS, "attention_rows_per_rank": m_local, "ffn_rows": m_ffn,
+            "layers": {n: [k, o] for n, k, o in C5_TOKEN_SHARDED + C5_NSPLIT},
+            "flops_per_rank_per_step": flops_rank,
+            "allgather_bytes_received_per_rank_per_step": gather_bytes,
+            "dgrad_allreduce_bytes_per_rank_per_step": reduce_bytes,
+            "wgrad_reduce_scatter_bytes_per_step": wgrad_rs_bytes,
+            "parallelism": f"gate_up N-split over {world} + token-sharded QKV/O/down",
+            "nsplit_gather": ("GEMM epilogue stores each tile into every rank's output over NVLink "
+                              "(rb_nvfp4_gemm_allgather, IPC-shared buffers)") if args.nsplit == "fused"
+            else "NCCL all_gather_into_tensor + column permute",
+            "timing": "eager Python step loop (CUDA events around the K steps; per-kernel events inside)",
+        },
+        "kernels": {k: {"launches": v["launches"], "ms": round(v["ms"], 3)} for k, v in per_kind.items()},
+        "roofline": {
+            "kernel": "nvfp4_gemm2_kernel",
+            "bound": "tensor",
+            "achieved": None if gemm_tflops is None else round(gemm_tflops, 1),
+            "peak": round(fp4_peak, 1),
+            "peak_basis": f"4 x {peak_kind} dense bf16 ({peaks['bf16_tflops']} TF/s)",
+            "unit": "TFLOP/s",
+            "frac": None if gemm_tflops is None else round(gemm_tflops / fp4_peak, 4),
+            "traffic": None,
+        },
+        "gpu_launches": kt.launches,
+    }
+    if parity is not None:
+        rec["parity_ok"] = parity
+        rec["parity"] = ("rank 0: rows 0..4095 of the N-split gate_up output (every rank's slice, gathered) equal "
+                         "the unsplit FP4Linear's with the same full-input global scale, bit for bit")
+    return rec
+
+
+def run_config5(args):
+    import torch
+    import torch.distributed as dist
+
+    rank, world, local = _dist_setup(args)
+    device = torch.device("cuda", local if world > 1 else 0)
+    barrier, max_over_ranks = _dist_helpers(world, device)
+    visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+    phys = visible.split(",")[torch.cuda.current_device()] if visible else str(torch.cuda.current_device())
+    clocks = ClockSampler(phys)
+    clocks.start()
+    rec = measure_config5(args, rank, world, device, barrier, max_over_ranks, max(3, min(args.steps, 20)))
+    clk = clocks.stop()
     if rank == 0:
-        peaks, peak_kind = _peaks()
-        fp4_peak = 4.0 * peaks["bf16_tflops"]
-        gemm = per_kind.get("gemm", {"launches": 0, "ms": 0.0, "work": 0.0})
-        gemm_tflops = gemm["work"] / (gemm["ms"] * 1e-3) / 1e12 if gemm["ms"] else None
-        line = {
-            "metric": C5_METRIC,
-            "value": round(C5_FLOPS / (ms * 1e-3) / 1e12, 2),
-            "unit": "TFLOPS",
-            "n_gpus": world,
-            "steps": steps,
-            "warmup": args.warmup,
-            "ms_per_step": round(ms, 3),
-            "higher_is_better": True,
-            "scaling": "strong",
-            "vs_baseline": None,
-            "dtype": "nvfp4 (e2m1 x e4m3 block scales, fp32 accumulate; bf16 in/out, fp32 dW)",
-            "data": "synthetic (seeded; W~N(0,0.02), X~N(0,1), dY~N(0,1e-3))",
-            "config": {
-                "workload": "config5: d_model 4096 block linears fwd+dgrad+wgrad; QKV/O/down token-sharded, "
-                            "gate_up (the largest) N-split with an NCCL all-gather of its bf16 output",
-                "tokens_per_job": C5_TOKENS, "attention_rows_per_rank": m_local, "ffn_rows": m_ffn,
-                "layers": {n: [k, o] for n, k, o in C5_TOKEN_SHARDED + C5_NSPLIT},
-                "flops_per_rank_per_step": flops_rank,
-                "allgather_bytes_received_per_rank_per_step": gather_bytes,
-                "dgrad_allreduce_bytes_per_rank_per_step": reduce_bytes,
-                "parallelism": f"gate_up N-split over {world} + token-sharded QKV/O/down",
-                "nsplit_gather": ("GEMM epilogue stores each tile into every rank's output over NVLink "
-                                  "(rb_nvfp4_gemm_allgather, symmetric memory)") if args.nsplit == "fused"
-                else "NCCL all_gather_into_tensor + column permute",
-            },
-            "kernels": {k: {"launches": v["launches"], "ms": round(v["ms"], 3)} for k, v in per_kind.items()},
-            "roofline": {
-                "kernel": "nvfp4_gemm2_kernel",
-                "bound": "tensor",
-                "achieved": None if gemm_tflops is None else round(gemm_tflops, 1),
-                "peak": round(fp4_peak, 1),
-                "peak_basis": f"4 x {peak_kind} dense bf16 ({peaks['bf16_tflops']} TF/s)",
-                "unit": "TFLOP/s",
-                "frac": None if gemm_tflops is None else round(gemm_tflops / fp4_peak, 4),
-                "traffic": None,
-            },
-            "gpu_launches": kt.launches,
-            "clocks": clk,
-        }
-        print(json.dumps(line), flush=True)
+        rec.update({"warmup": args.warmup, "vs_baseline": None,
+                    "dtype": "nvfp4 (e2m1 x e4m3 block scales, fp32 accumulate; bf16 in/out, fp32 dW)",
+                    "data": "synthetic (seeded; W~N(0,0.02), X~N(0,1), dY~N(0,1e-3))", "clocks": clk})
+        print(json.dumps(rec), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -1039,6 +1224,11 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
+    ap.add_argument("--tokens-per-rank", type=int, default=0,
+                    help="config 3: run this many tokens on every rank instead of sharding the job's 16384 "
+                         "(weak scaling; no gradient reduction unless N > 1)")
+    ap.add_argument("--no-subrecords", action="store_true",
+                    help="config 3: skip the config 4 and config 5 sub-records of the headline line")
     ap.add_argument("--eager", action="store_true",
                     help="config 3: time the Python step loop instead of a captured CUDA graph of the step")
     ap.add_argument("--nsplit", choices=["fused", "nccl"], default="fused",

@@ -31,7 +31,7 @@
 extern "C" {
 #endif
 
-#define RB_NVFP4_ABI_VERSION 5
+#define RB_NVFP4_ABI_VERSION 6
 
 /* Input element types. */
 #define RB_DTYPE_BF16 0
@@ -86,6 +86,8 @@ int rb_nvfp4_global_scale(const void* x, int dtype, int64_t rows, int64_t cols, 
  *   on the scratch: order them (for example, issue them on one stream).
  *   The first call on each device looks up the scratch's device address; make that first call
  *   before any stream capture.
+ *   The call uses the scratch of the current device: x and stream must belong to it.  An x on
+ *   another device returns RB_ERR_ARG.
  */
 int rb_nvfp4_global_scale_noalloc(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld, float* gs_out,
                                   void* stream);
@@ -145,7 +147,7 @@ int rb_nvfp4_gemm(const void* a_packed, const void* a_scale, const void* b_packe
  * columns r*n .. r*n+n-1 of a (m, g*n) output and stores them into all g copies over NVLink while
  * later tiles are still being multiplied.  peer_out is a host array of npeers (<= 7) device
  * pointers, each at the position `out` has in that GPU's buffer (same ldo); the memory must be
- * mapped into this process (peer access or symmetric memory).  The call only writes; the caller
+ * mapped into this process (rb_peer_open, or peer access between the devices).  The call only writes; the caller
  * synchronises the GPUs before reading the peers' copies.  It stands in for the bf16 output
  * all-gather of the N-split layers (no reference counterpart: radiance has no N-split path).
  */
@@ -153,6 +155,23 @@ int rb_nvfp4_gemm_allgather(const void* a_packed, const void* a_scale, const voi
                             int64_t m, int64_t n, int64_t k, const float* alpha_a, const float* alpha_b,
                             const void* bias, int bias_dtype, void* out, int out_dtype, int64_t ldo,
                             void* const* peer_out, int npeers, void* stream);
+
+/*
+ * Peer buffers for rb_nvfp4_gemm_allgather, shared between the processes of one box by CUDA IPC
+ * (no NVLink multicast object is created; peers touch a mapping only with plain loads and stores).
+ * No reference counterpart: radiance has no multi-GPU path.
+ *   rb_peer_alloc  : one cudaMalloc allocation of `bytes` (IPC needs a whole allocation).
+ *   rb_peer_handle : its RB_PEER_HANDLE_BYTES-byte IPC handle, for the caller to send to the peers.
+ *   rb_peer_open   : map a peer's handle into this process (peer access enabled lazily);
+ *                    rb_peer_close unmaps it.  rb_peer_free frees an rb_peer_alloc allocation.
+ * These synchronise like the CUDA calls they wrap; none of them may run during stream capture.
+ */
+#define RB_PEER_HANDLE_BYTES 64
+int rb_peer_alloc(size_t bytes, void** ptr_out);
+int rb_peer_free(void* ptr);
+int rb_peer_handle(void* ptr, void* handle_out);
+int rb_peer_open(const void* handle, void** ptr_out);
+int rb_peer_close(void* ptr);
 
 /*
  * The optimizer's last in-place step on a weight fused with the start of its cache refresh:
@@ -285,6 +304,19 @@ int rb_nvfp4_selftest_division(const float* x, const float* d, int64_t n, uint32
  * uint32, accumulated).  Test aid; no counterpart in the reference.
  */
 int rb_nvfp4_selftest_scale(const float* amax, int64_t n, const float* gs, uint32_t* mismatches, void* stream);
+
+/*
+ * Self-test of the failure path: launches one CTA that waits, with the library's bounded mbarrier
+ * wait shortened to limit_cycles (0 < limit_cycles <= the ~1 s production limit), on a barrier that
+ * nothing ever arrives on.  No TMA copy, MMA or TMEM allocation is issued, so nothing is in flight
+ * when the wait gives up; the kernel then records the status a real timeout records and returns.
+ *   which = 0 : the quantizer's wait (status 1, TMA data), recorded in the quantizer's status word;
+ *   which = 1 : the GEMM epilogue's sleeping wait (status 2, MMA completion), in the GEMM's word.
+ *   waited_cycles : device uint32, set to the cycles the wait took before giving up.
+ * rb_nvfp4_device_status then reports the code, and later launches run normally.  Test aid; no
+ * counterpart in the reference.
+ */
+int rb_nvfp4_selftest_wait_timeout(int which, long long limit_cycles, uint32_t* waited_cycles, void* stream);
 
 #ifdef __cplusplus
 }

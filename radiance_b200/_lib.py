@@ -67,9 +67,17 @@ SIGNATURES: dict[str, tuple] = {
     "rb_nvfp4_selftest_division": (_int, [_c_void_p, _c_void_p, _i64, _c_void_p, _c_void_p]),
     "rb_nvfp4_selftest_scale": (_int, [_c_void_p, _i64, _c_void_p, _c_void_p, _c_void_p]),
     "rb_nvfp4_selftest_silu": (_int, [_c_void_p, _c_void_p]),
+    "rb_nvfp4_selftest_wait_timeout": (_int, [_int, ctypes.c_longlong, _c_void_p, _c_void_p]),
+    "rb_peer_alloc": (_int, [ctypes.c_size_t, ctypes.POINTER(_c_void_p)]),
+    "rb_peer_free": (_int, [_c_void_p]),
+    "rb_peer_handle": (_int, [_c_void_p, ctypes.c_char_p]),
+    "rb_peer_open": (_int, [ctypes.c_char_p, ctypes.POINTER(_c_void_p)]),
+    "rb_peer_close": (_int, [_c_void_p]),
 }
 
-ABI_VERSION = 5
+RB_PEER_HANDLE_BYTES = 64
+
+ABI_VERSION = 6
 
 RB_DTYPE_BF16 = 0
 RB_DTYPE_F32 = 1

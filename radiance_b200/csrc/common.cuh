@@ -70,23 +70,25 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Waits for the phase with the given parity to complete.  Returns false after ~1 s.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// Waits for the phase with the given parity to complete.  Returns false after ~1 s (`limit`
+// cycles; only the wait self-test passes a shorter limit).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, long long limit = kWaitLimitCycles) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long start = clock64();
   while (!mbar_try_wait(bar, parity)) {
-    if (clock64() - start > kWaitLimitCycles) return false;
+    if (clock64() - start > limit) return false;
   }
   return true;
 }
 
 // As mbar_wait, sleeping ~`ns` nanoseconds between polls: for long waits of warps that share a
 // scheduler with a latency-critical warp (the GEMM's epilogue warps beside its MMA issuer).
-__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns,
+                                                long long limit = kWaitLimitCycles) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long start = clock64();
   while (!mbar_try_wait(bar, parity)) {
-    if (clock64() - start > kWaitLimitCycles) return false;
+    if (clock64() - start > limit) return false;
     __nanosleep(ns);
   }
   return true;

@@ -1162,7 +1162,37 @@ bool sm100_device(int dev, const char* what) {
 
 }  // namespace
 
+namespace rb {
+// Failure-path self-test for the GEMM's status word: one CTA waits, the way the epilogue waits for
+// an accumulator (sleeping between polls), on an mbarrier that nothing ever arrives on -- no TMA,
+// MMA or TMEM allocation is made, so nothing is in flight when it gives up after `limit` cycles.
+// It then records kStatusTimeoutMma, as the epilogue does, and returns.
+__global__ void gemm_selftest_wait_kernel(long long limit, uint32_t* waited) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const long long t0 = clock64();
+  const bool ok = mbar_wait_sleep(&bar, 0, 64, limit);
+  const long long t1 = clock64();
+  if (__syncthreads_or(!ok)) {
+    if (threadIdx.x == 0) {
+      record_status(&g_gemm_status, kStatusTimeoutMma);
+      *waited = (uint32_t)min(t1 - t0, (long long)0xFFFFFFFF);
+    }
+    return;
+  }
+}
+}  // namespace rb
+
 extern "C" {
+
+uint32_t rb_internal_gemm_selftest_wait(long long limit, uint32_t* waited, cudaStream_t stream) {
+  rb::gemm_selftest_wait_kernel<<<1, 128, 0, stream>>>(limit, waited);
+  return 0;
+}
 
 uint32_t rb_internal_gemm_status(int clear) {
   uint32_t v = 0;

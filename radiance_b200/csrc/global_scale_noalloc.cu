@@ -162,6 +162,19 @@ extern "C" int rb_nvfp4_global_scale_noalloc(const void* x, int dtype, int64_t r
     rb_host::set_error("nvfp4 global_scale_noalloc: the current device is not an sm_100 GPU");
     return RB_ERR_DEVICE;
   }
+  // The scratch used is the current device's, so x must live there too (a stream of another device
+  // cannot be checked here; it must belong to the current device as well).
+  cudaPointerAttributes attr;
+  if (cudaPointerGetAttributes(&attr, x) == cudaSuccess) {
+    if ((attr.type == cudaMemoryTypeDevice || attr.type == cudaMemoryTypeManaged) && attr.device != dev) {
+      rb_host::set_error(
+          "nvfp4 global_scale_noalloc: x is on device %d but the current device is %d; make x's device current "
+          "(the call uses the current device's scratch)", attr.device, dev);
+      return RB_ERR_ARG;
+    }
+  } else {
+    cudaGetLastError();  // an unregistered host pointer is not an error for this check
+  }
   uint32_t* scratch = scratch_ptr(dev);
   if (scratch == nullptr) return RB_ERR_CUDA;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);

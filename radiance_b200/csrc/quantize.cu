@@ -1055,6 +1055,29 @@ __global__ void __launch_bounds__(256) colsum_finish_kernel(const float* partial
 
 __global__ void fill_float_kernel(float* p, float v) { *p = v; }
 
+// Failure-path self-test: one CTA waits on an mbarrier that nothing ever arrives on (no TMA, no MMA
+// is issued, so nothing is in flight when it gives up), with the tile loop's bounded wait shortened
+// to `limit` cycles.  When the wait runs out the CTA records kStatusTimeoutTma in the quantizer's
+// status word, exactly as the tile loop does, and returns.  `waited` receives the cycles spent.
+__global__ void selftest_wait_timeout_kernel(long long limit, uint32_t* waited) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const long long t0 = clock64();
+  const bool ok = mbar_wait(&bar, 0, limit);
+  const long long t1 = clock64();
+  if (__syncthreads_or(!ok)) {
+    if (threadIdx.x == 0) {
+      record_status(&g_quant_status, kStatusTimeoutTma);
+      *waited = (uint32_t)min(t1 - t0, (long long)0xFFFFFFFF);
+    }
+    return;
+  }
+}
+
 __global__ void selftest_division_kernel(const float* x, const float* d, int64_t n, uint32_t* mismatches) {
   uint32_t bad = 0;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
@@ -1506,6 +1529,29 @@ int rb_nvfp4_selftest_division(const float* x, const float* d, int64_t n, uint32
   }
   const int sms = rb_host::num_sms(rb_host::current_device());
   rb::selftest_division_kernel<<<4 * sms, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(x, d, n, mismatches);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    rb_host::set_error("selftest launch failed: %s", cudaGetErrorString(e));
+    return RB_ERR_CUDA;
+  }
+  return RB_OK;
+}
+
+uint32_t rb_internal_gemm_selftest_wait(long long limit, uint32_t* waited, cudaStream_t stream);
+
+int rb_nvfp4_selftest_wait_timeout(int which, long long limit_cycles, uint32_t* waited_cycles, void* stream) {
+  if (waited_cycles == nullptr || limit_cycles <= 0 || limit_cycles > rb::kWaitLimitCycles || (which != 0 && which != 1)) {
+    rb_host::set_error("nvfp4 selftest_wait_timeout: which must be 0 or 1, 0 < limit_cycles <= %lld, and "
+                       "waited_cycles a device pointer", (long long)rb::kWaitLimitCycles);
+    return RB_ERR_ARG;
+  }
+  if (!device_is_sm100()) {
+    rb_host::set_error("nvfp4 selftest_wait_timeout: the current device is not an sm_100 GPU");
+    return RB_ERR_DEVICE;
+  }
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (which == 0) rb::selftest_wait_timeout_kernel<<<1, 128, 0, s>>>(limit_cycles, waited_cycles);
+  else rb_internal_gemm_selftest_wait(limit_cycles, waited_cycles, s);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     rb_host::set_error("selftest launch failed: %s", cudaGetErrorString(e));

@@ -3,7 +3,9 @@
 Inactive by default: each op checks one module global.  ``with kernel_timer() as kt:`` records a
 start/end event pair around every C-ABI launch, with the launch's algorithmic work (FLOPs for a
 GEMM, bytes for a quantizer or amax pass), so a caller can report per-kind device time and
-throughput without a profiler.
+throughput without a profiler.  The events are created "external", so a step captured in a CUDA
+graph under the timer keeps them as event-record nodes: every replay re-records them, and
+``summary()`` after a replay gives that replay's per-launch times.
 """
 
 from __future__ import annotations
@@ -48,7 +50,7 @@ def begin(kind: str, work: float):
     if _active is None:
         return None
     _active.launches += 1
-    s = torch.cuda.Event(enable_timing=True)
+    s = torch.cuda.Event(enable_timing=True, external=True)
     s.record()
     return (kind, work, s)
 
@@ -56,6 +58,6 @@ def begin(kind: str, work: float):
 def end(token) -> None:
     if token is None or _active is None:
         return
-    e = torch.cuda.Event(enable_timing=True)
+    e = torch.cuda.Event(enable_timing=True, external=True)
     e.record()
     _active.records.append((token[0], token[1], token[2], e))

@@ -63,7 +63,8 @@ class _FP4LinearFn(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, x, weight, bias, w_fwd_packed, w_fwd_scale, w_fwd_gs, w_dgrad_packed, w_dgrad_scale,
-                w_dgrad_gs, hadamard, seed, recipe, reduce_grad_scale=None, output_gemm=None, x_global_scale=None):
+                w_dgrad_gs, hadamard, seed, recipe, reduce_grad_scale=None, output_gemm=None, x_global_scale=None,
+                wgrad_hook=None):
         # The input's global scale, unless its producer already computed it (a SwiGLU epilogue).
         gx = global_scale_of(x) if x_global_scale is None else x_global_scale
         rot = hadamard if recipe.hadamard and hadamard.numel() else None
@@ -78,6 +79,8 @@ class _FP4LinearFn(torch.autograd.Function):
             y = mm(xq, wq, out_dtype=x.dtype, bias=bias)
         else:  # e.g. an N-split slice whose GEMM also writes the peers' copies of the output
             y = output_gemm(xq, wq, bias, x.dtype)
+        # Saved for backward: the packed wgrad operand (or x itself when it is not saved quantized),
+        # the weight's dgrad operand, the rotation, the seed and x's global scale.
         if save_quantized:
             saved = (xqt.packed, xqt.scale, weight, w_dgrad_packed, w_dgrad_scale, w_dgrad_gs, hadamard, seed, gx)
         else:
@@ -85,6 +88,7 @@ class _FP4LinearFn(torch.autograd.Function):
         ctx.save_for_backward(*saved)
         ctx.recipe = recipe
         ctx.reduce_grad_scale = reduce_grad_scale
+        ctx.wgrad_hook = wgrad_hook
         ctx.has_bias = bias is not None
         ctx.save_quantized = save_quantized
         ctx.x_dtype = x.dtype
@@ -93,7 +97,7 @@ class _FP4LinearFn(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, grad_y):
-        x_or_packed, x_or_scale, weight, wdp, wds, wdg, hadamard, seed, gx = ctx.saved_tensors
+        xt_or_x, xt_scale, weight, wt_packed, wt_scale, wt_gs, hadamard, seed, gx = ctx.saved_tensors
         recipe: FP4Recipe = ctx.recipe
         if grad_y.stride(-1) != 1:  # row-strided gradients (an N-split slice) are read in place
             grad_y = grad_y.contiguous()
@@ -111,15 +115,18 @@ class _FP4LinearFn(torch.autograd.Function):
             # both stochastically rounded with the same seed (linear.py:129, :133-136).
             gq, gqt = quantize_both(grad_y, global_scale=gg, hadamard=rot,
                                     stochastic=recipe.stochastic_rounding, seed=seed)
-            grad_x = mm(gq, NVFP4Tensor(wdp, wds, wdg), out_dtype=x_dtype)
             if ctx.save_quantized:
-                xqt = NVFP4Tensor(x_or_packed, x_or_scale, gx)
+                xqt = NVFP4Tensor(xt_or_x, xt_scale, gx)
             else:
-                xqt = quantize(x_or_packed, 0, global_scale=gx, hadamard=rot)
+                xqt = quantize(xt_or_x, 0, global_scale=gx, hadamard=rot)
+            # wgrad first: a hook (a data-parallel gradient reduction) can start on it while dgrad runs.
             grad_w = mm(gqt, xqt, out_dtype=torch.float32)
+            if ctx.wgrad_hook is not None:
+                ctx.wgrad_hook(grad_w)
+            grad_x = mm(gq, NVFP4Tensor(wt_packed, wt_scale, wt_gs), out_dtype=x_dtype)
         else:
             grad_x = grad_y @ weight.to(grad_y.dtype)
-            grad_w = grad_y.t() @ x_or_packed
+            grad_w = grad_y.t() @ xt_or_x
         grad_b = None
         if ctx.has_bias:
             # The reference's grad_y.sum(0) is a bf16 tensor (fp32 accumulation, one rounding).
@@ -128,7 +135,7 @@ class _FP4LinearFn(torch.autograd.Function):
             grad_x.to(x_dtype),
             grad_w.to(weight.dtype),
             None if grad_b is None else grad_b.to(weight.dtype),
-            None, None, None, None, None, None, None, None, None, None, None, None,
+            None, None, None, None, None, None, None, None, None, None, None, None, None,
         )
 
 
@@ -159,6 +166,9 @@ class FP4Linear(nn.Linear):
         # forward GEMM, called as output_gemm(xq, wq, bias, out_dtype) (set by the fused N-split).
         self.reduce_grad_scale = None
         self.output_gemm = None
+        # Optional callable given the fp32 weight gradient as soon as the wgrad GEMM has produced it,
+        # before dgrad runs (a data-parallel job starts the gradient's reduction there).
+        self.wgrad_hook = None
         self.register_load_state_dict_post_hook(lambda module, *_: module.invalidate_fp4_cache())
 
     def invalidate_fp4_cache(self) -> None:
@@ -189,13 +199,17 @@ class FP4Linear(nn.Linear):
         self._cache_valid = True
 
     @torch.no_grad()
-    def apply_update_and_refresh_(self, update: torch.Tensor, alpha: float) -> None:
+    def apply_update_and_refresh_(self, update: torch.Tensor, alpha: float, reduce_global_scale=None) -> None:
         """The optimizer's last in-place step on this weight, ``weight.add_(update, alpha=alpha)``
         (radiance's Muon step, optim.py:518), fused with the cache refresh: one kernel applies the
         update and computes the new weight's global scale, then one pass quantizes both layouts.
-        Same cache contents as ``refresh_fp4_cache()`` after the update, without its amax read."""
+        Same cache contents as ``refresh_fp4_cache()`` after the update, without its amax read.
+        ``reduce_global_scale`` is applied to the new global scale before quantizing, as in
+        ``refresh_fp4_cache`` (an N-split slice passes the all-reduce(MAX) to the full weight's)."""
         w = self.weight.data
         update_and_global_scale_(w, update, alpha, out=self._w_fwd_gs)
+        if reduce_global_scale is not None:
+            reduce_global_scale(self._w_fwd_gs)
         self._w_dgrad_gs.copy_(self._w_fwd_gs)
         quantize_into_(
             w, global_scale=self._w_fwd_gs,
@@ -229,7 +243,7 @@ class FP4Linear(nn.Linear):
             _warn_fallback_once(self, x)
             return F.linear(x, self.weight.to(x.dtype), None if self.bias is None else self.bias.to(x.dtype))
         flat = x.reshape(-1, self.in_features).contiguous()
-        y = _FP4LinearFn.apply(*self._fn_args(flat), self.output_gemm, global_scale)
+        y = _FP4LinearFn.apply(*self._fn_args(flat), self.output_gemm, global_scale, self.wgrad_hook)
         return y.view(*x.shape[:-1], self.out_features)
 
 
@@ -255,7 +269,8 @@ class _FP4SwiGLUFn(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, x, weight, bias, w_fwd_packed, w_fwd_scale, w_fwd_gs, w_dgrad_packed, w_dgrad_scale,
-                w_dgrad_gs, hadamard, seed, recipe, reduce_grad_scale=None, output_gemm=None, x_global_scale=None):
+                w_dgrad_gs, hadamard, seed, recipe, reduce_grad_scale=None, output_gemm=None, x_global_scale=None,
+                wgrad_hook=None):
         produced = {}
 
         def gemm(xq, wq, b, out_dtype):
@@ -265,7 +280,7 @@ class _FP4SwiGLUFn(torch.autograd.Function):
 
         gu = _FP4LinearFn.forward(ctx, x, weight, bias, w_fwd_packed, w_fwd_scale, w_fwd_gs, w_dgrad_packed,
                                   w_dgrad_scale, w_dgrad_gs, hadamard, seed, recipe, reduce_grad_scale, gemm,
-                                  x_global_scale)
+                                  x_global_scale, wgrad_hook)
         ctx.gu = gu  # an intermediate, kept on ctx for the SwiGLU backward
         ctx.mark_non_differentiable(produced["gs"])
         return produced["h"], produced["gs"]
@@ -321,7 +336,7 @@ class FP4SwiGLU(FP4Linear):
             g, u = split_gate_up(gu)
             return F.silu(g) * u, None
         flat = x.reshape(-1, self.in_features).contiguous()
-        h, gs = _FP4SwiGLUFn.apply(*self._fn_args(flat), None, global_scale)
+        h, gs = _FP4SwiGLUFn.apply(*self._fn_args(flat), None, global_scale, self.wgrad_hook)
         return h.view(*x.shape[:-1], self.hidden_features), gs
 
 

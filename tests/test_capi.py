@@ -165,3 +165,12 @@ def test_update_global_scale_contract_is_checked_on_the_host():
     assert "dtypes" in lib.rb_nvfp4_last_error().decode()
     assert lib.rb_nvfp4_update_global_scale(None, 0, buf, 0, 16, ctypes.c_float(1.0), buf, buf, None) == 2
     assert lib.rb_nvfp4_update_global_scale(buf, 0, buf, 0, -1, ctypes.c_float(1.0), buf, buf, None) == 2
+
+
+def test_wait_selftest_rejects_bad_arguments_on_the_host():
+    lib = _lib.load()
+    buf = ctypes.c_void_p(256)
+    assert lib.rb_nvfp4_selftest_wait_timeout(2, 1000, buf, None) == 2
+    assert lib.rb_nvfp4_selftest_wait_timeout(0, 0, buf, None) == 2
+    assert lib.rb_nvfp4_selftest_wait_timeout(0, 1 << 40, buf, None) == 2
+    assert "limit_cycles" in lib.rb_nvfp4_last_error().decode()

@@ -26,7 +26,9 @@ def _worker(rank, world, port, results):
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
-    dist.init_process_group("gloo", rank=rank, world_size=world)
+    import datetime
+
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
     try:
         torch.manual_seed(0)
         m, k, n = 6, 8, 12
@@ -66,10 +68,7 @@ def test_column_parallel_collectives(world):
     for p in procs:
         p.start()
     for p in procs:
-        p.join(timeout=120)
-    for p in procs:
-        if p.is_alive():
-            p.kill()
+        p.join(timeout=300)
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     for r in range(world):
         assert all(results[r]), (r, results[r])
