@@ -124,6 +124,23 @@ int rb_nvfp4_quantize(const void* x, int dtype, int64_t rows, int64_t cols, int6
                       void* col_packed, void* col_scale, void* stream);
 
 /*
+ * rb_nvfp4_global_scale followed by rb_nvfp4_quantize, in one launch: the kernel reduces amax|x|
+ * over the whole input, meets all its CTAs at a grid barrier (a cooperative launch), writes
+ * *gs_out = max(amax / 2688, 1e-12) exactly as rb_nvfp4_global_scale does, and quantizes with it --
+ * the same bytes as the two calls, one launch fewer, and the quantizing pass re-reads the input from
+ * L2 when it fits there.  Replaces the `global_scale_of(x)` + `quantize(x, ...)` pairs of
+ * linear.py:79-80 and :127-136.
+ *   gs_out    : device fp32, written by the call.
+ *   workspace : 16 bytes of device memory, 16-byte aligned, zeroed before the first call; every call
+ *               leaves it ready for the next.  Calls that share a workspace must be ordered (same
+ *               stream).
+ * Other arguments, contract and outputs as rb_nvfp4_quantize.
+ */
+int rb_nvfp4_quantize_auto_scale(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld, float* gs_out,
+                                 const float* hadamard, const int64_t* seed, void* row_packed, void* row_scale,
+                                 void* col_packed, void* col_scale, void* workspace, void* stream);
+
+/*
  * Block-scaled NVFP4 GEMM on the tcgen05 tensor cores:
  *   out[i, j] = (alpha_a * alpha_b) * sum_k deq(a)[i, k] * deq(b)[j, k]  (+ bias[j])
  * with deq() the e2m1 codes times their e4m3 block scales.  Replaces `nvfp4_mm` + `mm`

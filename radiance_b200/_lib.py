@@ -30,6 +30,11 @@ SIGNATURES: dict[str, tuple] = {
         [_c_void_p, _int, _i64, _i64, _i64, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
          _c_void_p, _c_void_p],
     ),
+    "rb_nvfp4_quantize_auto_scale": (
+        _int,
+        [_c_void_p, _int, _i64, _i64, _i64, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
+         _c_void_p, _c_void_p, _c_void_p],
+    ),
     "rb_nvfp4_gemm": (
         _int,
         [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _c_void_p, _c_void_p, _c_void_p, _int,

@@ -49,8 +49,43 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
+// The tensor-map encoder is a driver call and needs a context current on this thread.  The runtime
+// binds the device's primary context lazily, on a thread's first runtime call that needs one; a
+// thread whose first call into this library encodes a tensor map (autograd's backward thread, for
+// one) gets it bound here, with driver calls that are legal during stream capture.
+static void bind_context() {
+  static thread_local int bound = -1;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || bound == dev) return;
+  using GetCurrent = CUresult (*)(CUcontext*);
+  using Retain = CUresult (*)(CUcontext*, CUdevice);
+  using SetCurrent = CUresult (*)(CUcontext);
+  static GetCurrent get_current = nullptr;
+  static Retain retain = nullptr;
+  static SetCurrent set_current = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess && p)
+      get_current = reinterpret_cast<GetCurrent>(p);
+    if (cudaGetDriverEntryPoint("cuDevicePrimaryCtxRetain", &p, cudaEnableDefault, &q) == cudaSuccess && p)
+      retain = reinterpret_cast<Retain>(p);
+    if (cudaGetDriverEntryPoint("cuCtxSetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess && p)
+      set_current = reinterpret_cast<SetCurrent>(p);
+  });
+  if (get_current == nullptr || retain == nullptr || set_current == nullptr) return;
+  CUcontext cur = nullptr;
+  if (get_current(&cur) == CUDA_SUCCESS && cur == nullptr) {
+    CUcontext primary = nullptr;  // the runtime's own context for this device (retained once per thread)
+    if (retain(&primary, (CUdevice)dev) == CUDA_SUCCESS) set_current(primary);
+  }
+  bound = dev;
+}
+
 bool make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, uint64_t cols, uint64_t rows,
                   uint64_t ld_bytes, uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swizzle) {
+  bind_context();
   auto enc = tensor_map_encoder();
   if (enc == nullptr) {
     set_error("cuTensorMapEncodeTiled is unavailable from the CUDA driver");

@@ -84,6 +84,14 @@ struct QuantArgs {
   // 128-row tile takes the group of its first row.
   const int64_t* offs;
   int ngroups;
+  // Fused global scale (gsync != nullptr; a cooperative launch): the kernel first reduces amax|x|
+  // over the whole input (x, row stride ld_bytes), meets every other CTA at a grid barrier, and
+  // writes the global scale to gs_out before quantizing with it.  gsync: four words {arrivals,
+  // generation, amax[2]} -- zero before the first launch, left consistent by each.
+  const void* x;
+  int64_t ld_bytes;
+  uint32_t* gsync;
+  float* gs_out;
 };
 
 // Group of row r: the last g with offs[g] <= r (empty groups share offsets with their neighbour).
@@ -685,6 +693,82 @@ __device__ __forceinline__ void col_part_f32(uint32_t tile, const uint32_t (&sgn
 }
 
 // ---------------------------------------------------------------------------------------------
+// Fused global scale: amax over the whole input, a grid barrier, then gs for every CTA
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Every thread of every CTA calls this (the launch is cooperative, so all CTAs are resident).  Each
+// warp scans whole rows with 16-byte loads (rows are 16-byte aligned: the quantizer's contract),
+// folding max |x| as fp32 bit patterns (non-negative floats order like their bits; NaN sorts above
+// infinity and propagates, as torch's amax does).  Thread 0 of each CTA folds the CTA's maximum
+// into amax[g & 1] of the generation g it read on entry and arrives at the barrier; the last to
+// arrive clears the arrival count and the other amax word (the next launch's), then releases the
+// generation.  Returns the global scale max(amax / 2688, 1e-12) (quantize.py:205-213), or -1 in
+// every thread if the barrier wait ran out (the kernel then reports status 1 and stops).
+template <bool F32IN>
+__device__ float fused_global_scale(const QuantArgs& a, uint32_t* red) {
+  constexpr int kPer = F32IN ? 4 : 8;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t nvec = a.K / kPer;
+  const int64_t gwarp = (int64_t)blockIdx.x * (kQThreads / 32) + warp;
+  const int64_t nwarps = (int64_t)gridDim.x * (kQThreads / 32);
+  uint32_t g = 0;
+  if (threadIdx.x == 0) g = ld_acquire_u32(a.gsync + 1);
+  uint32_t m = 0;
+  for (int64_t r = gwarp; r < a.M; r += nwarps) {
+    const uint4* row = reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(a.x) + r * a.ld_bytes);
+    for (int64_t c = lane; c < nvec; c += 32) {
+      const uint4 v = __ldg(row + c);
+      if constexpr (F32IN) {
+        m = max(m, max(max(v.x & 0x7FFFFFFFu, v.y & 0x7FFFFFFFu), max(v.z & 0x7FFFFFFFu, v.w & 0x7FFFFFFFu)));
+      } else {
+        m = __vmaxu2(m, __vmaxu2(__vmaxu2(v.x & 0x7FFF7FFFu, v.y & 0x7FFF7FFFu), __vmaxu2(v.z & 0x7FFF7FFFu, v.w & 0x7FFF7FFFu)));
+      }
+    }
+  }
+  if constexpr (!F32IN) m = max(m & 0xFFFFu, m >> 16) << 16;  // bf16 bits -> fp32 bits
+  m = __reduce_max_sync(0xFFFFFFFFu, m);
+  if (lane == 0) red[warp] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < kQThreads / 32; ++w) m = max(m, red[w]);
+    uint32_t* amax = a.gsync + 2;
+    atomicMax(amax + (g & 1), m);
+    __threadfence();
+    bool ok = true;
+    if (atomicAdd(a.gsync, 1u) == gridDim.x - 1) {
+      atomicExch(a.gsync, 0u);
+      atomicExch(amax + ((g + 1) & 1), 0u);
+      __threadfence();
+      atomicExch(a.gsync + 1, g + 1);
+    } else {
+      const long long start = clock64();
+      while (ld_acquire_u32(a.gsync + 1) == g) {
+        if (clock64() - start > kWaitLimitCycles) {
+          ok = false;
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+    float gs = -1.0f;
+    if (ok) {
+      const uint32_t mb = ld_acquire_u32(amax + (g & 1));
+      gs = __fdiv_rn(__uint_as_float(mb), 2688.0f);  // amax / (6 * 448), one IEEE divide
+      gs = (gs < 1e-12f) ? 1e-12f : gs;             // clamp(min=1e-12); NaN passes through
+      if (blockIdx.x == 0) *a.gs_out = gs;
+    }
+    red[0] = __float_as_uint(gs);
+  }
+  __syncthreads();
+  return __uint_as_float(red[0]);
+}
+
+// ---------------------------------------------------------------------------------------------
 // The tile loop and the kernel
 // ---------------------------------------------------------------------------------------------
 template <bool F32IN>
@@ -776,9 +860,23 @@ __global__ void __launch_bounds__(kQThreads, 2)
   c.had = smem_u32(hdr->had);
   c.key = 0;
   c.key_col = 0;
-  const int first_group =
-      (a.offs != nullptr) ? group_of_row(a.offs, a.ngroups, (int64_t)((int)blockIdx.x / a.tiles_k) * kQRows) : 0;
-  const float gs = a.gs[first_group];
+  float gs;
+  if (a.gsync != nullptr) {
+    // The global scale of the whole input, computed here while the first tiles are in flight.
+    gs = fused_global_scale<F32IN>(a, reinterpret_cast<uint32_t*>(hdr->sign_word));
+    if (gs < 0.0f) {
+      if (tid == 0) {
+        record_status(&g_quant_status, kStatusTimeoutTma);
+        for (int it = 0; it < S && it < n_my; ++it) mbar_wait(&hdr->full[it], 0);  // the copies in flight
+      }
+      __syncthreads();
+      return;
+    }
+  } else {
+    const int first_group =
+        (a.offs != nullptr) ? group_of_row(a.offs, a.ngroups, (int64_t)((int)blockIdx.x / a.tiles_k) * kQRows) : 0;
+    gs = a.gs[first_group];
+  }
   build_tables(hdr, gs, c);
   if constexpr (HAD) hdr->had[tid] = a.hadamard[tid];
   if constexpr (SR) {
@@ -1208,7 +1306,23 @@ static int launch_quant(const CUtensorMap& tmap, const QuantArgs& a, cudaStream_
   const int sms = rb_host::num_sms(dev);
   const int slots = sms * ((dev >= 0 && dev < 64) ? per_sm[dev] : 1);
   const int grid = a.n_tiles < slots ? a.n_tiles : slots;
-  kern<<<grid, kQThreads, smem, stream>>>(tmap, a);
+  if (a.gsync != nullptr) {
+    // The fused global scale meets every CTA at a grid barrier: a cooperative launch guarantees
+    // they are all resident (the grid never exceeds the occupancy-derived slot count).
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kQThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kern, tmap, a);
+  } else {
+    kern<<<grid, kQThreads, smem, stream>>>(tmap, a);
+  }
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     rb_host::set_error("nvfp4 quantize launch failed: %s", cudaGetErrorString(e));
@@ -1328,7 +1442,8 @@ int rb_nvfp4_update_global_scale(void* w, int w_dtype, const void* u, int u_dtyp
 
 static int quantize_impl(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld, const float* gs,
                          const int64_t* offs, int ngroups, const float* hadamard, const int64_t* seed,
-                         void* row_packed, void* row_scale, void* col_packed, void* col_scale, void* stream) {
+                         void* row_packed, void* row_scale, void* col_packed, void* col_scale, void* stream,
+                         float* gs_out = nullptr, uint32_t* gsync = nullptr) {
   const bool row = row_packed != nullptr || row_scale != nullptr;
   const bool col = col_packed != nullptr || col_scale != nullptr;
   if (!row && !col) {
@@ -1389,6 +1504,10 @@ static int quantize_impl(const void* x, int dtype, int64_t rows, int64_t cols, i
   a.n_tiles = (int)((rows / 128) * a.tiles_k);
   a.offs = offs;
   a.ngroups = ngroups;
+  a.x = x;
+  a.ld_bytes = ld * esize;
+  a.gsync = gsync;
+  a.gs_out = gs_out;
   const bool had = col && hadamard != nullptr;
   const bool sr = seed != nullptr;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
@@ -1400,6 +1519,17 @@ int rb_nvfp4_quantize(const void* x, int dtype, int64_t rows, int64_t cols, int6
                       void* col_packed, void* col_scale, void* stream) {
   return quantize_impl(x, dtype, rows, cols, ld, gs, nullptr, 0, hadamard, seed, row_packed, row_scale, col_packed,
                        col_scale, stream);
+}
+
+int rb_nvfp4_quantize_auto_scale(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld, float* gs_out,
+                                 const float* hadamard, const int64_t* seed, void* row_packed, void* row_scale,
+                                 void* col_packed, void* col_scale, void* workspace, void* stream) {
+  if (gs_out == nullptr || workspace == nullptr || (reinterpret_cast<uintptr_t>(workspace) & 15) != 0) {
+    rb_host::set_error("nvfp4 quantize_auto_scale: needs a global-scale output and a 16-byte aligned workspace");
+    return RB_ERR_ARG;
+  }
+  return quantize_impl(x, dtype, rows, cols, ld, gs_out, nullptr, 0, hadamard, seed, row_packed, row_scale,
+                       col_packed, col_scale, stream, gs_out, reinterpret_cast<uint32_t*>(workspace));
 }
 
 int rb_nvfp4_quantize_grouped(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld,

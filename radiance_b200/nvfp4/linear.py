@@ -31,6 +31,7 @@ from .quantize import (
     hadamard_matrix,
     mm,
     quantize,
+    quantize_auto_scale_into_,
     quantize_both,
     quantize_into_,
     quantize_supported_shape,
@@ -65,15 +66,16 @@ class _FP4LinearFn(torch.autograd.Function):
     def forward(ctx, x, weight, bias, w_fwd_packed, w_fwd_scale, w_fwd_gs, w_dgrad_packed, w_dgrad_scale,
                 w_dgrad_gs, hadamard, seed, recipe, reduce_grad_scale=None, output_gemm=None, x_global_scale=None,
                 wgrad_hook=None):
-        # The input's global scale, unless its producer already computed it (a SwiGLU epilogue).
-        gx = global_scale_of(x) if x_global_scale is None else x_global_scale
+        # The input's global scale comes from its producer when that computed it (a SwiGLU epilogue);
+        # otherwise the quantizer computes it in the same launch (global_scale_of, linear.py:79).
         rot = hadamard if recipe.hadamard and hadamard.numel() else None
         save_quantized = recipe.save_activations and recipe.grad_gemms and quantize_supported_shape(*x.shape)
         if save_quantized:
             # One read of x emits the forward operand and the packed wgrad operand (1.125 B/elt saved).
-            xq, xqt = quantize_both(x, global_scale=gx, hadamard=rot)
+            xq, xqt = quantize_both(x, global_scale=x_global_scale, hadamard=rot)
         else:
-            xq = quantize(x, -1, global_scale=gx)
+            xq = quantize(x, -1, global_scale=x_global_scale)
+        gx = xq.global_scale
         wq = NVFP4Tensor(w_fwd_packed, w_fwd_scale, w_fwd_gs)
         if output_gemm is None:
             y = mm(xq, wq, out_dtype=x.dtype, bias=bias)
@@ -105,9 +107,10 @@ class _FP4LinearFn(torch.autograd.Function):
         fp4_backward = recipe.grad_gemms and quantize_supported_shape(*grad_y.shape)
         if fp4_backward:
             rot = hadamard if recipe.hadamard and hadamard.numel() else None
+            gg = None  # by default the quantizer computes dY's global scale in the same launch
             if ctx.has_bias:  # the bias gradient's column sums come from the same read of dY
                 gg, colsum = global_scale_and_column_sums(grad_y)
-            else:
+            elif ctx.reduce_grad_scale is not None:
                 gg = global_scale_of(grad_y)
             if ctx.reduce_grad_scale is not None:  # e.g. the full gradient's scale for an N-split slice
                 ctx.reduce_grad_scale(gg)
@@ -188,14 +191,14 @@ class FP4Linear(nn.Linear):
         if not w.is_cuda:
             require_nvfp4("FP4Linear.refresh_fp4_cache")
             raise RuntimeError("FP4Linear.refresh_fp4_cache: the weight must be on the CUDA device")
-        global_scale_of(w, out=self._w_fwd_gs)
-        if reduce_global_scale is not None:
+        row, col = (self._w_fwd_packed, self._w_fwd_scale), (self._w_dgrad_packed, self._w_dgrad_scale)
+        if reduce_global_scale is None:  # global scale and both layouts in one launch
+            quantize_auto_scale_into_(w, out_scale=self._w_fwd_gs, row=row, col=col)
+        else:
+            global_scale_of(w, out=self._w_fwd_gs)
             reduce_global_scale(self._w_fwd_gs)
+            quantize_into_(w, global_scale=self._w_fwd_gs, row=row, col=col)
         self._w_dgrad_gs.copy_(self._w_fwd_gs)
-        quantize_into_(
-            w, global_scale=self._w_fwd_gs,
-            row=(self._w_fwd_packed, self._w_fwd_scale), col=(self._w_dgrad_packed, self._w_dgrad_scale),
-        )
         self._cache_valid = True
 
     @torch.no_grad()

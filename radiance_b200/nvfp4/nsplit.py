@@ -118,7 +118,7 @@ class PeerOutput:
     in this process (None for this rank).  Creating one is collective over the group (the handles
     travel by ``all_gather_object``); it cannot happen during stream capture."""
 
-    _TYPESTR = {torch.bfloat16: "<V2", torch.float32: "<f4"}
+    _TYPESTR = {torch.bfloat16: "<i2", torch.float32: "<f4"}
 
     def __init__(self, rows: int, cols: int, dtype: torch.dtype, device: torch.device, group, world: int, rank: int):
         lib = _lib.load()
@@ -140,9 +140,9 @@ class PeerOutput:
                 q = ctypes.c_void_p()
                 _lib.check(lib.rb_peer_open(handles[p], ctypes.byref(q)), "nsplit peer buffer")
                 self.peer_ptrs.append(q.value)
-        # bf16 has no array-interface type code: wrap as 2-byte raw words, then view as bf16.
+        # bf16 has no array-interface type code: wrap as 16-bit integers, then view as bf16.
         raw = torch.as_tensor(_CudaArray(self.ptr, (rows, cols), self._TYPESTR[dtype], self), device=device)
-        self.tensor = raw.view(torch.int16).view(dtype) if dtype == torch.bfloat16 else raw
+        self.tensor = raw.view(dtype) if dtype == torch.bfloat16 else raw
         self.handed_out = None  # weak reference to the last output view given to a caller
 
     def close(self, group) -> None:

@@ -345,6 +345,80 @@ def _quantize_into(
     _trace.end(tok)
 
 
+_SYNC_WS: dict[tuple[torch.device, int], torch.Tensor] = {}
+
+
+def _sync_workspace(device: torch.device) -> torch.Tensor:
+    """16 bytes of zeroed device memory per (device, stream) for the fused global-scale quantizer's
+    grid barrier; every call leaves it ready for the next, so calls ordered on one stream share it."""
+    key = (device, _stream_ptr(device))
+    ws = _SYNC_WS.get(key)
+    if ws is None:
+        ws = torch.zeros(4, dtype=torch.int32, device=device)
+        _SYNC_WS[key] = ws
+    return ws
+
+
+def _quantize_auto_scale_into(
+    x: torch.Tensor,
+    *,
+    out_scale: torch.Tensor,
+    hadamard: torch.Tensor | None,
+    stochastic: bool,
+    seed: torch.Tensor | int,
+    row: tuple[torch.Tensor, torch.Tensor] | None,
+    col: tuple[torch.Tensor, torch.Tensor] | None,
+) -> None:
+    lib = _lib.load()
+    m, k = x.shape
+    seed_t = None
+    if stochastic:
+        seed_t = seed if isinstance(seed, torch.Tensor) else _default_seed(x.device, int(seed))
+        if seed_t.dtype != torch.int64 or not seed_t.is_cuda:
+            seed_t = seed_t.to(device=x.device, dtype=torch.int64)
+    had = None
+    if hadamard is not None and hadamard.numel():
+        had = hadamard.to(device=x.device, dtype=torch.float32).contiguous()
+        if had.shape != (BLOCK, BLOCK):
+            raise ValueError(f"nvfp4.quantize: hadamard must be {BLOCK}x{BLOCK}, got {tuple(had.shape)}")
+    if out_scale.dtype != torch.float32 or not out_scale.is_cuda or out_scale.numel() != 1:
+        raise ValueError("nvfp4.quantize: the global-scale output must be a 0-d fp32 CUDA tensor")
+    forms = (row is not None) + (col is not None)
+    tok = _trace.begin("quantize", m * k * (x.element_size() + 0.5625 * forms))
+    _lib.check(
+        lib.rb_nvfp4_quantize_auto_scale(
+            x.data_ptr(), _dtype_code(x), m, k, x.stride(0), out_scale.data_ptr(),
+            None if had is None else had.data_ptr(), None if seed_t is None else seed_t.data_ptr(),
+            None if row is None else row[0].data_ptr(), None if row is None else row[1].data_ptr(),
+            None if col is None else col[0].data_ptr(), None if col is None else col[1].data_ptr(),
+            _sync_workspace(x.device).data_ptr(), _stream_ptr(x.device),
+        ),
+        "nvfp4.quantize",
+    )
+    _trace.end(tok)
+
+
+def quantize_auto_scale_into_(
+    x: torch.Tensor,
+    *,
+    out_scale: torch.Tensor,
+    row: tuple[torch.Tensor, torch.Tensor] | None = None,
+    col: tuple[torch.Tensor, torch.Tensor] | None = None,
+    hadamard: torch.Tensor | None = None,
+    stochastic: bool = False,
+    seed: torch.Tensor | int = 0,
+) -> torch.Tensor:
+    """``global_scale_of(x, out=out_scale)`` then ``quantize_into_(x, global_scale=out_scale, ...)`` in
+    one kernel (``rb_nvfp4_quantize_auto_scale``): the same global scale and bytes, one launch fewer,
+    and the quantizing pass re-reads ``x`` from L2 when it fits there.  Returns ``out_scale``."""
+    _require_cuda(x, "nvfp4.quantize_auto_scale_into_")
+    _check_shape(x, "rowblock" if col is None else "colblock")
+    x = _prep_input(x)
+    _quantize_auto_scale_into(x, out_scale=out_scale, hadamard=hadamard, stochastic=stochastic, seed=seed, row=row,
+                              col=col)
+    return out_scale
+
+
 def _check_shape(x: torch.Tensor, form: str) -> None:
     if x.dim() != 2:
         raise ValueError(f"nvfp4.quantize expects a 2-D tensor, got shape {tuple(x.shape)}")
@@ -402,16 +476,15 @@ def quantize(
         raise ValueError(f"nvfp4.quantize supports axis 0 or -1, got {axis}")
     _check_shape(x, form)
     x = _prep_input(x)
-    if global_scale is None:
-        global_scale = global_scale_of(x)
-    if form == "rowblock":
-        buf = _alloc_row(x)
-        _quantize_into(x, global_scale=global_scale, hadamard=None, stochastic=stochastic, seed=seed, row=buf, col=None)
+    buf = _alloc_row(x) if form == "rowblock" else _alloc_col(x)
+    row, col = (buf, None) if form == "rowblock" else (None, buf)
+    had = None if form == "rowblock" else hadamard
+    if global_scale is None:  # the global scale and the quantization in one launch
+        global_scale = torch.empty((), dtype=torch.float32, device=x.device)
+        _quantize_auto_scale_into(x, out_scale=global_scale, hadamard=had, stochastic=stochastic, seed=seed, row=row,
+                                  col=col)
     else:
-        buf = _alloc_col(x)
-        _quantize_into(
-            x, global_scale=global_scale, hadamard=hadamard, stochastic=stochastic, seed=seed, row=None, col=buf
-        )
+        _quantize_into(x, global_scale=global_scale, hadamard=had, stochastic=stochastic, seed=seed, row=row, col=col)
     return _as_nvfp4(buf, global_scale)
 
 
@@ -425,19 +498,23 @@ def quantize_both(
 ) -> tuple[NVFP4Tensor, NVFP4Tensor]:
     """Both forms from one read of ``x``: ``(quantize(x, -1, ...), quantize(x, 0, hadamard=...))``.
 
-    Bit-identical to the two separate calls for round-to-nearest.  This is what ``FP4Linear``
+    Bit-identical to the two separate calls for round-to-nearest.  Without ``global_scale`` the
+    global scale is computed in the same launch (``quantize_auto_scale_into_``).  This is what ``FP4Linear``
     uses: the reference quantizes each activation and each upstream gradient both ways per
     micro-batch (linear.py:80, :99, :129, :133), two full reads of the bf16 tensor.
     """
     _require_cuda(x, "nvfp4.quantize_both")
     _check_shape(x, "rowblock+colblock")
     x = _prep_input(x)
-    if global_scale is None:
-        global_scale = global_scale_of(x)
     row, col = _alloc_row(x), _alloc_col(x)
-    _quantize_into(
-        x, global_scale=global_scale, hadamard=hadamard, stochastic=stochastic, seed=seed, row=row, col=col
-    )
+    if global_scale is None:  # the global scale and both forms in one launch
+        global_scale = torch.empty((), dtype=torch.float32, device=x.device)
+        _quantize_auto_scale_into(x, out_scale=global_scale, hadamard=hadamard, stochastic=stochastic, seed=seed,
+                                  row=row, col=col)
+    else:
+        _quantize_into(
+            x, global_scale=global_scale, hadamard=hadamard, stochastic=stochastic, seed=seed, row=row, col=col
+        )
     return _as_nvfp4(row, global_scale), _as_nvfp4(col, global_scale)
 
 
