@@ -7,9 +7,9 @@ it -- two Triton kernels and ``torch._scaled_mm_v2`` in the reference -- is repl
 block-scaled GEMM for sm_100a.  There is no CPU path: every op raises on a non-CUDA tensor, and if
 the library is missing.
 
-The reference's pure-torch emulation (``quantize_reference``, ``ref_quantize_rowblock``,
-``ref_quantize_colblock``, ``encode_e2m1``, ``dequantize``, ``ref_to_blocked``) is the format's
-definition and stays in radiance; these kernels are asserted bit-identical to it.
+The reference's pure-torch format definition (``quantize_reference``, ``ref_quantize_rowblock``,
+``ref_quantize_colblock``, ``encode_e2m1``, ``dequantize``, ``ref_to_blocked``, ``_block_scale``) is
+re-exported from ``reference.py`` with the same names; nothing here calls it.
 """
 
 from __future__ import annotations
@@ -586,7 +586,18 @@ def _gemm(
     return out if native == out_dtype else out.to(out_dtype)
 
 
-@torch.library.custom_op("radiance_b200::nvfp4_mm", mutates_args=())
+def _nvfp4_mm_name() -> str:
+    """The reference registers its op as ``radiance::nvfp4_mm`` (quantize.py:359-371) and code that
+    swaps this package in finds it under that name.  Should radiance itself be loaded in the same
+    process, its registration stands and this one moves to ``radiance_b200::nvfp4_mm``."""
+    try:
+        torch.ops.radiance.nvfp4_mm  # noqa: B018 -- raises when no such op is registered
+    except (AttributeError, RuntimeError):
+        return "radiance::nvfp4_mm"
+    return "radiance_b200::nvfp4_mm"
+
+
+@torch.library.custom_op(_nvfp4_mm_name(), mutates_args=())
 def nvfp4_mm(
     a_packed: torch.Tensor,
     a_scale: torch.Tensor,
