@@ -11,6 +11,7 @@ needs; the weak-scaled replica number (16384 tokens on every rank, no reduction)
 it.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 2|3|4|5]
+    python bench.py case quant|gemm|swiglu|block-gemms [...]   (one kernel's workload, for ncu or --time)
 
 Prints one JSON line (rank 0).  ``--impl reference`` times the reference's CPU implementation of
 the path (the NumPy restatement of radiance's pure-torch NVFP4 emulation in ``oracle/``) on the
@@ -1216,7 +1217,217 @@ def run_config5(args):
         dist.destroy_process_group()
 
 
+# --------------------------------------------------------------------------------------------------
+# Profiling cases: one kernel's fixed workload at a time (for ncu, or timed with --time)
+# --------------------------------------------------------------------------------------------------
+CASES_DOC = """python bench.py case <name> [options]
+
+One kernel's fixed workload, run --iters times with nothing else in between and between
+cudaProfilerStart/Stop (so `ncu --profile-from-start off` captures only those launches), or, with
+--time, captured in a CUDA graph, replayed and timed with CUDA events (one JSON line).
+
+  quant        one quantization per iteration: --rows --cols --form row|col|both --hadamard --sr
+               --scale given (a precomputed global scale) | auto (the fused global-scale quantizer)
+               | separate (the amax kernel, then the quantizer)
+  gemm         one block-scaled GEMM, bf16 out: --m --n --k; --variant cublas runs cuBLASLt's NVFP4
+               GEMM (torch._scaled_mm_v2) on the same operands instead, for comparison
+  swiglu       the SwiGLU producer of a config-3 FFN: --variant fused (the gate/up GEMM whose epilogue
+               writes h and its global scale) | unfused (GEMM, torch F.silu(g) * u, amax); each then
+               quantizes h both ways
+  block-gemms  the twelve GEMMs of one config-3 block step (four linears x fwd, dgrad, wgrad): --tokens
+
+Inputs are seeded synthetic tensors (activations ~N(0, 1), weights ~N(0, 0.02)); a timed case reuses
+its inputs every iteration."""
+
+
+def _case_quant(args, dev):
+    import torch
+
+    from radiance_b200.nvfp4.quantize import (col_scale_bytes, global_scale_of, hadamard_matrix,
+                                              quantize_auto_scale_into_, quantize_into_, row_scale_bytes)
+
+    g = torch.Generator(device="cpu").manual_seed(7)
+    x = torch.randn(args.rows, args.cols, generator=g).to(dev, torch.bfloat16)
+    gs = global_scale_of(x)
+    h = hadamard_matrix(device=dev) if args.hadamard else None
+    seed = torch.tensor(3, device=dev, dtype=torch.int64)
+    row = (torch.empty(args.rows, args.cols // 2, dtype=torch.uint8, device=dev),
+           torch.empty(row_scale_bytes(args.rows, args.cols), dtype=torch.uint8, device=dev))
+    col = (torch.empty(args.cols, args.rows // 2, dtype=torch.uint8, device=dev),
+           torch.empty(col_scale_bytes(args.rows, args.cols), dtype=torch.uint8, device=dev))
+    r = row if args.form in ("row", "both") else None
+    c = col if args.form in ("col", "both") else None
+
+    def run():
+        if args.scale == "auto":
+            quantize_auto_scale_into_(x, out_scale=gs, row=r, col=c, hadamard=h, stochastic=args.sr, seed=seed)
+            return
+        if args.scale == "separate":
+            global_scale_of(x, out=gs)
+        quantize_into_(x, global_scale=gs, row=r, col=c, hadamard=h, stochastic=args.sr, seed=seed)
+
+    forms = (r is not None) + (c is not None)
+    return run, {"work": args.rows * args.cols * (2 + 0.5625 * forms), "unit": "GB/s",
+                 "basis": "algorithmic bytes of the quantizer: 2 B read + 0.5625 B written per element and form"}
+
+
+def _operands(m, n, k, dev, g, a_scale=1.0, b_scale=0.02):
+    import torch
+
+    from radiance_b200.nvfp4.quantize import quantize
+
+    a = quantize((torch.randn(m, k, generator=g) * a_scale).to(dev, torch.bfloat16), -1)
+    b = quantize((torch.randn(n, k, generator=g) * b_scale).to(dev, torch.bfloat16), -1)
+    return a, b
+
+
+def _case_gemm(args, dev):
+    import torch
+
+    from radiance_b200.nvfp4.quantize import _gemm
+
+    g = torch.Generator(device="cpu").manual_seed(11)
+    a, b = _operands(args.m, args.n, args.k, dev, g)
+    out = torch.empty(args.m, args.n, dtype=torch.bfloat16, device=dev)
+    if args.variant == "cublas":
+        from torch._C import _ScalingType, _SwizzleType
+
+        blk = [_ScalingType.BlockWise1x16.value]
+        swz = [_SwizzleType.SWIZZLE_32_4_4.value]
+
+        def run():
+            torch._scaled_mm_v2(a.packed, b.packed.t(), scale_a=[a.scale], recipe_a=blk, swizzle_a=swz,
+                                scale_b=[b.scale], recipe_b=blk, swizzle_b=swz, bias=None, out_dtype=torch.bfloat16)
+    else:
+        def run():
+            _gemm(a.packed.view(torch.uint8), a.scale.view(torch.uint8), b.packed.view(torch.uint8),
+                  b.scale.view(torch.uint8), a.global_scale, b.global_scale, None, torch.bfloat16, out)
+    return run, {"work": 2.0 * args.m * args.n * args.k, "unit": "TFLOP/s", "basis": "2*M*N*K"}
+
+
+def _case_swiglu(args, dev):
+    import torch
+    import torch.nn.functional as F
+
+    from radiance_b200.nvfp4.quantize import (_gemm, col_scale_bytes, global_scale_of, hadamard_matrix,
+                                              interleave_gate_up, quantize, quantize_into_, row_scale_bytes,
+                                              swiglu_mm)
+
+    g = torch.Generator(device="cpu").manual_seed(17)
+    m, k, hid = args.m, args.k, args.hidden
+    xq = quantize(torch.randn(m, k, generator=g).to(dev, torch.bfloat16), -1)
+    w = interleave_gate_up((torch.randn(hid, k, generator=g) * 0.02).to(dev, torch.bfloat16),
+                           (torch.randn(hid, k, generator=g) * 0.02).to(dev, torch.bfloat16))
+    wq = quantize(w, -1)
+    gu = torch.empty(m, 2 * hid, dtype=torch.bfloat16, device=dev)
+    h = torch.empty(m, hid, dtype=torch.bfloat16, device=dev)
+    gs = torch.empty((), dtype=torch.float32, device=dev)
+    rot = hadamard_matrix(device=dev)
+    row = (torch.empty(m, hid // 2, dtype=torch.uint8, device=dev),
+           torch.empty(row_scale_bytes(m, hid), dtype=torch.uint8, device=dev))
+    col = (torch.empty(hid, m // 2, dtype=torch.uint8, device=dev),
+           torch.empty(col_scale_bytes(m, hid), dtype=torch.uint8, device=dev))
+
+    def run():
+        if args.variant == "fused":
+            swiglu_mm(xq, wq, out=gu, h=h, h_global_scale=gs)
+            hh = h
+        else:  # separate gate_proj / up_proj outputs, as radiance has them
+            _gemm(xq.packed.view(torch.uint8), xq.scale.view(torch.uint8), wq.packed.view(torch.uint8),
+                  wq.scale.view(torch.uint8), xq.global_scale, wq.global_scale, None, torch.bfloat16, gu)
+            hh = F.silu(gu[:, :hid]) * gu[:, hid:]
+            global_scale_of(hh, out=gs)
+        quantize_into_(hh, global_scale=gs, row=row, col=col, hadamard=rot)
+
+    return run, {"work": 2.0 * m * 2 * hid * k, "unit": "TFLOP/s", "basis": "2*M*N*K of the gate/up GEMM"}
+
+
+def _case_block_gemms(args, dev):
+    """Per linear (in k, out n, T tokens): fwd (T x n x k, bf16 out), dgrad (T x k x n, bf16 out),
+    wgrad (n x k x T, fp32 out) -- the three ``mm`` calls of ``_FP4LinearFn``."""
+    import torch
+
+    from radiance_b200.nvfp4.quantize import _gemm
+
+    g = torch.Generator(device="cpu").manual_seed(13)
+    tokens = args.tokens
+    calls = []
+    for _, k, n in LAYERS:
+        for (m_, n_, k_, out_dtype) in ((tokens, n, k, torch.bfloat16), (tokens, k, n, torch.bfloat16),
+                                        (n, k, tokens, torch.float32)):
+            a, b = _operands(m_, n_, k_, dev, g)
+            out = torch.empty(m_, n_, dtype=out_dtype, device=dev)
+            calls.append((a, b, out, out_dtype))
+
+    def run():
+        for a, b, out, out_dtype in calls:
+            _gemm(a.packed.view(torch.uint8), a.scale.view(torch.uint8), b.packed.view(torch.uint8),
+                  b.scale.view(torch.uint8), a.global_scale, b.global_scale, None, out_dtype, out)
+
+    return run, {"work": 6.0 * tokens * LAYER_KN, "unit": "TFLOP/s", "basis": "6*T*sum(K*N) over the four linears"}
+
+
+def run_case(argv):
+    import torch
+
+    ap = argparse.ArgumentParser(prog="bench.py case", description=CASES_DOC,
+                                 formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("name", choices=["quant", "gemm", "swiglu", "block-gemms"])
+    ap.add_argument("--rows", type=int, default=16384)
+    ap.add_argument("--cols", type=int, default=6144)
+    ap.add_argument("--form", choices=["row", "col", "both"], default="both")
+    ap.add_argument("--hadamard", action="store_true")
+    ap.add_argument("--sr", action="store_true")
+    ap.add_argument("--scale", choices=["given", "auto", "separate"], default="given")
+    ap.add_argument("--m", type=int, default=16384)
+    ap.add_argument("--n", type=int, default=6144)
+    ap.add_argument("--k", type=int, default=2048)
+    ap.add_argument("--hidden", type=int, default=5632)
+    ap.add_argument("--tokens", type=int, default=16384)
+    ap.add_argument("--variant", default="ours", help="gemm: ours|cublas; swiglu: fused|unfused")
+    ap.add_argument("--iters", type=int, default=3)
+    ap.add_argument("--time", action="store_true", help="graph-capture the iterations and time them (one JSON line)")
+    args = ap.parse_args(argv)
+    if args.name == "swiglu" and args.variant == "ours":
+        args.variant = "fused"
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    run, info = {"quant": _case_quant, "gemm": _case_gemm, "swiglu": _case_swiglu,
+                 "block-gemms": _case_block_gemms}[args.name](args, dev)
+    if not args.time:
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        for _ in range(args.iters):
+            run()
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+        return
+    reps = max(args.iters, 3)
+    for _ in range(3):
+        run()
+    graph = _capture(lambda: [run() for _ in range(reps)])
+    graph.replay()
+    torch.cuda.synchronize()
+    best = None
+    for _ in range(5):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        graph.replay()
+        e.record()
+        torch.cuda.synchronize()
+        ms = s.elapsed_time(e) / reps
+        best = ms if best is None else min(best, ms)
+    scale = 1e9 if info["unit"] == "GB/s" else 1e12
+    print(json.dumps({"case": args.name, "args": {k: v for k, v in vars(args).items() if k != "time"},
+                      "us_per_iter": round(best * 1e3, 2), "value": round(info["work"] / (best * 1e-3) / scale, 1),
+                      "unit": info["unit"], "basis": info["basis"],
+                      "timing": f"{reps} iterations per CUDA graph replay, best of 5 replays"}), flush=True)
+
+
 def main():
+    if sys.argv[1:2] == ["case"]:
+        run_case(sys.argv[2:])
+        return
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=300)
