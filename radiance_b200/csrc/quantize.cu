@@ -107,6 +107,7 @@ __device__ __forceinline__ int group_of_row(const int64_t* offs, int ngroups, in
 
 struct QHeader {
   uint64_t full[kQStages];
+  uint64_t empty[kQStages];  // one arrive per warp when it is done with the stage's tile
   // Per e4m3 byte e: (D_e, RN(1/D_e), thr_e, 0), D_e = value(e) * gs and thr_e the smallest block
   // amax whose scale byte exceeds e (NaN: none).  16-byte entries, so both loads of pick_scale
   // are aligned.
@@ -784,54 +785,85 @@ __device__ __forceinline__ void issue_tile(const CUtensorMap& tmap, const QuantA
               mt * kQRows);
 }
 
+// The warps of a CTA run decoupled: each waits for a tile's TMA data on its own, works its part,
+// and releases the stage with one arrive on the stage's `empty` barrier.  Warp 0 refills a stage one
+// tile late -- after finishing tile it, it waits for every warp's release of tile it - 1 and loads
+// tile it - 1 + S into that stage -- so no warp ever waits at a block-wide barrier for the slowest
+// one (grouped launches still meet at one when a tile's group changes the scale tables).  A wait
+// that runs out records its status; the warp then skips the remaining work, still arriving where
+// the others count on it, with no further waiting.
 template <bool F32IN, bool DO_ROW, bool DO_COL, int HADM, bool SR>
 __device__ __forceinline__ void quant_loop(const CUtensorMap& tmap, const QuantArgs& a, QHeader* hdr, uint8_t* smem,
                                            QCtx& c, uint32_t cur_gs, int n_my) {
   constexpr int S = kQStages;
   constexpr int kCols = QTile<F32IN>::kCols;
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   uint32_t sgn[16];
 #pragma unroll
   for (int j = 0; j < 16; ++j) sgn[j] = (HADM == 1) ? hdr->sign_word[j] : 0u;
+  bool failed = false;  // warp-uniform
 
   for (int it = 0; it < n_my; ++it) {
     const int s = it % S;
-    const bool ok = mbar_wait(&hdr->full[s], (uint32_t)((it / S) & 1));
-    // Every thread has finished tile it-1 once past this barrier, so its stage may be refilled.
-    if (__syncthreads_or(!ok)) {
-      if (tid == 0) record_status(&g_quant_status, kStatusTimeoutTma);
-      return;
+    const bool ok = __all_sync(0xFFFFFFFFu, mbar_wait(&hdr->full[s], (uint32_t)((it / S) & 1),
+                                                      failed ? 0 : kWaitLimitCycles));
+    if (!ok && !failed) {
+      failed = true;
+      if (lane == 0) record_status(&g_quant_status, kStatusTimeoutTma);
     }
-    if (tid == 0 && it >= 1 && it - 1 + S < n_my) issue_tile<F32IN>(tmap, a, hdr, smem, it - 1 + S);
-
     const int t = (int)blockIdx.x + it * (int)gridDim.x;
     const int mt = t / a.tiles_k, kt = t - mt * a.tiles_k;
     const int64_t m0 = (int64_t)mt * kQRows, k0 = (int64_t)kt * kCols;
     const int valid_cols = (int)min((int64_t)kCols, a.K - k0);
     if (a.offs != nullptr) {
-      // A tile of another group: rebuild the tables for its global scale (every thread is past
-      // the previous tile here, so the tables are free).
+      // A tile of another group: rebuild the tables for its global scale once every warp is done
+      // with the previous tile (the condition is the same in every warp).
       const float gt = a.gs[group_of_row(a.offs, a.ngroups, m0)];
       if (__float_as_uint(gt) != cur_gs) {
         cur_gs = __float_as_uint(gt);
+        __syncthreads();
         build_tables(hdr, gt, c);
         __syncthreads();
       }
     }
-    const uint32_t tile = smem_u32(smem + (size_t)s * kQTileBytes);
-    if constexpr (DO_COL) {
-      if constexpr (!F32IN) col_part_bf16<HADM, SR>(tile, sgn, c, a, m0, k0, valid_cols);
-      else col_part_f32<HADM, SR>(tile, sgn, c, a, m0, k0);
-    }
-    if constexpr (DO_ROW) {
-      const int r = tid & 127, h = tid >> 7;
-      const uint32_t rb = tile + h * kQBoxBytes + r * 128 + ((r & 7) << 4);
-      uint32_t rk[8];
+    if (!failed) {
+      const uint32_t tile = smem_u32(smem + (size_t)s * kQTileBytes);
+      if constexpr (DO_COL) {
+        if constexpr (!F32IN) col_part_bf16<HADM, SR>(tile, sgn, c, a, m0, k0, valid_cols);
+        else col_part_f32<HADM, SR>(tile, sgn, c, a, m0, k0);
+      }
+      if constexpr (DO_ROW) {
+        const int r = tid & 127, h = tid >> 7;
+        const uint32_t rb = tile + h * kQBoxBytes + r * 128 + ((r & 7) << 4);
+        uint32_t rk[8];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) rk[k] = rb ^ (uint32_t)(k << 4);
-      row_part<F32IN, SR>(rk, c, a, m0, k0, mt, (F32IN ? 32 : 64) * h < valid_cols);
+        for (int k = 0; k < 8; ++k) rk[k] = rb ^ (uint32_t)(k << 4);
+        row_part<F32IN, SR>(rk, c, a, m0, k0, mt, (F32IN ? 32 : 64) * h < valid_cols);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&hdr->empty[s]);  // this warp is done reading the stage
+    if (warp == 0 && it >= 1 && it - 1 + S < n_my) {
+      const int ps = (it - 1) % S;
+      bool e = false;
+      if (lane == 0 && !failed) {
+        e = mbar_wait(&hdr->empty[ps], (uint32_t)(((it - 1) / S) & 1));
+        if (e) issue_tile<F32IN>(tmap, a, hdr, smem, it - 1 + S);
+        else record_status(&g_quant_status, kStatusTimeoutProducer);
+      }
+      e = __shfl_sync(0xFFFFFFFFu, e, 0);
+      if (!e) failed = true;
     }
   }
+}
+
+// The general-rotation loop as a separate (not inlined) function: it holds more values live than
+// the Sylvester fast path, and keeping it out of the kernel body leaves the fast path's register
+// allocation to itself.
+template <bool F32IN, bool DO_ROW, bool DO_COL, bool SR>
+__device__ __noinline__ void quant_loop_general(const CUtensorMap& tmap, const QuantArgs& a, QHeader* hdr,
+                                                uint8_t* smem, QCtx& c, uint32_t cur_gs, int n_my) {
+  quant_loop<F32IN, DO_ROW, DO_COL, 2, SR>(tmap, a, hdr, smem, c, cur_gs, n_my);
 }
 
 template <bool F32IN, bool DO_ROW, bool DO_COL, bool HAD, bool SR>
@@ -847,7 +879,10 @@ __global__ void __launch_bounds__(kQThreads, 2)
   const int n_my = (a.n_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
 
   if (tid == 0) {
-    for (int s = 0; s < S; ++s) mbar_init(&hdr->full[s], 1);
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&hdr->full[s], 1);
+      mbar_init(&hdr->empty[s], kQThreads / 32);
+    }
     fence_mbar_init();
     prefetch_tensormap(&tmap);
   }
@@ -900,7 +935,7 @@ __global__ void __launch_bounds__(kQThreads, 2)
     }
     __syncthreads();
     if (hdr->had_fast) quant_loop<F32IN, DO_ROW, DO_COL, 1, SR>(tmap, a, hdr, smem, c, __float_as_uint(gs), n_my);
-    else quant_loop<F32IN, DO_ROW, DO_COL, 2, SR>(tmap, a, hdr, smem, c, __float_as_uint(gs), n_my);
+    else quant_loop_general<F32IN, DO_ROW, DO_COL, SR>(tmap, a, hdr, smem, c, __float_as_uint(gs), n_my);
   } else {
     quant_loop<F32IN, DO_ROW, DO_COL, 0, SR>(tmap, a, hdr, smem, c, __float_as_uint(gs), n_my);
   }
