@@ -175,10 +175,10 @@ class BlockStep:
     r*N/g .. (r+1)*N/g) on a side stream, issued from the layer's wgrad hook the moment its wgrad GEMM
     has produced dW, so the reduction overlaps that layer's dgrad and the layers still to come."""
 
-    def __init__(self, layers, world, device, reduce=True):
+    def __init__(self, layers, world, device, reduce=True, group=None):
         import torch
 
-        self.layers, self.world = layers, world
+        self.layers, self.world, self.group = layers, world, group
         self.reduce = reduce and world > 1
         self.side = torch.cuda.Stream(device)
         self.shards = [torch.empty(lin.out_features // world, lin.in_features, device=device) for lin in layers]
@@ -195,7 +195,7 @@ class BlockStep:
             self.side.wait_stream(torch.cuda.current_stream())
             with torch.cuda.stream(self.side):
                 tok = _trace.begin("reduce_scatter", grad_w.numel() * 4)
-                dist.reduce_scatter_tensor(self.shards[i], grad_w)
+                dist.reduce_scatter_tensor(self.shards[i], grad_w, group=self.group)
                 _trace.end(tok)
             self._pending.append(grad_w)  # keeps dW alive until the side stream has consumed it
         return hook
@@ -309,7 +309,22 @@ def run_ours(args):
     xs_host, dys_host = _make_inputs(tokens, seed=1000 + rank)
     xs = [x.to(device) for x in xs_host]
     dys = [d.to(device) for d in dys_host]
-    step = BlockStep(layers, world, device)
+    rs_group = None
+    comm_sms = 0
+    if world > 1:
+        # The gradient reduce-scatters get their own communicator, limited to --comm-sms CTAs, and
+        # this library's kernels leave that many SMs free, so the collective runs beside the GEMMs
+        # and quantizers instead of waiting for SMs between them.
+        from radiance_b200 import _lib
+
+        comm_sms = max(0, args.comm_sms)
+        opts = dist.ProcessGroupNCCL.Options()
+        if comm_sms:
+            opts.config.max_ctas = comm_sms
+            opts.config.min_ctas = min(comm_sms, 4)
+            _lib.set_sm_budget(torch.cuda.get_device_properties(device).multi_processor_count - comm_sms)
+        rs_group = dist.new_group(ranks=list(range(world)), backend="nccl", pg_options=opts)
+    step = BlockStep(layers, world, device, group=rs_group)
 
     def barrier():
         if world > 1:
@@ -345,6 +360,9 @@ def run_ours(args):
     # ---- weak-scaled replicas (N > 1): every rank a whole 16384-token micro-batch, no collective
     weak = None
     if world > 1 and not args.tokens_per_rank:
+        from radiance_b200 import _lib
+
+        _lib.set_sm_budget(0)  # replicas have no collective to make room for
         wx_host, wdy_host = _make_inputs(TOKENS, seed=2000 + rank)
         wxs = [x.to(device) for x in wx_host]
         wdys = [d.to(device) for d in wdy_host]
@@ -359,10 +377,16 @@ def run_ours(args):
                 "what": "every rank runs its own 16384-token micro-batch, no gradient reduction (replicas)"}
         del wgraph, wxs, wdys
         torch.cuda.synchronize()
+        if comm_sms:
+            _lib.set_sm_budget(torch.cuda.get_device_properties(device).multi_processor_count - comm_sms)
 
     # ---- end-to-end through the public API with host buffers (e2e) --------------------------
     e2e = _e2e(layers, xs_host, dys_host, step, device, world, args, barrier, max_over_ranks)
     reducing, reduce_bytes = step.reduce, step.reduce_bytes
+    if comm_sms:
+        from radiance_b200 import _lib
+
+        _lib.set_sm_budget(0)
     comparators = None
     if world == 1 and not args.no_subrecords and not args.tokens_per_rank:
         comparators = measure_comparators(layers, xs, dys, device)
@@ -418,6 +442,7 @@ def run_ours(args):
                                 "fp32 dW reduce-scattered (NCCL, overlapped from the wgrad hook) inside the step")
                 if world > 1 and reducing else "one GPU" if world == 1 else f"{world} replicas",
                 "grad_reduce_bytes_per_step": reduce_bytes,
+                "comm_sms": comm_sms,
                 "l2": "inputs larger than L2 (about 1 GB of activations and gradients per 16384 tokens)",
                 "timing": "eager Python step loop" if args.eager else
                           "the step captured in one CUDA graph, replayed K times; per-kernel times from event pairs "
@@ -1667,6 +1692,9 @@ def main():
     ap.add_argument("--tokens-per-rank", type=int, default=0,
                     help="config 3: run this many tokens on every rank instead of sharding the job's 16384 "
                          "(weak scaling; no gradient reduction unless N > 1)")
+    ap.add_argument("--comm-sms", type=int, default=16,
+                    help="config 3, N > 1: SMs left to the gradient reduce-scatter (its communicator's CTA limit; "
+                         "this library's kernels size their grids for the rest)")
     ap.add_argument("--no-subrecords", action="store_true",
                     help="config 3: skip the config 4 and config 5 sub-records of the headline line")
     ap.add_argument("--eager", action="store_true",

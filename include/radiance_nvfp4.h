@@ -55,6 +55,14 @@ const char* rb_nvfp4_last_error(void);
 int rb_nvfp4_abi_version(void);
 
 /*
+ * SM budget of this library's kernels on the current device: their grids are sized for `sms`
+ * streaming multiprocessors (0 = all of them), so that kernels of another stream -- a gradient
+ * reduce-scatter overlapping the backward pass -- find SMs free while ours run.  Returns the previous
+ * budget.  Host-side setting for the launches that follow; no counterpart in the reference.
+ */
+int rb_nvfp4_set_sm_budget(int sms);
+
+/*
  * First non-zero status recorded by any kernel of this library on the current device since the
  * last clear; 0 if none.  Synchronises the device.  Codes: 1-4 a bounded device-side wait ran out
  * (TMA data, MMA completion, accumulator hand-off, free pipeline stage); 5 a grouped-GEMM record

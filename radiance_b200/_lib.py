@@ -23,6 +23,7 @@ SIGNATURES: dict[str, tuple] = {
     "rb_nvfp4_last_error": (ctypes.c_char_p, []),
     "rb_nvfp4_abi_version": (_int, []),
     "rb_nvfp4_device_status": (_int, [_int]),
+    "rb_nvfp4_set_sm_budget": (_int, [_int]),
     "rb_nvfp4_global_scale": (_int, [_c_void_p, _int, _i64, _i64, _i64, _c_void_p, _c_void_p, _c_void_p]),
     "rb_nvfp4_global_scale_noalloc": (_int, [_c_void_p, _int, _i64, _i64, _i64, _c_void_p, _c_void_p]),
     "rb_nvfp4_quantize": (
@@ -128,6 +129,12 @@ def check(rc: int, what: str) -> None:
     if rc != 0:
         msg = _lib.rb_nvfp4_last_error().decode(errors="replace") if _lib is not None else ""
         raise _ERRORS.get(rc, RuntimeError)(f"{what}: {msg}")
+
+
+def set_sm_budget(sms: int) -> int:
+    """Size this library's kernel grids for `sms` SMs of the current device (0 = all); returns the
+    previous budget.  Leaves SMs free for kernels of other streams (an overlapped collective)."""
+    return int(load().rb_nvfp4_set_sm_budget(int(sms)))
 
 
 def device_status(clear: bool = True) -> int:

@@ -161,6 +161,10 @@ namespace rb_host {
 
 void set_error(const char* fmt, ...);
 int num_sms(int device);
+// The SMs this library's kernels size their grids for on `device`: all of them unless the caller
+// set a smaller budget (rb_nvfp4_set_sm_budget), leaving the rest to concurrent kernels.
+int sm_budget(int device);
+int set_sm_budget(int device, int sms);
 int current_device();
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no link-time libcuda).

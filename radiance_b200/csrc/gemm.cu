@@ -1084,7 +1084,7 @@ int launch_two_sm(GemmArgs& g, const CUtensorMap& tmA, const CUtensorMap& tmB, c
                              (uint64_t)(b_rows / 128) * (uint64_t)g.kb_total * 2, 256, 256, 8,
                              CU_TENSOR_MAP_SWIZZLE_NONE))
     return RB_ERR_CUDA;
-  const int sms = rb_host::num_sms(dev);
+  const int sms = rb_host::sm_budget(dev);
   const size_t smem = sizeof(Gemm2Smem) + 1024;
   static int max_clusters[64] = {0};
   cudaLaunchConfig_t cfg = {};
@@ -1112,7 +1112,7 @@ int launch_two_sm(GemmArgs& g, const CUtensorMap& tmA, const CUtensorMap& tmB, c
     }
     max_clusters[dev] = nc;
   }
-  const int cap = (dev >= 0 && dev < 64) ? max_clusters[dev] : sms / 2;
+  const int cap = min((dev >= 0 && dev < 64) ? max_clusters[dev] : sms / 2, sms / 2);
   const int clusters = clusters_wanted < cap ? clusters_wanted : cap;
   if (clusters < 1) return RB_OK;
   cfg.gridDim = dim3(2 * clusters, 1, 1);
@@ -1129,7 +1129,7 @@ int launch_two_sm(GemmArgs& g, const CUtensorMap& tmA, const CUtensorMap& tmB, c
 template <bool kSwiglu>
 int launch_one_sm(const GemmArgs& g, const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmO, int dev,
                   cudaStream_t st) {
-  const int sms = rb_host::num_sms(dev);
+  const int sms = rb_host::sm_budget(dev);
   const size_t smem = sizeof(GemmSmem) + 1024;
   static bool configured[64] = {false};
   if (dev >= 0 && dev < 64 && !configured[dev]) {
@@ -1288,7 +1288,7 @@ static int gemm_impl(const void* a_packed, const void* a_scale, const void* b_pa
   g.k_steps = (g.k_blocks + 3) / 4;
   g.tiles_n = (int)((n + kBN - 1) / kBN);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  const int sms = rb_host::num_sms(dev);
+  const int sms = rb_host::sm_budget(dev);
   const bool two_sm = m >= 256;
   CUtensorMap tmA, tmB, tmO;
   // Output boxes are 32 rows x 128 bytes (64 bf16 or 32 fp32 columns), 128-byte swizzled.

@@ -35,6 +35,21 @@ int num_sms(int device) {
   return cache[device];
 }
 
+static int g_sm_budget[64] = {0};
+
+int sm_budget(int device) {
+  const int n = num_sms(device);
+  if (device < 0 || device >= 64 || g_sm_budget[device] <= 0 || g_sm_budget[device] >= n) return n;
+  return g_sm_budget[device];
+}
+
+int set_sm_budget(int device, int sms) {
+  if (device < 0 || device >= 64) return 0;
+  const int prev = g_sm_budget[device];
+  g_sm_budget[device] = sms < 0 ? 0 : sms;
+  return prev;
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
@@ -116,6 +131,8 @@ extern "C" {
 const char* rb_nvfp4_last_error(void) { return rb_host::g_last_error; }
 
 int rb_nvfp4_abi_version(void) { return RB_NVFP4_ABI_VERSION; }
+
+int rb_nvfp4_set_sm_budget(int sms) { return rb_host::set_sm_budget(rb_host::current_device(), sms); }
 
 int rb_nvfp4_device_status(int clear) {
   uint32_t s = rb_internal_quant_status(clear);

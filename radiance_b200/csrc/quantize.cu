@@ -1338,7 +1338,7 @@ static int launch_quant(const CUtensorMap& tmap, const QuantArgs& a, cudaStream_
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kQThreads, smem) != cudaSuccess || n < 1) n = 1;
     per_sm[dev] = n;
   }
-  const int sms = rb_host::num_sms(dev);
+  const int sms = rb_host::sm_budget(dev);
   const int slots = sms * ((dev >= 0 && dev < 64) ? per_sm[dev] : 1);
   const int grid = a.n_tiles < slots ? a.n_tiles : slots;
   if (a.gsync != nullptr) {
@@ -1420,7 +1420,7 @@ int rb_nvfp4_global_scale(const void* x, int dtype, int64_t rows, int64_t cols, 
   if (rows * cols == 0) {
     rb::fill_float_kernel<<<1, 1, 0, s>>>(gs_out, 1e-12f);
   } else {
-    const int sms = rb_host::num_sms(rb_host::current_device());
+    const int sms = rb_host::sm_budget(rb_host::current_device());
     const int64_t per = (dtype == RB_DTYPE_BF16 ? 8 : 4) * 512 * 4;
     int64_t grid = (rows * cols + per - 1) / per;
     if (grid > 4 * sms) grid = 4 * sms;
@@ -1457,7 +1457,7 @@ int rb_nvfp4_update_global_scale(void* w, int w_dtype, const void* u, int u_dtyp
   if (n == 0) {
     rb::fill_float_kernel<<<1, 1, 0, s>>>(gs_out, 1e-12f);
   } else {
-    const int sms = rb_host::num_sms(rb_host::current_device());
+    const int sms = rb_host::sm_budget(rb_host::current_device());
     int64_t grid = (n + 4 * 512 - 1) / (4 * 512);
     if (grid > 8 * sms) grid = 8 * sms;
     uint32_t* ws = reinterpret_cast<uint32_t*>(workspace);
@@ -1582,7 +1582,7 @@ int rb_nvfp4_quantize_grouped(const void* x, int dtype, int64_t rows, int64_t co
 // Row splits of global_scale_colsum_kernel for a launch of `gx` column chunks: enough blocks to
 // fill the GPU four times over, and at most one per row.
 static int64_t colsum_parts(int64_t rows, int64_t gx) {
-  const int64_t want = (4 * (int64_t)rb_host::num_sms(rb_host::current_device()) + gx - 1) / gx;
+  const int64_t want = (4 * (int64_t)rb_host::sm_budget(rb_host::current_device()) + gx - 1) / gx;
   return max((int64_t)1, min(rows, want));
 }
 
@@ -1665,7 +1665,7 @@ int rb_nvfp4_global_scale_grouped(const void* x, int dtype, int64_t rows, int64_
     return RB_ERR_DEVICE;
   }
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  const int sms = rb_host::num_sms(rb_host::current_device());
+  const int sms = rb_host::sm_budget(rb_host::current_device());
   const int64_t per = (int64_t)(16 / esize) * 256 * 8;  // ~8 loads per thread
   int64_t grid = (rows * cols + per - 1) / per;
   if (grid > 4 * sms) grid = 4 * sms;
@@ -1692,7 +1692,7 @@ int rb_nvfp4_selftest_division(const float* x, const float* d, int64_t n, uint32
     rb_host::set_error("nvfp4 selftest_division: the current device is not an sm_100 GPU");
     return RB_ERR_DEVICE;
   }
-  const int sms = rb_host::num_sms(rb_host::current_device());
+  const int sms = rb_host::sm_budget(rb_host::current_device());
   rb::selftest_division_kernel<<<4 * sms, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(x, d, n, mismatches);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
@@ -1734,7 +1734,7 @@ int rb_nvfp4_selftest_scale(const float* amax, int64_t n, const float* gs, uint3
     rb_host::set_error("nvfp4 selftest_scale: the current device is not an sm_100 GPU");
     return RB_ERR_DEVICE;
   }
-  const int sms = rb_host::num_sms(rb_host::current_device());
+  const int sms = rb_host::sm_budget(rb_host::current_device());
   rb::selftest_scale_kernel<<<2 * sms, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(amax, n, gs, mismatches);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {

@@ -65,7 +65,8 @@ def _worker(rank, world, port, results):
         cx, cw = cos(gx1, gx2), cos(gw1[sl], gw2)
         # The fused path: the slice's GEMM writes every rank's copy of the output over NVLink, into
         # IPC-shared plain device buffers (no multicast object).
-        fused = FP4ColumnParallelLinear(k, n, recipe=recipe, device="cuda", fused_gather=True)
+        # Three output buffers: y3 stays alive while the two accumulation forwards below run.
+        fused = FP4ColumnParallelLinear(k, n, recipe=recipe, device="cuda", fused_gather=True, output_buffers=3)
         fused.load_full_weight(w)
         fused.refresh_fp4_cache()
         x3 = x.clone().requires_grad_(True)
