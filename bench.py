@@ -39,6 +39,9 @@ LAYERS = [("qkv", 2048, 6144), ("o", 2048, 2048), ("gate_up", 2048, 11264), ("do
 LAYER_KN = sum(k * n for _, k, n in LAYERS)
 STEP_FLOPS = 6.0 * TOKENS * LAYER_KN  # 5.051e12 per step of the job
 METRIC = "NVFP4 linear fwd+bwd TFLOPS (BASELINE config 3 block linears, 16384 tokens per step, token-sharded)"
+# SMs left to the dW reduce-scatter per world size (measured best of 0/8/16/24/32 at N=2 and 0/16/32 at
+# N=8: the collective's share of the step grows with N while each rank's GEMM work shrinks).
+COMM_SMS_DEFAULT = {2: 16, 4: 24, 8: 32}
 
 # Average DRAM bytes (read + write) per GEMM launch of this workload's twelve GEMMs, from one `ncu`
 # capture (profiles/gemm_block_step_traffic.md).
@@ -138,64 +141,96 @@ def _dist_setup(args):
     return rank, world, local
 
 
-def _make_layers(device):
-    """The block's four linears, identical on every rank (data-parallel replicas of one model)."""
-    import torch
+class Block:
+    """The block's NVFP4 layers, identical on every rank (data-parallel replicas of one model).
 
-    from radiance_b200 import nvfp4 as nv
+    ``ffn=True`` (the headline): QKV and O as ``FP4Linear``, and the FFN as radiance's FeedForward
+    (``down_proj(F.silu(gate_proj(x)) * up_proj(x))``, src/radiance/model/ffn.py:32) built as
+    ``FP4FeedForward``: the gate/up GEMM writes h = silu(g) * u and h's global scale in its epilogue,
+    and down_proj quantizes h with that scale.  ``ffn=False``: the four linears on independent inputs.
+    Either way the linears are BASELINE config 3's (QKV 2048->6144, O 2048->2048, gate/up
+    2048->11264, down 5632->2048) and the GEMM work per token is the same.
+    ``units``: (name, module, in_features, out_features, FP4Linear modules holding weights)."""
 
-    g = torch.Generator(device="cpu").manual_seed(1234)
-    layers = []
-    for name, k, n in LAYERS:
-        lin = nv.FP4Linear(k, n, bias=False, recipe=nv.FP4Recipe())
-        with torch.no_grad():
-            lin.weight.copy_(torch.randn(n, k, generator=g) * 0.02)
-        lin = lin.to(device)
-        lin.refresh_fp4_cache()
-        layers.append(lin)
-    return layers
+    def __init__(self, device, ffn=True):
+        import torch
 
+        from radiance_b200 import nvfp4 as nv
 
-def _make_inputs(tokens, seed):
-    """This rank's token shard: activations ~N(0,1) and upstream gradients ~N(0,1e-3), bf16, on the host."""
-    import torch
+        g = torch.Generator(device="cpu").manual_seed(1234)
+        rec = nv.FP4Recipe()
 
-    g = torch.Generator(device="cpu").manual_seed(seed)
-    xs, dys = [], []
-    for name, k, n in LAYERS:
-        xs.append(torch.randn(tokens, k, generator=g).to(torch.bfloat16))
-        dys.append((torch.randn(tokens, n, generator=g) * 1e-3).to(torch.bfloat16))
-    return xs, dys
+        def linear(k, n):
+            lin = nv.FP4Linear(k, n, bias=False, recipe=rec)
+            with torch.no_grad():
+                lin.weight.copy_(torch.randn(n, k, generator=g) * 0.02)
+            return lin.to(device)
+
+        self.ffn = ffn
+        self.units = []
+        names = LAYERS if not ffn else LAYERS[:2]
+        for name, k, n in names:
+            lin = linear(k, n)
+            self.units.append((name, lin, k, n, [lin]))
+        if ffn:
+            d, hid = LAYERS[2][1], LAYERS[3][1]
+            mod = nv.FP4FeedForward(d, hid, bias=False, recipe=rec)
+            with torch.no_grad():
+                mod.gate_up.weight.copy_(torch.randn(2 * hid, d, generator=g) * 0.02)
+                mod.down_proj.weight.copy_(torch.randn(d, hid, generator=g) * 0.02)
+            mod = mod.to(device)
+            self.units.append(("ffn", mod, d, d, [mod.gate_up, mod.down_proj]))
+        for unit in self.units:
+            for lin in unit[4]:
+                lin.refresh_fp4_cache()
+
+    def linears(self):
+        return [lin for unit in self.units for lin in unit[4]]
+
+    def inputs(self, tokens, seed):
+        """This rank's token shard: activations ~N(0,1) and upstream gradients ~N(0,1e-3), bf16, on
+        the host."""
+        import torch
+
+        g = torch.Generator(device="cpu").manual_seed(seed)
+        xs, dys = [], []
+        for _, _, k, n, _ in self.units:
+            xs.append(torch.randn(tokens, k, generator=g).to(torch.bfloat16))
+            dys.append((torch.randn(tokens, n, generator=g) * 1e-3).to(torch.bfloat16))
+        return xs, dys
 
 
 class BlockStep:
-    """One training step of the block's linears on this rank's token shard: the four forwards, then
-    the four backwards in reverse order (as a block's backward runs).  With several ranks, each
-    linear's fp32 dW is reduce-scattered over the ranks (ZeRO-style: rank r keeps the summed rows
-    r*N/g .. (r+1)*N/g) on a side stream, issued from the layer's wgrad hook the moment its wgrad GEMM
-    has produced dW, so the reduction overlaps that layer's dgrad and the layers still to come."""
+    """One training step of the block on this rank's token shard: the forwards, then the backwards
+    in reverse order (as a block's backward runs).  With several ranks, each linear's fp32 dW is
+    reduce-scattered over the ranks (ZeRO-style: rank r keeps the summed rows r*N/g .. (r+1)*N/g) on
+    a side stream, issued from the layer's wgrad hook the moment its wgrad GEMM has produced dW, so
+    the reduction overlaps that layer's dgrad and the layers still to come."""
 
-    def __init__(self, layers, world, device, reduce=True, group=None):
+    def __init__(self, block, world, device, reduce=True, group=None):
         import torch
 
-        self.layers, self.world, self.group = layers, world, group
+        self.block, self.world, self.group = block, world, group
         self.reduce = reduce and world > 1
         self.side = torch.cuda.Stream(device)
-        self.shards = [torch.empty(lin.out_features // world, lin.in_features, device=device) for lin in layers]
-        self.reduce_bytes = sum(lin.weight.numel() * 4 for lin in layers) if self.reduce else 0
+        lins = block.linears()
+        self.shards = {id(lin): torch.empty(lin.out_features // world, lin.in_features, device=device) for lin in lins}
+        self.reduce_bytes = sum(lin.weight.numel() * 4 for lin in lins) if self.reduce else 0
         self._pending = []
 
-    def _hook(self, i):
+    def _hook(self, lin):
         import torch
         import torch.distributed as dist
 
         from radiance_b200.nvfp4 import _trace
 
+        shard = self.shards[id(lin)]
+
         def hook(grad_w):
             self.side.wait_stream(torch.cuda.current_stream())
             with torch.cuda.stream(self.side):
                 tok = _trace.begin("reduce_scatter", grad_w.numel() * 4)
-                dist.reduce_scatter_tensor(self.shards[i], grad_w, group=self.group)
+                dist.reduce_scatter_tensor(shard, grad_w, group=self.group)
                 _trace.end(tok)
             self._pending.append(grad_w)  # keeps dW alive until the side stream has consumed it
         return hook
@@ -203,22 +238,25 @@ class BlockStep:
     def __call__(self, xs, dys, outs=None):
         import torch
 
+        lins = self.block.linears()
         if self.reduce:
-            for i, lin in enumerate(self.layers):
-                lin.wgrad_hook = self._hook(i)
+            for lin in lins:
+                lin.wgrad_hook = self._hook(lin)
         ins, ys = [], []
-        for i, lin in enumerate(self.layers):
+        for i, unit in enumerate(self.block.units):
             x = xs[i].detach().requires_grad_(True)
             ins.append(x)
-            ys.append(lin(x))
-        for i in reversed(range(len(self.layers))):
-            gx, gw = torch.autograd.grad(ys[i], (ins[i], self.layers[i].weight), dys[i])
+            ys.append(unit[1](x))
+        for i in reversed(range(len(self.block.units))):
+            params = [lin.weight for lin in self.block.units[i][4]]
+            grads = torch.autograd.grad(ys[i], (ins[i], *params), dys[i])
             if outs is not None:
-                outs.append((i, gx, self.shards[i] if self.reduce else gw))
+                dws = [self.shards[id(lin)] for lin in self.block.units[i][4]] if self.reduce else list(grads[1:])
+                outs.append((i, grads[0], dws))
         if self.reduce:
             torch.cuda.current_stream().wait_stream(self.side)
             self._pending.clear()
-            for lin in self.layers:
+            for lin in lins:
                 lin.wgrad_hook = None
 
 
@@ -305,8 +343,8 @@ def run_ours(args):
             raise SystemExit(f"{TOKENS} tokens do not shard into multiples of 128 over {world} ranks")
         tokens, scaling = TOKENS // world, "strong"
     step_flops = 6.0 * tokens * LAYER_KN  # this rank's GEMM work per step
-    layers = _make_layers(device)
-    xs_host, dys_host = _make_inputs(tokens, seed=1000 + rank)
+    block = Block(device, ffn=not args.linears_only)
+    xs_host, dys_host = block.inputs(tokens, seed=1000 + rank)
     xs = [x.to(device) for x in xs_host]
     dys = [d.to(device) for d in dys_host]
     rs_group = None
@@ -317,14 +355,14 @@ def run_ours(args):
         # and quantizers instead of waiting for SMs between them.
         from radiance_b200 import _lib
 
-        comm_sms = max(0, args.comm_sms)
+        comm_sms = max(0, args.comm_sms) if args.comm_sms >= 0 else COMM_SMS_DEFAULT.get(world, 32)
         opts = dist.ProcessGroupNCCL.Options()
         if comm_sms:
             opts.config.max_ctas = comm_sms
             opts.config.min_ctas = min(comm_sms, 4)
             _lib.set_sm_budget(torch.cuda.get_device_properties(device).multi_processor_count - comm_sms)
         rs_group = dist.new_group(ranks=list(range(world)), backend="nccl", pg_options=opts)
-    step = BlockStep(layers, world, device, group=rs_group)
+    step = BlockStep(block, world, device, group=rs_group)
 
     def barrier():
         if world > 1:
@@ -357,16 +395,33 @@ def run_ours(args):
     per_kind, launches_per_step = _graph_kernel_times(lambda: step(xs, dys), replays=max(3, min(args.steps, 20)))
     del graph, run_step
 
+    # ---- the same shard without the gradient reduction (N > 1): fwd + dgrad + wgrad on 16384/N
+    # tokens per rank and nothing else -- token sharding as a pure partition ("Token (M) rows shard
+    # with no communication"); the difference to `value` is the reduce-scatter's exposed time.
+    no_reduce = None
+    if world > 1:
+        nstep = BlockStep(block, world, device, reduce=False)
+        for _ in range(3):
+            nstep(xs, dys)
+        ngraph = _capture(lambda: nstep(xs, dys))
+        nms, _ = _timed_replays(ngraph.replay, args.steps, barrier)
+        nms_max = max_over_ranks(nms) / args.steps
+        no_reduce = {"value": round(step_flops * world / (nms_max * 1e-3) / 1e12, 2), "unit": "TFLOPS",
+                     "ms_per_step": round(nms_max, 4), "tokens_per_gpu": tokens, "scaling": scaling,
+                     "what": "the same token-sharded step without the dW reduce-scatter"}
+        del ngraph, nstep
+        torch.cuda.synchronize()
+
     # ---- weak-scaled replicas (N > 1): every rank a whole 16384-token micro-batch, no collective
     weak = None
     if world > 1 and not args.tokens_per_rank:
         from radiance_b200 import _lib
 
         _lib.set_sm_budget(0)  # replicas have no collective to make room for
-        wx_host, wdy_host = _make_inputs(TOKENS, seed=2000 + rank)
+        wx_host, wdy_host = block.inputs(TOKENS, seed=2000 + rank)
         wxs = [x.to(device) for x in wx_host]
         wdys = [d.to(device) for d in wdy_host]
-        wstep = BlockStep(layers, world, device, reduce=False)
+        wstep = BlockStep(block, world, device, reduce=False)
         for _ in range(3):
             wstep(wxs, wdys)
         wgraph = _capture(lambda: wstep(wxs, wdys))
@@ -381,7 +436,7 @@ def run_ours(args):
             _lib.set_sm_budget(torch.cuda.get_device_properties(device).multi_processor_count - comm_sms)
 
     # ---- end-to-end through the public API with host buffers (e2e) --------------------------
-    e2e = _e2e(layers, xs_host, dys_host, step, device, world, args, barrier, max_over_ranks)
+    e2e = _e2e(block, xs_host, dys_host, step, device, world, args, barrier, max_over_ranks)
     reducing, reduce_bytes = step.reduce, step.reduce_bytes
     if comm_sms:
         from radiance_b200 import _lib
@@ -389,7 +444,7 @@ def run_ours(args):
         _lib.set_sm_budget(0)
     comparators = None
     if world == 1 and not args.no_subrecords and not args.tokens_per_rank:
-        comparators = measure_comparators(layers, xs, dys, device)
+        comparators = measure_comparators(block, xs, dys, device)
     del xs, dys, step
 
     # ---- configs 4 and 5 as sub-records (with their parity checks at N > 1) --------------------
@@ -432,7 +487,10 @@ def run_ours(args):
             "dtype": "nvfp4 (e2m1 x e4m3 block scales, fp32 accumulate; bf16 in/out, fp32 dW)",
             "data": "synthetic (seeded; W~N(0,0.02), X~N(0,1), dY~N(0,1e-3))",
             "config": {
-                "workload": "config3: dense block linears fwd+dgrad+wgrad via FP4Linear",
+                "workload": ("config3: dense block linears fwd+dgrad+wgrad; QKV and O via FP4Linear, the FFN (gate/up "
+                             "-> SwiGLU -> down) via FP4FeedForward (SwiGLU and h's global scale in the gate/up GEMM's "
+                             "epilogue)") if block.ffn else "config3: the four block linears fwd+dgrad+wgrad via FP4Linear "
+                                                            "on independent inputs",
                 "d_model": D_MODEL,
                 "layers": {n: [k, o] for n, k, o in LAYERS},
                 "global_batch_tokens": tokens * world,
@@ -492,6 +550,8 @@ def run_ours(args):
                 "calls_per_step": rs["launches"], "ms_per_step": round(rs["ms"], 4),
                 "GBps_algbw": round(rs["work"] / (rs["ms"] * 1e-3) / 1e9, 1) if rs["ms"] else None,
                 "note": "NCCL on a side stream, overlapped with the GEMMs; its time is not additive"}
+        if no_reduce is not None:
+            line["without_grad_reduction"] = no_reduce
         if weak is not None:
             line["weak_replicas"] = weak
         if comparators is not None:
@@ -509,21 +569,24 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
-def _e2e(layers, xs_host, dys_host, step, device, world, args, barrier, max_over_ranks):
+def _e2e(block, xs_host, dys_host, step, device, world, args, barrier, max_over_ranks):
     """The same step through the public API with host buffers: every step copies its inputs from
-    pinned host memory and copies its results (dX of every linear, and this rank's dW rows -- the
-    reduce-scattered shard with several ranks) back to pinned host memory, inside the timed region.
-    Step s+1's uploads run on a copy stream during step s (double-buffered inputs, the way a data
-    loader feeds a training loop), and step s's downloads on another while step s+1 computes."""
+    pinned host memory and copies its results (every input gradient, and this rank's weight-gradient
+    rows -- the reduce-scattered shards with several ranks) back to pinned host memory, inside the
+    timed region.  Step s+1's uploads run on a copy stream during step s (double-buffered inputs,
+    the way a data loader feeds a training loop), and step s's downloads on another while step s+1
+    computes."""
     import torch
 
     pinned_x = [x.pin_memory() for x in xs_host]
     pinned_dy = [d.pin_memory() for d in dys_host]
     tokens = xs_host[0].shape[0]
-    out_dx = [torch.empty(tokens, k, dtype=torch.bfloat16).pin_memory() for _, k, _ in LAYERS]
-    out_dw = [torch.empty(n // world if step.reduce else n, k, dtype=torch.float32).pin_memory() for _, k, n in LAYERS]
+    out_dx = [torch.empty(tokens, unit[2], dtype=torch.bfloat16).pin_memory() for unit in block.units]
+    out_dw = [[torch.empty(lin.out_features // world if step.reduce else lin.out_features, lin.in_features,
+                           dtype=torch.float32).pin_memory() for lin in unit[4]] for unit in block.units]
     h2d = sum(t.numel() * t.element_size() for t in pinned_x + pinned_dy)
-    d2h = sum(t.numel() * t.element_size() for t in out_dx + out_dw)
+    d2h = sum(t.numel() * t.element_size() for t in out_dx) + sum(t.numel() * 4 for ws in out_dw for t in ws)
+    n_in = len(block.units)
     dev_sets = [([torch.empty_like(x, device=device) for x in xs_host],
                  [torch.empty_like(d, device=device) for d in dys_host]) for _ in range(2)]
     up, down = torch.cuda.Stream(device), torch.cuda.Stream(device)
@@ -535,7 +598,7 @@ def _e2e(layers, xs_host, dys_host, step, device, world, args, barrier, max_over
         with torch.cuda.stream(up):
             if used[b]:
                 up.wait_event(consumed[b])
-            for i in range(len(LAYERS)):
+            for i in range(n_in):
                 dev_sets[b][0][i].copy_(pinned_x[i], non_blocking=True)
                 dev_sets[b][1][i].copy_(pinned_dy[i], non_blocking=True)
             copied[b].record(up)
@@ -556,11 +619,12 @@ def _e2e(layers, xs_host, dys_host, step, device, world, args, barrier, max_over
             used[b] = True
             down.wait_stream(cur)
             with torch.cuda.stream(down):
-                for i, gx, gw in outs:
+                for i, gx, gws in outs:
                     out_dx[i].copy_(gx, non_blocking=True)
-                    out_dw[i].copy_(gw, non_blocking=True)
                     gx.record_stream(down)
-                    gw.record_stream(down)
+                    for j, gw in enumerate(gws):
+                        out_dw[i][j].copy_(gw, non_blocking=True)
+                        gw.record_stream(down)
         cur.wait_stream(down)
 
     e2e_steps = max(3, min(args.steps, 20))
@@ -627,7 +691,7 @@ def _graph_ms(fn, reps=5, warm=3):
     return best, mode
 
 
-def measure_comparators(layers, xs, dys, device):
+def measure_comparators(block, xs, dys, device):
     """One GPU, the config-3 shapes: (1) the reference's own GPU path -- radiance's FP4Linear
     (Triton quantizers, torch._scaled_mm_v2 GEMMs) from baseline/_ref -- on the same block step, and
     (2) the step's twelve GEMMs through cuBLASLt's NVFP4 GEMM (torch._scaled_mm_v2, the GEMM radiance
@@ -678,39 +742,59 @@ def measure_comparators(layers, xs, dys, device):
         del calls
     except Exception as e:
         out["gemms_vs_cublaslt"] = {"error": f"{type(e).__name__}: {e}"[:300]}
-    # (1) the reference's own FP4Linear on the same block step
+    # (1) the reference's own layers on the same block step: radiance's FP4Linear for QKV and O, and
+    # its FeedForward for the FFN (gate_proj and up_proj as separate FP4Linears, F.silu(g) * u in
+    # torch, down_proj), ffn.py:21-36
     rnv, why = _import_reference()
     if rnv is None:
         out["reference_gpu_step"] = {"unavailable": why}
         return out
     try:
-        ref_layers = []
-        for lin in layers:
-            r = rnv.FP4Linear(lin.in_features, lin.out_features, bias=False)
+        import torch.nn.functional as F
+
+        from radiance_b200.nvfp4 import split_gate_up
+
+        def ref_linear(weight):
+            r = rnv.FP4Linear(weight.shape[1], weight.shape[0], bias=False)
             with torch.no_grad():
-                r.weight.copy_(lin.weight.detach().cpu())
+                r.weight.copy_(weight.detach().cpu())
             r = r.to(device)
             r.refresh_fp4_cache()
-            ref_layers.append(r)
+            return r
+
+        units = []
+        for name, mod, k, n, lins in block.units:
+            if name == "ffn":
+                g_t, u_t = split_gate_up(mod.gate_up.weight.detach().t())
+                gate, up = ref_linear(g_t.t().contiguous()), ref_linear(u_t.t().contiguous())
+                down = ref_linear(mod.down_proj.weight)
+
+                def ffn(x, gate=gate, up=up, down=down):
+                    return down(F.silu(gate(x)) * up(x))
+                units.append((ffn, [gate.weight, up.weight, down.weight]))
+            else:
+                r = ref_linear(mod.weight)
+                units.append((r, [r.weight]))
 
         def ref_step():
             ins, ys = [], []
-            for i, r in enumerate(ref_layers):
+            for i, (fn, _) in enumerate(units):
                 x = xs[i].detach().requires_grad_(True)
                 ins.append(x)
-                ys.append(r(x))
-            for i in reversed(range(len(ref_layers))):
-                torch.autograd.grad(ys[i], (ins[i], ref_layers[i].weight), dys[i])
+                ys.append(fn(x))
+            for i in reversed(range(len(units))):
+                torch.autograd.grad(ys[i], (ins[i], *units[i][1]), dys[i])
 
         ms_r, mode = _graph_ms(ref_step)
         flops = 6.0 * tokens * LAYER_KN
         out["reference_gpu_step"] = {
             "value": round(flops / (ms_r * 1e-3) / 1e12, 2), "unit": "TFLOPS", "ms_per_step": round(ms_r, 4),
             "timing": mode,
-            "what": "radiance's own FP4Linear (src/radiance/nvfp4: Triton quantizers + torch._scaled_mm_v2), installed "
-                    "unmodified under baseline/_ref, on the same block step (same weights, inputs and recipe)",
+            "what": "radiance's own layers (src/radiance/nvfp4: Triton quantizers + torch._scaled_mm_v2; its FeedForward "
+                    "with separate gate/up projections and torch SwiGLU), installed unmodified under baseline/_ref, on the "
+                    "same block step (same weights, inputs and recipe)",
         }
-        del ref_layers
+        del units
     except Exception as e:
         out["reference_gpu_step"] = {"error": f"{type(e).__name__}: {e}"[:300]}
     return out
@@ -1489,6 +1573,7 @@ cudaProfilerStart/Stop (so `ncu --profile-from-start off` captures only those la
                writes h and its global scale) | unfused (GEMM, torch F.silu(g) * u, amax); each then
                quantizes h both ways
   block-gemms  the twelve GEMMs of one config-3 block step (four linears x fwd, dgrad, wgrad): --tokens
+  block-step   one whole config-3 block step (QKV, O, fused FFN; forward then backward): --tokens
 
 Inputs are seeded synthetic tensors (activations ~N(0, 1), weights ~N(0, 0.02)); a timed case reuses
 its inputs every iteration."""
@@ -1621,12 +1706,24 @@ def _case_block_gemms(args, dev):
     return run, {"work": 6.0 * tokens * LAYER_KN, "unit": "TFLOP/s", "basis": "6*T*sum(K*N) over the four linears"}
 
 
+def _case_block_step(args, dev):
+    """One config-3 block step (QKV, O, the fused FFN; forward then backward) on --tokens tokens,
+    one GPU, no collective."""
+    block = Block(dev, ffn=True)
+    xs_host, dys_host = block.inputs(args.tokens, seed=1000)
+    xs = [x.to(dev) for x in xs_host]
+    dys = [d.to(dev) for d in dys_host]
+    step = BlockStep(block, 1, dev)
+    return (lambda: step(xs, dys)), {"work": 6.0 * args.tokens * LAYER_KN, "unit": "TFLOP/s",
+                                     "basis": "6*T*sum(K*N) over the block's four linears"}
+
+
 def run_case(argv):
     import torch
 
     ap = argparse.ArgumentParser(prog="bench.py case", description=CASES_DOC,
                                  formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("name", choices=["quant", "gemm", "swiglu", "block-gemms"])
+    ap.add_argument("name", choices=["quant", "gemm", "swiglu", "block-gemms", "block-step"])
     ap.add_argument("--rows", type=int, default=16384)
     ap.add_argument("--cols", type=int, default=6144)
     ap.add_argument("--form", choices=["row", "col", "both"], default="both")
@@ -1647,7 +1744,7 @@ def run_case(argv):
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     run, info = {"quant": _case_quant, "gemm": _case_gemm, "swiglu": _case_swiglu,
-                 "block-gemms": _case_block_gemms}[args.name](args, dev)
+                 "block-gemms": _case_block_gemms, "block-step": _case_block_step}[args.name](args, dev)
     if not args.time:
         torch.cuda.synchronize()
         torch.cuda.profiler.start()
@@ -1692,9 +1789,12 @@ def main():
     ap.add_argument("--tokens-per-rank", type=int, default=0,
                     help="config 3: run this many tokens on every rank instead of sharding the job's 16384 "
                          "(weak scaling; no gradient reduction unless N > 1)")
-    ap.add_argument("--comm-sms", type=int, default=16,
+    ap.add_argument("--comm-sms", type=int, default=-1,
                     help="config 3, N > 1: SMs left to the gradient reduce-scatter (its communicator's CTA limit; "
-                         "this library's kernels size their grids for the rest)")
+                         "this library's kernels size their grids for the rest); default by N: "
+                         "16 at N=2, 24 at N=4, 32 at N=8")
+    ap.add_argument("--linears-only", action="store_true",
+                    help="config 3: the four linears on independent inputs instead of QKV, O and the fused FFN")
     ap.add_argument("--no-subrecords", action="store_true",
                     help="config 3: skip the config 4 and config 5 sub-records of the headline line")
     ap.add_argument("--eager", action="store_true",
