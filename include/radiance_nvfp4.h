@@ -237,6 +237,23 @@ int rb_nvfp4_gemm_swiglu(const void* a_packed, const void* a_scale, const void* 
                          float* h_global_scale, void* stream);
 
 /*
+ * The backward of the SwiGLU producer (h = F.silu(g) * u, src/radiance/model/ffn.py:32) in one pass:
+ *   grad_gu[r, 64c + j]      = bf16(silu_backward(bf16(grad_h * u), g))   (the gate half)
+ *   grad_gu[r, 64c + 32 + j] = bf16(grad_h * bf16(silu(g)))               (the up half)
+ * for g = gu[r, 64c + j], u = gu[r, 64c + 32 + j], grad_h = grad_h[r, 32c + j] -- the interleaved
+ * layout of rb_nvfp4_gemm_swiglu -- with the roundings of the eager torch ops autograd runs for that
+ * line (silu(g) = g / (1 + exp(-g)), silu_backward(dy, g) = dy * s * (1 + g * (1 - s)),
+ * s = 1 / (1 + exp(-g)), each evaluated in fp32 from bf16 inputs and rounded to bf16), and
+ * *gs_out = the global scale of grad_gu (quantize.py:205-213), the gate/up linear's next input.
+ *   grad_h : rows x hidden bf16, row stride ldgh;  gu, grad_gu: rows x 2*hidden bf16, strides ldgu,
+ *            ldgg.  hidden % 32 == 0, 16-byte aligned tensors, strides multiples of 8 elements.
+ *   workspace : the 8-byte workspace of rb_nvfp4_global_scale.
+ */
+int rb_nvfp4_swiglu_backward(const void* grad_h, int64_t ldgh, const void* gu, int64_t ldgu, int64_t rows,
+                             int64_t hidden, void* grad_gu, int64_t ldgg, float* gs_out, void* workspace,
+                             void* stream);
+
+/*
  * Test aid: the SwiGLU epilogue takes silu(g), rounded to bf16, from a table and three closed forms
  * instead of evaluating g / (1 + exp(-g)) per element; this checks that mapping on all 65536 bf16
  * bit patterns g against bf16 of the IEEE evaluation.  mismatches: 2 device uint32 (zeroed by the

@@ -73,6 +73,9 @@ SIGNATURES: dict[str, tuple] = {
     "rb_nvfp4_selftest_division": (_int, [_c_void_p, _c_void_p, _i64, _c_void_p, _c_void_p]),
     "rb_nvfp4_selftest_scale": (_int, [_c_void_p, _i64, _c_void_p, _c_void_p, _c_void_p]),
     "rb_nvfp4_selftest_silu": (_int, [_c_void_p, _c_void_p]),
+    "rb_nvfp4_swiglu_backward": (
+        _int, [_c_void_p, _i64, _c_void_p, _i64, _i64, _i64, _c_void_p, _i64, _c_void_p, _c_void_p, _c_void_p],
+    ),
     "rb_nvfp4_selftest_wait_timeout": (_int, [_int, ctypes.c_longlong, _c_void_p, _c_void_p]),
     "rb_peer_alloc": (_int, [ctypes.c_size_t, ctypes.POINTER(_c_void_p)]),
     "rb_peer_free": (_int, [_c_void_p]),

@@ -41,6 +41,7 @@ from .quantize import (
     interleave_gate_up,
     merge_gate_up,
     split_gate_up,
+    swiglu_backward,
     swiglu_mm,
     update_and_global_scale_,
 )
@@ -107,10 +108,12 @@ class _FP4LinearFn(torch.autograd.Function):
         fp4_backward = recipe.grad_gemms and quantize_supported_shape(*grad_y.shape)
         if fp4_backward:
             rot = hadamard if recipe.hadamard and hadamard.numel() else None
-            gg = None  # by default the quantizer computes dY's global scale in the same launch
+            # dY's global scale: from its producer when that computed it (the SwiGLU backward), else
+            # computed by the quantizer in the same launch.
+            gg = getattr(ctx, "grad_global_scale", None)
             if ctx.has_bias:  # the bias gradient's column sums come from the same read of dY
                 gg, colsum = global_scale_and_column_sums(grad_y)
-            elif ctx.reduce_grad_scale is not None:
+            elif ctx.reduce_grad_scale is not None and gg is None:
                 gg = global_scale_of(grad_y)
             if ctx.reduce_grad_scale is not None:  # e.g. the full gradient's scale for an N-split slice
                 ctx.reduce_grad_scale(gg)
@@ -250,24 +253,14 @@ class FP4Linear(nn.Linear):
         return y.view(*x.shape[:-1], self.out_features)
 
 
-def _swiglu_backward(grad_h: torch.Tensor, gu: torch.Tensor) -> torch.Tensor:
-    """Gradient of ``F.silu(g) * u`` with respect to the interleaved pre-activations, computed with
-    the same torch kernels (and roundings) eager autograd runs for ffn.py:32: the product's
-    backward (grad * u, grad * silu(g)) and ``silu_backward``."""
-    g, u = split_gate_up(gu)
-    grad_h = grad_h.reshape(g.shape)
-    grad_u = grad_h * F.silu(g)
-    grad_g = torch.ops.aten.silu_backward(grad_h * u, g)
-    return merge_gate_up(grad_g, grad_u)
-
-
 class _FP4SwiGLUFn(torch.autograd.Function):
     """``h = F.silu(x Wg^T + bg) * (x Wu^T + bu)`` with the gate/up GEMM in NVFP4 and the activation
     and h's global scale computed in the GEMM's epilogue.  Same inputs as ``_FP4LinearFn``; the
     weight is the interleaved gate/up matrix.  Returns ``(h, global_scale(h))``.
 
     Forward and the gate/up weight/input gradients are ``_FP4LinearFn``'s, with the output GEMM
-    replaced by ``swiglu_mm``; the pre-activations are kept for the SwiGLU backward.
+    replaced by ``swiglu_mm``; the pre-activations are kept for the SwiGLU backward, which runs as one
+    kernel (``swiglu_backward``) that also hands the gate/up backward its gradient's global scale.
     """
 
     @staticmethod
@@ -290,7 +283,8 @@ class _FP4SwiGLUFn(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, grad_h, _grad_gs):
-        grad_gu = _swiglu_backward(grad_h, ctx.gu)
+        # One kernel: the SwiGLU derivative (eager autograd's roundings) and its global scale.
+        grad_gu, ctx.grad_global_scale = swiglu_backward(grad_h, ctx.gu)
         del ctx.gu
         return _FP4LinearFn.backward(ctx, grad_gu)
 

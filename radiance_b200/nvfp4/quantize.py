@@ -727,6 +727,39 @@ def swiglu_mm(a: NVFP4Tensor, b: NVFP4Tensor, *, bias=None, out: torch.Tensor | 
     return out, h, h_global_scale
 
 
+def swiglu_backward(grad_h: torch.Tensor, gu: torch.Tensor, out: torch.Tensor | None = None,
+                    out_scale: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """The gradient of ``h = F.silu(g) * u`` with respect to the interleaved pre-activations ``gu``
+    (``swiglu_mm``'s layout), and that gradient's global scale, in one kernel.  Bit-identical to
+    eager autograd's ``grad_h * F.silu(g)`` and ``aten.silu_backward(grad_h * u, g)`` (ffn.py:32).
+    Returns ``(grad_gu, global_scale_of(grad_gu))``."""
+    _require_cuda(grad_h, "nvfp4.swiglu_backward")
+    lib = _lib.load()
+    gh = grad_h.reshape(-1, grad_h.shape[-1])
+    if gh.stride(-1) != 1 or gh.data_ptr() % 16 or gh.stride(0) % 8:
+        gh = gh.contiguous()
+    g2 = gu.reshape(-1, gu.shape[-1])
+    if g2.stride(-1) != 1 or g2.data_ptr() % 16 or g2.stride(0) % 8:
+        g2 = g2.contiguous()
+    if gh.dtype != torch.bfloat16 or g2.dtype != torch.bfloat16:
+        raise ValueError("nvfp4.swiglu_backward: bf16 tensors expected")
+    rows, hidden = gh.shape
+    if g2.shape != (rows, 2 * hidden):
+        raise ValueError(f"nvfp4.swiglu_backward: pre-activations {tuple(g2.shape)} vs gradient {tuple(gh.shape)}")
+    if out is None:
+        out = torch.empty(rows, 2 * hidden, dtype=torch.bfloat16, device=gh.device)
+    if out_scale is None:
+        out_scale = torch.empty((), dtype=torch.float32, device=gh.device)
+    _lib.check(
+        lib.rb_nvfp4_swiglu_backward(
+            gh.data_ptr(), gh.stride(0), g2.data_ptr(), g2.stride(0), rows, hidden, out.data_ptr(), out.stride(0),
+            out_scale.data_ptr(), _workspace(gh.device).data_ptr(), _stream_ptr(gh.device),
+        ),
+        "nvfp4.swiglu_backward",
+    )
+    return out, out_scale
+
+
 def mm(a: NVFP4Tensor, b: NVFP4Tensor, *, out_dtype: torch.dtype = torch.bfloat16, bias=None) -> torch.Tensor:
     """``a @ b.T`` with the global scales folded back in (quantize.py:400-409).
 

@@ -196,3 +196,39 @@ def test_feedforward_from_radiance_layers(nv):
         ref_h = F.silu(src.gate_proj(x[:100])) * src.up_proj(x[:100])
         torch.testing.assert_close(h.float(), ref_h.float(), rtol=2e-2, atol=2e-2)
     _status_ok()
+
+
+def _torch_swiglu_backward(nv, grad_h, gu):
+    """Eager autograd's backward of h = F.silu(g) * u (ffn.py:32), on the interleaved layout."""
+    import torch.nn.functional as F
+
+    g, u = nv.split_gate_up(gu)
+    grad_u = grad_h * F.silu(g)
+    grad_g = torch.ops.aten.silu_backward(grad_h * u, g)
+    return nv.merge_gate_up(grad_g, grad_u)
+
+
+@pytest.mark.parametrize("rows,hidden", [(128, 32), (512, 1408), (2048, 5632)])
+def test_swiglu_backward_matches_eager_autograd(nv, rows, hidden):
+    gen = torch.Generator(device="cuda").manual_seed(rows + hidden)
+    gu = (torch.randn(rows, 2 * hidden, device="cuda", generator=gen) * 3).bfloat16()
+    grad_h = (torch.randn(rows, hidden, device="cuda", generator=gen) * 1e-3).bfloat16()
+    got, gs = nv.swiglu_backward(grad_h, gu)
+    want = _torch_swiglu_backward(nv, grad_h, gu)
+    assert torch.equal(got.view(torch.int16), want.view(torch.int16))
+    assert gs.view(torch.int32).item() == nv.global_scale_of(want).view(torch.int32).item()
+    got2, gs2 = nv.swiglu_backward(grad_h, gu)  # the workspace came back zeroed
+    assert torch.equal(got2, got) and torch.equal(gs2, gs)
+
+
+def test_swiglu_backward_on_every_bf16_gate_value(nv):
+    """Every bf16 bit pattern of g (finite, infinite and NaN), against several gradients and up values."""
+    g = torch.arange(0, 65536, dtype=torch.int32, device="cuda").to(torch.int16).view(torch.bfloat16)
+    for dh_val, u_val in ((1.0, 1.0), (-3.5e-3, 0.75), (1e-30, -2.0), (448.0, 1e-3)):
+        g2 = g.view(-1, 32)  # 2048 rows of one 32-unit group
+        u2 = torch.full_like(g2, u_val)
+        gu = nv.merge_gate_up(g2, u2)
+        grad_h = torch.full_like(g2, dh_val)
+        got, _ = nv.swiglu_backward(grad_h, gu)
+        want = _torch_swiglu_backward(nv, grad_h, gu)
+        assert torch.equal(got.view(torch.int16), want.view(torch.int16)), (dh_val, u_val)
