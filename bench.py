@@ -412,6 +412,25 @@ def run_ours(args):
         del ngraph, nstep
         torch.cuda.synchronize()
 
+    # ---- the four linears alone (N = 1): the same GEMM work on independent inputs, no SwiGLU
+    linears_only = None
+    if world == 1 and block.ffn and not args.no_subrecords:
+        lblock = Block(device, ffn=False)
+        lx_host, ldy_host = lblock.inputs(tokens, seed=3000)
+        lxs = [x.to(device) for x in lx_host]
+        ldys = [d.to(device) for d in ldy_host]
+        lstep = BlockStep(lblock, 1, device, reduce=False)
+        for _ in range(3):
+            lstep(lxs, ldys)
+        lgraph = _capture(lambda: lstep(lxs, ldys))
+        lms, _ = _timed_replays(lgraph.replay, args.steps, barrier)
+        lms /= args.steps
+        linears_only = {"value": round(step_flops / (lms * 1e-3) / 1e12, 2), "unit": "TFLOPS", "ms_per_step": round(lms, 4),
+                        "what": "the four linears fwd+dgrad+wgrad on independent inputs (no SwiGLU between gate/up and "
+                                "down): the same GEMM work as the headline step"}
+        del lgraph, lstep, lxs, ldys, lblock
+        torch.cuda.synchronize()
+
     # ---- weak-scaled replicas (N > 1): every rank a whole 16384-token micro-batch, no collective
     weak = None
     if world > 1 and not args.tokens_per_rank:
@@ -552,6 +571,8 @@ def run_ours(args):
                 "note": "NCCL on a side stream, overlapped with the GEMMs; its time is not additive"}
         if no_reduce is not None:
             line["without_grad_reduction"] = no_reduce
+        if linears_only is not None:
+            line["linears_only"] = linears_only
         if weak is not None:
             line["weak_replicas"] = weak
         if comparators is not None:
