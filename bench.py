@@ -1594,6 +1594,7 @@ cudaProfilerStart/Stop (so `ncu --profile-from-start off` captures only those la
                writes h and its global scale) | unfused (GEMM, torch F.silu(g) * u, amax); each then
                quantizes h both ways
   block-gemms  the twelve GEMMs of one config-3 block step (four linears x fwd, dgrad, wgrad): --tokens
+  swiglu-bwd   the fused SwiGLU backward (grad_gu and its global scale): --m --hidden
   block-step   one whole config-3 block step (QKV, O, fused FFN; forward then backward): --tokens
 
 Inputs are seeded synthetic tensors (activations ~N(0, 1), weights ~N(0, 0.02)); a timed case reuses
@@ -1727,6 +1728,23 @@ def _case_block_gemms(args, dev):
     return run, {"work": 6.0 * tokens * LAYER_KN, "unit": "TFLOP/s", "basis": "6*T*sum(K*N) over the four linears"}
 
 
+def _case_swiglu_bwd(args, dev):
+    """The fused SwiGLU backward of a config-3 FFN: grad_h (--m x --hidden) and the interleaved
+    pre-activations in, grad_gu and its global scale out."""
+    import torch
+
+    from radiance_b200.nvfp4.quantize import swiglu_backward
+
+    g = torch.Generator(device="cpu").manual_seed(19)
+    gu = (torch.randn(args.m, 2 * args.hidden, generator=g) * 2).to(dev, torch.bfloat16)
+    gh = (torch.randn(args.m, args.hidden, generator=g) * 1e-3).to(dev, torch.bfloat16)
+    out = torch.empty_like(gu)
+    gs = torch.empty((), dtype=torch.float32, device=dev)
+    return (lambda: swiglu_backward(gh, gu, out=out, out_scale=gs)), {
+        "work": args.m * args.hidden * 2 * 4.0, "unit": "GB/s",
+        "basis": "8 B per hidden unit: grad_h, g, u read and grad_g, grad_u written, bf16"}
+
+
 def _case_block_step(args, dev):
     """One config-3 block step (QKV, O, the fused FFN; forward then backward) on --tokens tokens,
     one GPU, no collective."""
@@ -1744,7 +1762,7 @@ def run_case(argv):
 
     ap = argparse.ArgumentParser(prog="bench.py case", description=CASES_DOC,
                                  formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("name", choices=["quant", "gemm", "swiglu", "block-gemms", "block-step"])
+    ap.add_argument("name", choices=["quant", "gemm", "swiglu", "swiglu-bwd", "block-gemms", "block-step"])
     ap.add_argument("--rows", type=int, default=16384)
     ap.add_argument("--cols", type=int, default=6144)
     ap.add_argument("--form", choices=["row", "col", "both"], default="both")
@@ -1765,7 +1783,8 @@ def run_case(argv):
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     run, info = {"quant": _case_quant, "gemm": _case_gemm, "swiglu": _case_swiglu,
-                 "block-gemms": _case_block_gemms, "block-step": _case_block_step}[args.name](args, dev)
+                 "swiglu-bwd": _case_swiglu_bwd, "block-gemms": _case_block_gemms,
+                 "block-step": _case_block_step}[args.name](args, dev)
     if not args.time:
         torch.cuda.synchronize()
         torch.cuda.profiler.start()
