@@ -33,32 +33,41 @@ __device__ __forceinline__ void swiglu_grad(float dh, float g, float u, uint32_t
   gg = bf16_bits(t * s * __fmaf_rn(g, 1.0f - s, 1.0f));                  // silu_backward(t, g)
 }
 
+// Thread layout: blockIdx.x and threadIdx.x pick an 8-unit chunk q of the hidden dimension (a chunk
+// never straddles a 32-unit group), blockIdx.y a run of `rows_per_y` rows; a warp's 32 chunks of one
+// row are contiguous in all three tensors.  No index division in the loop.
 __global__ void __launch_bounds__(256) swiglu_backward_kernel(const uint16_t* grad_h, int64_t ldgh, const uint16_t* gu,
                                                               int64_t ldgu, int64_t rows, int64_t hidden,
-                                                              uint16_t* grad_gu, int64_t ldgg, uint32_t* ws,
-                                                              float* gs_out) {
-  const int64_t per_row = hidden / 8;  // 8-unit chunks; a chunk never straddles a 32-unit group
-  const int64_t n = rows * per_row;
+                                                              int64_t rows_per_y, uint16_t* grad_gu, int64_t ldgg,
+                                                              uint32_t* ws, float* gs_out) {
+  const int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t r0 = (int64_t)blockIdx.y * rows_per_y;
+  const int64_t r1 = min(rows, r0 + rows_per_y);
   uint32_t m = 0;  // max of |grad_gu| bf16 bit patterns, two halves packed
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / per_row, q = i - r * per_row;
+  if (q < hidden / 8) {
     const int64_t c = (8 * q) >> 5, j0 = (8 * q) & 31;
-    const uint4 dh = __ldg(reinterpret_cast<const uint4*>(grad_h + r * ldgh + 8 * q));
-    const uint4 gv = __ldg(reinterpret_cast<const uint4*>(gu + r * ldgu + 64 * c + j0));
-    const uint4 uv = __ldg(reinterpret_cast<const uint4*>(gu + r * ldgu + 64 * c + 32 + j0));
-    const uint32_t dw[4] = {dh.x, dh.y, dh.z, dh.w}, gw[4] = {gv.x, gv.y, gv.z, gv.w}, uw[4] = {uv.x, uv.y, uv.z, uv.w};
-    uint32_t og[4], ou[4];
+    const uint16_t* ph = grad_h + r0 * ldgh + 8 * q;
+    const uint16_t* pg = gu + r0 * ldgu + 64 * c + j0;
+    uint16_t* po = grad_gu + r0 * ldgg + 64 * c + j0;
+    for (int64_t r = r0; r < r1; ++r, ph += ldgh, pg += ldgu, po += ldgg) {
+      const uint4 dh = __ldg(reinterpret_cast<const uint4*>(ph));
+      const uint4 gv = __ldg(reinterpret_cast<const uint4*>(pg));
+      const uint4 uv = __ldg(reinterpret_cast<const uint4*>(pg + 32));
+      const uint32_t dw[4] = {dh.x, dh.y, dh.z, dh.w}, gw[4] = {gv.x, gv.y, gv.z, gv.w};
+      const uint32_t uw[4] = {uv.x, uv.y, uv.z, uv.w};
+      uint32_t og[4], ou[4];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      uint32_t g0, u0, g1, u1;
-      swiglu_grad(bf16_lo(dw[k]), bf16_lo(gw[k]), bf16_lo(uw[k]), g0, u0);
-      swiglu_grad(bf16_hi(dw[k]), bf16_hi(gw[k]), bf16_hi(uw[k]), g1, u1);
-      og[k] = g0 | (g1 << 16);
-      ou[k] = u0 | (u1 << 16);
-      m = __vmaxu2(m, __vmaxu2(og[k] & 0x7FFF7FFFu, ou[k] & 0x7FFF7FFFu));
+      for (int k = 0; k < 4; ++k) {
+        uint32_t g0, u0, g1, u1;
+        swiglu_grad(bf16_lo(dw[k]), bf16_lo(gw[k]), bf16_lo(uw[k]), g0, u0);
+        swiglu_grad(bf16_hi(dw[k]), bf16_hi(gw[k]), bf16_hi(uw[k]), g1, u1);
+        og[k] = g0 | (g1 << 16);
+        ou[k] = u0 | (u1 << 16);
+        m = __vmaxu2(m, __vmaxu2(og[k] & 0x7FFF7FFFu, ou[k] & 0x7FFF7FFFu));
+      }
+      *reinterpret_cast<uint4*>(po) = make_uint4(og[0], og[1], og[2], og[3]);
+      *reinterpret_cast<uint4*>(po + 32) = make_uint4(ou[0], ou[1], ou[2], ou[3]);
     }
-    *reinterpret_cast<uint4*>(grad_gu + r * ldgg + 64 * c + j0) = make_uint4(og[0], og[1], og[2], og[3]);
-    *reinterpret_cast<uint4*>(grad_gu + r * ldgg + 64 * c + 32 + j0) = make_uint4(ou[0], ou[1], ou[2], ou[3]);
   }
   // max |x| bits -> fp32 bits, block maximum, one atomic per block; the last block converts.
   m = max(m & 0xFFFFu, m >> 16) << 16;
@@ -72,7 +81,7 @@ __global__ void __launch_bounds__(256) swiglu_backward_kernel(const uint16_t* gr
     for (int w = 1; w < (int)(blockDim.x >> 5); ++w) m = max(m, red[w]);
     atomicMax(&ws[0], m);
     __threadfence();
-    last = atomicAdd(&ws[1], 1u) == gridDim.x - 1;
+    last = atomicAdd(&ws[1], 1u) == gridDim.x * gridDim.y - 1;
     if (last) {
       __threadfence();
       const uint32_t mb = atomicExch(&ws[0], 0u);
@@ -111,13 +120,17 @@ extern "C" int rb_nvfp4_swiglu_backward(const void* grad_h, int64_t ldgh, const 
     rb_host::set_error("nvfp4 swiglu_backward: the current device is not an sm_100 GPU");
     return RB_ERR_DEVICE;
   }
-  const int64_t chunks = rows * (hidden / 8);
-  int64_t grid = (chunks + 255) / 256;
-  const int64_t cap = 8 * (int64_t)rb_host::sm_budget(dev);
-  if (grid > cap) grid = cap;
-  rb::swiglu_backward_kernel<<<(int)grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  // About eight 256-thread blocks per SM, each covering a run of rows for 256 chunks of the hidden
+  // dimension.
+  const int64_t gx = (hidden / 8 + 255) / 256;
+  int64_t gy = (8 * (int64_t)rb_host::sm_budget(dev) + gx - 1) / gx;
+  if (gy > rows) gy = rows;
+  if (gy > 65535) gy = 65535;
+  const int64_t rows_per_y = (rows + gy - 1) / gy;
+  gy = (rows + rows_per_y - 1) / rows_per_y;
+  rb::swiglu_backward_kernel<<<dim3((unsigned)gx, (unsigned)gy), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<const uint16_t*>(grad_h), ldgh, reinterpret_cast<const uint16_t*>(gu), ldgu, rows, hidden,
-      reinterpret_cast<uint16_t*>(grad_gu), ldgg, reinterpret_cast<uint32_t*>(workspace), gs_out);
+      rows_per_y, reinterpret_cast<uint16_t*>(grad_gu), ldgg, reinterpret_cast<uint32_t*>(workspace), gs_out);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     rb_host::set_error("nvfp4 swiglu_backward launch failed: %s", cudaGetErrorString(e));
