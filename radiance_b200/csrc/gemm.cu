@@ -244,7 +244,7 @@ __device__ __forceinline__ float silu_ieee(float g) { return g / (1.0f + expf(-g
 // The table replaces an exp, a division and their range handling per element (about 40
 // instructions), which the epilogue's one warp per scheduler could not hide behind the MMAs.
 // rb_nvfp4_selftest_silu compares the whole mapping with bf16(silu_ieee(g)) for all 65536 g.
-constexpr uint32_t kSiluE0 = 118, kSiluE1 = 134;  // table exponents [kSiluE0, kSiluE1)
+constexpr uint32_t kSiluE0 = 118;  // table exponents [kSiluE0, kSiluE0 + 16)
 constexpr int kSiluTab = 2048;                     // entries per sign: 16 exponents x 128 significands
 
 // Fills the table at `tab` (threads tid = 0..nthreads-1 of the caller): entry s * 2048 + i is the

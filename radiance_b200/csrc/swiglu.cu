@@ -18,19 +18,47 @@ namespace rb {
 
 __device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
-__device__ __forceinline__ uint32_t bf16_bits(float f) {
-  return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(f));
+
+// RN(g / d) for d = 1 + exp(-g), two elements at a time, given nd = -d and s = RN(1/d).
+// Markstein's correctly rounded division (P. Markstein, IBM J. R&D 34(1), 1990; Muller et al.,
+// Handbook of Floating-Point Arithmetic, ch. 4): q = RN(g * s), then two residual corrections
+// r = g - q*d, q += r*s, each one fused multiply-add on the packed f32x2 pipe; the first makes q
+// faithful, the second, with a correctly rounded reciprocal, makes it the correctly rounded
+// quotient.  That needs a finite g, a finite d and a normal residual, so the rare elements outside
+// 2^-100 <= |g| < 2^100 and g > -64 (exp(64) < 2^93) -- signed zeros, subnormals, infinities, NaN,
+// large negative gates whose d overflows -- take the IEEE divide.
+__device__ __forceinline__ bool markstein_ok(float g) { return fabsf(g) >= 0x1p-100f && g > -64.0f && g < 0x1p100f; }
+
+__device__ __forceinline__ float2 silu_quotient2(float2 g, float2 d, float2 nd, float2 s) {
+  float2 q = __fmul2_rn(g, s);
+  float2 r = __ffma2_rn(q, nd, g);
+  q = __ffma2_rn(r, s, q);
+  r = __ffma2_rn(q, nd, g);
+  q = __ffma2_rn(r, s, q);
+  if (!markstein_ok(g.x)) q.x = __fdiv_rn(g.x, d.x);
+  if (!markstein_ok(g.y)) q.y = __fdiv_rn(g.y, d.y);
+  return q;
 }
 
-// One element: (grad_g, grad_u) as bf16 bit patterns.
-__device__ __forceinline__ void swiglu_grad(float dh, float g, float u, uint32_t& gg, uint32_t& gu) {
-  const float e = expf(-g);
-  const float d = 1.0f + e;
-  const float silu = __uint_as_float(bf16_bits(__fdiv_rn(g, d)) << 16);  // F.silu(g), bf16
-  gu = bf16_bits(dh * silu);                                             // grad_h * F.silu(g)
-  const float t = __uint_as_float(bf16_bits(dh * u) << 16);              // grad_h * u, bf16
-  const float s = __fdiv_rn(1.0f, d);
-  gg = bf16_bits(t * s * __fmaf_rn(g, 1.0f - s, 1.0f));                  // silu_backward(t, g)
+// Two fp32 values -> two bf16 (round to nearest even), x in the low half.
+__device__ __forceinline__ uint32_t bf16x2_bits(float2 v) {
+  const __nv_bfloat162 b = __float22bfloat162_rn(v);
+  return *reinterpret_cast<const uint32_t*>(&b);
+}
+__device__ __forceinline__ float2 bf16x2_float2(uint32_t w) { return make_float2(bf16_lo(w), bf16_hi(w)); }
+
+// Two elements (the low and high bf16 of each word): (grad_g, grad_u) as bf16x2 words.  s = 1 / d is
+// the correctly rounded reciprocal, the value the IEEE divide 1.0f / d gives.
+__device__ __forceinline__ void swiglu_grad2(uint32_t dhw, uint32_t gw, uint32_t uw, uint32_t& ggw, uint32_t& guw) {
+  const float2 dh = bf16x2_float2(dhw), g = bf16x2_float2(gw), u = bf16x2_float2(uw);
+  const float2 d = make_float2(1.0f + expf(-g.x), 1.0f + expf(-g.y));
+  const float2 s = make_float2(__frcp_rn(d.x), __frcp_rn(d.y));
+  const float2 one = make_float2(1.0f, 1.0f);
+  const float2 silu = bf16x2_float2(bf16x2_bits(silu_quotient2(g, d, make_float2(-d.x, -d.y), s)));  // F.silu(g)
+  guw = bf16x2_bits(__fmul2_rn(dh, silu));                                      // grad_h * F.silu(g)
+  const float2 t = bf16x2_float2(bf16x2_bits(__fmul2_rn(dh, u)));               // grad_h * u, bf16
+  const float2 w = __ffma2_rn(g, __fadd2_rn(one, make_float2(-s.x, -s.y)), one);  // 1 + g * (1 - s)
+  ggw = bf16x2_bits(__fmul2_rn(__fmul2_rn(t, s), w));                           // silu_backward(t, g)
 }
 
 // Thread layout: blockIdx.x and threadIdx.x pick an 8-unit chunk q of the hidden dimension (a chunk
@@ -58,11 +86,7 @@ __global__ void __launch_bounds__(256) swiglu_backward_kernel(const uint16_t* gr
       uint32_t og[4], ou[4];
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-        uint32_t g0, u0, g1, u1;
-        swiglu_grad(bf16_lo(dw[k]), bf16_lo(gw[k]), bf16_lo(uw[k]), g0, u0);
-        swiglu_grad(bf16_hi(dw[k]), bf16_hi(gw[k]), bf16_hi(uw[k]), g1, u1);
-        og[k] = g0 | (g1 << 16);
-        ou[k] = u0 | (u1 << 16);
+        swiglu_grad2(dw[k], gw[k], uw[k], og[k], ou[k]);
         m = __vmaxu2(m, __vmaxu2(og[k] & 0x7FFF7FFFu, ou[k] & 0x7FFF7FFFu));
       }
       *reinterpret_cast<uint4*>(po) = make_uint4(og[0], og[1], og[2], og[3]);
@@ -120,10 +144,17 @@ extern "C" int rb_nvfp4_swiglu_backward(const void* grad_h, int64_t ldgh, const 
     rb_host::set_error("nvfp4 swiglu_backward: the current device is not an sm_100 GPU");
     return RB_ERR_DEVICE;
   }
-  // About eight 256-thread blocks per SM, each covering a run of rows for 256 chunks of the hidden
-  // dimension.
+  // One wave: as many 256-thread blocks as the SMs hold at once, each covering a run of rows for 256
+  // chunks of the hidden dimension, so no SM idles through a partial last wave.
+  static int resident[64] = {0};
+  int& per_sm = resident[dev & 63];
+  if (per_sm == 0 &&
+      (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rb::swiglu_backward_kernel, 256, 0) != cudaSuccess ||
+       per_sm < 1))
+    per_sm = 1;
   const int64_t gx = (hidden / 8 + 255) / 256;
-  int64_t gy = (8 * (int64_t)rb_host::sm_budget(dev) + gx - 1) / gx;
+  int64_t gy = ((int64_t)per_sm * rb_host::sm_budget(dev)) / gx;
+  if (gy < 1) gy = 1;
   if (gy > rows) gy = rows;
   if (gy > 65535) gy = 65535;
   const int64_t rows_per_y = (rows + gy - 1) / gy;
