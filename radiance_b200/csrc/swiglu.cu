@@ -64,7 +64,7 @@ __device__ __forceinline__ void swiglu_grad2(uint32_t dhw, uint32_t gw, uint32_t
 // Thread layout: blockIdx.x and threadIdx.x pick an 8-unit chunk q of the hidden dimension (a chunk
 // never straddles a 32-unit group), blockIdx.y a run of `rows_per_y` rows; a warp's 32 chunks of one
 // row are contiguous in all three tensors.  No index division in the loop.
-__global__ void __launch_bounds__(256) swiglu_backward_kernel(const uint16_t* grad_h, int64_t ldgh, const uint16_t* gu,
+__global__ void __launch_bounds__(256, 6) swiglu_backward_kernel(const uint16_t* grad_h, int64_t ldgh, const uint16_t* gu,
                                                               int64_t ldgu, int64_t rows, int64_t hidden,
                                                               int64_t rows_per_y, uint16_t* grad_gu, int64_t ldgg,
                                                               uint32_t* ws, float* gs_out) {
