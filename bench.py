@@ -752,13 +752,36 @@ def measure_comparators(block, xs, dys, device):
         flops = 6.0 * tokens * LAYER_KN
         ms_o, _ = _graph_ms(ours)
         ms_c, mode = _graph_ms(cublaslt)
+        # Each GEMM alone, 4 back-to-back launches per graph replay (the operands stay in L2 only
+        # where they fit, as they do inside the step).
+        per_gemm = []
+        names = [f"{name}.{kind}" for name, _, _ in LAYERS for kind in ("fwd", "dgrad", "wgrad")]
+        for name, (a, b, o, od) in zip(names, calls):
+            def one_ours(a=a, b=b, o=o, od=od):
+                for _ in range(4):
+                    _gemm(a.packed.view(torch.uint8), a.scale.view(torch.uint8), b.packed.view(torch.uint8),
+                          b.scale.view(torch.uint8), a.global_scale, b.global_scale, None, od, o)
+
+            def one_cublaslt(a=a, b=b, od=od):
+                for _ in range(4):
+                    torch._scaled_mm_v2(a.packed, b.packed.t(), scale_a=[a.scale], recipe_a=blk, swizzle_a=swz,
+                                        scale_b=[b.scale], recipe_b=blk, swizzle_b=swz, bias=None, out_dtype=od)
+
+            po, _ = _graph_ms(one_ours)
+            pc, _ = _graph_ms(one_cublaslt)
+            m_, k2 = a.packed.shape
+            per_gemm.append({"gemm": name, "mnk": [m_, b.packed.shape[0], 2 * k2],
+                             "ours_us": round(po * 250, 1), "cublaslt_us": round(pc * 250, 1),
+                             "ratio": round(pc / po, 3)})
         out["gemms_vs_cublaslt"] = {
             "ours_ms": round(ms_o, 4), "cublaslt_ms": round(ms_c, 4),
             "ours_TFLOPS": round(flops / (ms_o * 1e-3) / 1e12, 1), "cublaslt_TFLOPS": round(flops / (ms_c * 1e-3) / 1e12, 1),
             "ratio": round(ms_c / ms_o, 4), "timing": mode,
+            "slower_than_cublaslt": [p["gemm"] for p in per_gemm if p["ratio"] < 1.0],
+            "per_gemm": per_gemm,
             "what": "the step's 12 GEMMs (fwd, dgrad, wgrad of the 4 linears; bf16, bf16, fp32 outputs) on identical "
                     "NVFP4 operands: rb_nvfp4_gemm vs torch._scaled_mm_v2 (cuBLASLt, the GEMM radiance calls); "
-                    "ratio = cuBLASLt time / ours",
+                    "ratio = cuBLASLt time / ours; per_gemm times each alone (4 launches per graph replay)",
         }
         del calls
     except Exception as e:
