@@ -1615,7 +1615,7 @@ cudaProfilerStart/Stop (so `ncu --profile-from-start off` captures only those la
                GEMM (torch._scaled_mm_v2) on the same operands instead, for comparison
   swiglu       the SwiGLU producer of a config-3 FFN: --variant fused (the gate/up GEMM whose epilogue
                writes h and its global scale) | unfused (GEMM, torch F.silu(g) * u, amax); each then
-               quantizes h both ways
+               quantizes h both ways; --variant fused-gemm times the SwiGLU GEMM alone
   block-gemms  the twelve GEMMs of one config-3 block step (four linears x fwd, dgrad, wgrad): --tokens
   swiglu-bwd   the fused SwiGLU backward (grad_gu and its global scale): --m --hidden
   block-step   one whole config-3 block step (QKV, O, fused FFN; forward then backward): --tokens
@@ -1713,6 +1713,9 @@ def _case_swiglu(args, dev):
            torch.empty(col_scale_bytes(m, hid), dtype=torch.uint8, device=dev))
 
     def run():
+        if args.variant == "fused-gemm":  # the SwiGLU GEMM alone
+            swiglu_mm(xq, wq, out=gu, h=h, h_global_scale=gs)
+            return
         if args.variant == "fused":
             swiglu_mm(xq, wq, out=gu, h=h, h_global_scale=gs)
             hh = h
@@ -1797,7 +1800,7 @@ def run_case(argv):
     ap.add_argument("--k", type=int, default=2048)
     ap.add_argument("--hidden", type=int, default=5632)
     ap.add_argument("--tokens", type=int, default=16384)
-    ap.add_argument("--variant", default="ours", help="gemm: ours|cublas; swiglu: fused|unfused")
+    ap.add_argument("--variant", default="ours", help="gemm: ours|cublas; swiglu: fused|fused-gemm|unfused")
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--time", action="store_true", help="graph-capture the iterations and time them (one JSON line)")
     args = ap.parse_args(argv)

@@ -359,9 +359,9 @@ __device__ __forceinline__ void swiglu_finish(const GemmArgs& g, uint32_t hmax, 
   }
 }
 
-// In SwiGLU mode each warp stages through one box: its first, except warp 1, which uses its second;
-// the 8 KB from warp 0's second box through warp 1's first hold the silu table.
-template <bool kSwiglu>
+// kOneBox (SwiGLU mode): the warp stages every bf16 piece through the one box at `slots`;
+// otherwise bf16 pieces alternate between the warp's two boxes.
+template <bool kSwiglu, bool kOneBox = kSwiglu>
 __device__ __forceinline__ void epilogue_piece(const uint32_t (&r)[kEpiChunk], float alpha, const GemmArgs& g,
                                                const CUtensorMap* tmO, uint32_t slots, int& slot, int col0,
                                                int64_t row0, int64_t row_end, int lane, uint32_t& hmax,
@@ -435,12 +435,11 @@ __device__ __forceinline__ void epilogue_piece(const uint32_t (&r)[kEpiChunk], f
     }
   } else {
     if (lane == 0) {
-      if constexpr (kSwiglu) bulk_wait_read<0>();
+      if constexpr (kOneBox) bulk_wait_read<0>();
       else bulk_wait_read<1>();
     }
     __syncwarp();
-    const uint32_t box =
-        slots + (kSwiglu ? (((threadIdx.x >> 5) & 3) == 1 ? (uint32_t)kOutBox : 0u) : (uint32_t)slot * kOutBox);
+    const uint32_t box = kOneBox ? slots : slots + (uint32_t)slot * kOutBox;
 #pragma unroll
     for (int c = 0; c < 8; ++c)
       st_shared_v4(box + row_off + ((c ^ sw) << 4), pack_bf16x2(v[8 * c], v[8 * c + 1]),
@@ -609,7 +608,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else {
     // ------------------------------------------------------------------ epilogue (warps 2..5)
     const int q = warp & 3;  // TMEM lanes 32q .. 32q+31
-    const uint32_t slots = smem_u32(sm.out[q]);
+    // SwiGLU mode: one box per warp (its first; warp q == 1 its second), the 8 KB from sm.out[0][1]
+    // through sm.out[1][0] holding the silu table.
+    const uint32_t slots = smem_u32(sm.out[q]) + ((kSwiglu && q == 1) ? (uint32_t)kOutBox : 0u);
     int slot = 0;
     uint32_t hmax = 0;  // SwiGLU mode: this lane's max |h| (bf16 bits)
     const uint32_t tab = smem_u32(sm.out[0][1]);  // SwiGLU mode: 8 KB, through sm.out[1][0]
@@ -676,25 +677,43 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // same shared-memory offsets in both CTAs and write the same TMEM columns in both.  The leader's
 // commits arrive on both CTAs' barriers (multicast commit), and the peer's epilogue warps release
 // the shared accumulator columns on the leader's barrier.  One 256x256x64 MMA and three scale
-// copies serve two SMs, half the per-FLOP issue and copy work of the one-SM kernel.
+// copies serve two SMs, half the per-FLOP issue and copy work of the one-SM kernel.  The SwiGLU
+// instantiation runs eight epilogue warps (10 warps per CTA) and four operand stages (Gemm2Cfg).
 // =============================================================================================
-constexpr int kStages2 = 5;
 constexpr int kSfStep = 2048;  // one K step's scale atoms for 128 rows (4 x 512 B)
 
+// Per instantiation: the plain GEMM keeps five operand stages and four epilogue warps.  The SwiGLU
+// GEMM is bound by its epilogue (the per-element SwiGLU work on top of the output), so it runs two
+// epilogue warps on each TMEM lane quarter -- eight in all, two per scheduler, each taking every
+// other 64-column chunk -- and pays for their staging boxes and the silu table with one stage less.
+template <bool kSwiglu>
+struct Gemm2Cfg {
+  static constexpr int kStages = kSwiglu ? 4 : 5;
+  static constexpr int kEpiWarps = kSwiglu ? 8 : 4;
+  static constexpr int kThreads = 64 + 32 * kEpiWarps;  // producer, MMA issuer, epilogue
+};
+
+template <bool kSwiglu>
 struct Gemm2Smem {
-  uint8_t a[kStages2][kBM * kStepBytes];  // this CTA's 128 A rows (16 KB)
-  uint8_t b[kStages2][kBM * kStepBytes];  // this CTA's 128 of the tile's 256 B rows (16 KB)
-  uint8_t sfa[kStages2][kSfStep];         // scale atoms of this CTA's A rows
-  uint8_t sfb[kStages2][2 * kSfStep];     // scale atoms of all 256 B rows: [half][k block]
-  uint8_t out[4][2][4096];                // per epilogue warp: two staged output boxes
-  int tile_prefix[kMaxGroups + 1];        // grouped mode: tiles of groups 0..g-1
-  uint64_t full[kStages2];                // leader: both CTAs' loads of a stage
-  uint64_t empty[kStages2];               // each CTA: the leader's MMAs finished with a stage
-  uint64_t acc_full;                      // each CTA: the accumulator of a tile is complete
-  uint64_t acc_empty;                     // leader: the pair's 8 epilogue warps drained the shared columns
+  static constexpr int S = Gemm2Cfg<kSwiglu>::kStages;
+  uint8_t a[S][kBM * kStepBytes];  // this CTA's 128 A rows (16 KB)
+  uint8_t b[S][kBM * kStepBytes];  // this CTA's 128 of the tile's 256 B rows (16 KB)
+  uint8_t sfa[S][kSfStep];         // scale atoms of this CTA's A rows
+  uint8_t sfb[S][2 * kSfStep];     // scale atoms of all 256 B rows: [half][k block]
+  uint8_t out[4][2][4096];  // staged output boxes: two per epilogue warp, or one in SwiGLU mode
+  uint16_t silu_tab[kSwiglu ? 2 * kSiluTab : 8];  // SwiGLU mode: the silu table
+  int tile_prefix[kMaxGroups + 1];  // grouped mode: tiles of groups 0..g-1
+  uint64_t full[S];                 // leader: both CTAs' loads of a stage
+  uint64_t empty[S];                // each CTA: the leader's MMAs finished with a stage
+  uint64_t acc_full;                // each CTA: the accumulator of a tile is complete
+  uint64_t acc_empty;               // leader: the pair's epilogue warps are done with the shared columns
   uint64_t drain;
   uint32_t tmem_base;
 };
+
+// Dynamic shared memory is the struct plus 1 KB for the 1024-byte alignment; 227 KB per CTA at most.
+static_assert(sizeof(Gemm2Smem<false>) + 1024 <= 232448 && sizeof(Gemm2Smem<true>) + 1024 <= 232448,
+              "two-SM GEMM shared memory exceeds 227 KB");
 
 constexpr uint32_t kStageBytes2 = 2 * kBM * kStepBytes + 3 * kSfStep;  // per CTA
 
@@ -825,12 +844,15 @@ __device__ __forceinline__ Tile2 tile2_at(int t, const GemmArgs& g, const int* p
 }
 
 template <bool kSwiglu>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+__global__ void __launch_bounds__(Gemm2Cfg<kSwiglu>::kThreads, 1)
     nvfp4_gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                        const __grid_constant__ CUtensorMap tmSA, const __grid_constant__ CUtensorMap tmSB,
                        const __grid_constant__ CUtensorMap tmO, const GemmArgs g) {
   extern __shared__ uint8_t smem_raw[];
-  Gemm2Smem& sm = *reinterpret_cast<Gemm2Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  using Smem = Gemm2Smem<kSwiglu>;
+  constexpr int kS = Gemm2Cfg<kSwiglu>::kStages;
+  constexpr int kEW = Gemm2Cfg<kSwiglu>::kEpiWarps;
+  Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_rank();
   const int cid = (int)cluster_id(), ncl = (int)cluster_count();
@@ -861,12 +883,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages2; ++s) {
+    for (int s = 0; s < kS; ++s) {
       mbar_init(&sm.full[s], 1);
       mbar_init(&sm.empty[s], 1);
     }
     mbar_init(&sm.acc_full, 1);
-    mbar_init(&sm.acc_empty, 8);
+    mbar_init(&sm.acc_empty, 2 * kEW);
     mbar_init(&sm.drain, 1);
     fence_mbar_init();
     prefetch_tensormap(&tmA);
@@ -925,7 +947,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                                   (int)((sb_row + g.kb_total + 4 * ks) * 2));
           }
           __syncwarp();
-          if (++stage == kStages2) {
+          if (++stage == kS) {
             stage = 0;
             phase ^= 1u;
           }
@@ -980,7 +1002,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             tc_commit2(&sm.empty[stage], 0x3);
           }
           __syncwarp();
-          if (++stage == kStages2) {
+          if (++stage == kS) {
             stage = 0;
             phase ^= 1u;
           }
@@ -994,15 +1016,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_wait_warp(&sm.drain, 0);
     }
   } else {
-    // ------------------------------------------------------------------ epilogue (warps 2..5, both CTAs)
+    // ------------------------------------------------------------------ epilogue (warps 2 .. 2+kEW-1, both CTAs)
+    // A warp reaches the TMEM lanes of its warp id mod 4.  With eight epilogue warps, warps w and
+    // w + 4 share a lane quarter and split its 64-column chunks: `half` takes chunks c with
+    // c % 2 == half.
     const int q = warp & 3;  // TMEM lanes 32q .. 32q+31
-    const uint32_t slots = smem_u32(sm.out[q]);
+    constexpr int kStride = kEW / 4;
+    const int half = (warp - 2) / 4;
+    // Staging: two boxes per warp (pieces alternate between them), or in SwiGLU mode one box per
+    // warp, box w - 2 of the eight (two boxes each measured slower: the stores are not the limit).
+    const uint32_t slots =
+        kSwiglu ? smem_u32(&sm.out[0][0][0]) + (uint32_t)(warp - 2) * kOutBox : smem_u32(&sm.out[q][0][0]);
     int slot = 0;
     uint32_t hmax = 0;  // SwiGLU mode: this lane's max |h| (bf16 bits)
-    const uint32_t tab = smem_u32(sm.out[0][1]);  // SwiGLU mode: 8 KB, through sm.out[1][0]
-    if constexpr (kSwiglu) {  // the four epilogue warps (threads 64..191) build the silu table
-      silu_table_build(tab, (int)threadIdx.x - 64, 128);
-      asm volatile("bar.sync 1, 128;" ::: "memory");
+    const uint32_t tab = smem_u32(&sm.silu_tab[0]);
+    if constexpr (kSwiglu) {  // the epilogue warps (threads 64 ..) build the silu table
+      silu_table_build(tab, (int)threadIdx.x - 64, 32 * kEW);
+      asm volatile("bar.sync 1, %0;" ::"n"(32 * kEW) : "memory");
     }
     for (int i = 0; i < n_my; ++i) {
       const Tile2 T = tile2_at(cid + i * ncl, g, sm.tile_prefix);
@@ -1018,15 +1048,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       tc_fence_after();
       const int nch = width / kEpiChunk;
-      const int first = (buf == 0) ? ((width == kBN) ? nch - 1 : -1) : 0;
+      // The chunk in the columns both buffers use ([192, 256)): its reader drains it first and then
+      // releases; every other warp releases at once.  acc_empty completes after all 2 * kEW.
+      const int sc = (buf == 0) ? ((width == kBN) ? nch - 1 : -1) : 0;
+      const bool mine_sc = sc >= 0 && (sc % kStride) == half;
       auto release = [&]() {
         if (rank == 0) mbar_arrive(&sm.acc_empty);
         else mbar_arrive_leader(&sm.acc_empty);
       };
-      if (first < 0 && lane == 0) release();
+      if (!mine_sc && lane == 0) release();
       const int64_t row0 = T.orow + (int64_t)rank * kBM + 32 * q;
-      for (int step = 0; step < nch; ++step) {
-        const int c = (first < 0) ? step : (step == 0 ? first : (buf == 0 ? step - 1 : step));
+      const int nmine = (nch - half + kStride - 1) / kStride;
+      for (int step = 0; step < nmine; ++step) {
+        // This warp's chunks in ascending order, except that a shared last chunk (buffer 0) goes first.
+        const int c = (mine_sc && buf == 0) ? (step == 0 ? sc : half + (step - 1) * kStride) : half + step * kStride;
         uint32_t r[kEpiChunk];
         if (T.k_blocks > 0) {
           const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(base_col + c * kEpiChunk);
@@ -1037,7 +1072,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
           for (int j = 0; j < kEpiChunk; ++j) r[j] = 0u;
         }
-        if (step == 0 && first >= 0) {
+        if (step == 0 && mine_sc) {
           tc_fence_before();
           __syncwarp();
           if (lane == 0) release();
@@ -1046,7 +1081,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                                 hmax, tab);
       }
     }
-    if constexpr (kSwiglu) swiglu_finish(g, hmax, gridDim.x * 4u, lane);
+    if constexpr (kSwiglu) swiglu_finish(g, hmax, gridDim.x * (uint32_t)kEW, lane);
     if (lane == 0) bulk_wait_all();
     if (g.npeers > 0) __threadfence_system();
     __syncwarp();
@@ -1085,7 +1120,7 @@ int launch_two_sm(GemmArgs& g, const CUtensorMap& tmA, const CUtensorMap& tmB, c
                              CU_TENSOR_MAP_SWIZZLE_NONE))
     return RB_ERR_CUDA;
   const int sms = rb_host::sm_budget(dev);
-  const size_t smem = sizeof(Gemm2Smem) + 1024;
+  const size_t smem = sizeof(Gemm2Smem<kSwiglu>) + 1024;
   static int max_clusters[64] = {0};
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
@@ -1093,7 +1128,7 @@ int launch_two_sm(GemmArgs& g, const CUtensorMap& tmA, const CUtensorMap& tmB, c
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
-  cfg.blockDim = dim3(kGemmThreads, 1, 1);
+  cfg.blockDim = dim3(Gemm2Cfg<kSwiglu>::kThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cfg.attrs = attr;
