@@ -272,15 +272,42 @@ __device__ __forceinline__ float silu_lookup(uint32_t b, float gf, uint32_t tab)
   return a < 0.001953125f /* 2^-9 */ ? half : (a < 128.0f ? t : gf);  // NaN fails a < 128: gf
 }
 
+// silu_lookup for the two bf16 gates in the halves of gw, as a bf16x2 word: the same mapping with
+// packed integer and bf16x2 operations.  Per half: |g| < 2^-9 (bits below 0x3B00) gives g * 0.5 as
+// one bf16 multiply (the exact product rounded once, as bf16(float(g) * 0.5f) rounds it); bits
+// 0x3B00 .. 0x42FF the table entry; |g| >= 128, inf and NaN (bits 0x4300 and up) g itself.
+// rb_nvfp4_selftest_silu checks it on every bf16 input in both halves.
+__device__ __forceinline__ uint32_t sign_mask2(uint32_t x) {  // 0xFFFF in each half whose bit 15 is set
+  uint32_t m;
+  asm("prmt.b32 %0, %1, 0, 0xBB99;" : "=r"(m) : "r"(x));
+  return m;
+}
+__device__ __forceinline__ uint32_t silu_lookup2(uint32_t gw, uint32_t tab) {
+  const uint32_t a = (gw & 0x7FFF7FFFu) | 0x80008000u;  // |g| bits with a guard bit: no borrow between halves
+  const uint32_t not_small = sign_mask2(a - 0x3B003B00u);        // |g| >= 2^-9
+  const uint32_t big = sign_mask2(a - 0x43004300u);              // |g| >= 128, inf, NaN
+  // Table offsets 2 * (((b - (kSiluE0 << 7)) & 0x7FF) | (sign << 11)) per half; the guard bit in the
+  // low half keeps its subtraction from borrowing out of the high half.
+  const uint32_t off = ((((gw | 0x8000u) - (kSiluE0 << 7) * 0x10001u) & 0x07FF07FFu) | ((gw >> 4) & 0x08000800u)) << 1;
+  uint16_t t0, t1;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(t0) : "r"(tab + (off & 0xFFFFu)));
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(t1) : "r"(tab + (off >> 16)));
+  const uint32_t t = (uint32_t)t0 | ((uint32_t)t1 << 16);
+  const __nv_bfloat162 hv = __hmul2_rn(*reinterpret_cast<const __nv_bfloat162*>(&gw), __float2bfloat162_rn(0.5f));
+  const uint32_t halfw = *reinterpret_cast<const uint32_t*>(&hv);
+  const uint32_t mid = (t & not_small) | (halfw & ~not_small);
+  return (gw & big) | (mid & ~big);
+}
+
 // The SwiGLU half of a 64-column piece: v[j] (gate) and v[32 + j] (up), j < 32, are one row's
 // pre-activations of 32 consecutive hidden units.  Each h is rounded as radiance's bf16
 // F.silu(g) * u rounds it (src/radiance/model/ffn.py:32): g and u to bf16 (as stored in the
-// output), silu(g) to bf16, the product (exact in fp32) to bf16.  The row's 32 values are one
-// 64-byte run of h.  Rows at or past row_end are neither stored nor counted in the maximum.  The
-// whole warp runs this: a gate value at or below -128 anywhere in it sends the warp down the
-// IEEE evaluation (rare).
-__device__ __forceinline__ void swiglu_piece(const float* v, const GemmArgs& g, int col0, int64_t row,
-                                             int64_t row_end, uint32_t& hmax, uint32_t tab) {
+// output), silu(g) to bf16, the product (exact in fp32) to bf16.  w receives the row's 32 values
+// (one 64-byte run of h); rows at or past row_end are not counted in the maximum.  The whole warp
+// runs this: a gate value at or below -128 anywhere in it sends the warp down the IEEE evaluation
+// (rare).
+__device__ __forceinline__ void swiglu_piece(const float* v, int64_t row, int64_t row_end, uint32_t& hmax,
+                                             uint32_t tab, uint32_t (&w)[16]) {
   uint32_t gw[16];
   __nv_bfloat162 mn = __float2bfloat162_rn(0.0f);
 #pragma unroll
@@ -289,37 +316,34 @@ __device__ __forceinline__ void swiglu_piece(const float* v, const GemmArgs& g, 
     mn = __hmin2(mn, *reinterpret_cast<const __nv_bfloat162*>(&gw[j]));
   }
   const bool far = fminf(__low2float(mn), __high2float(mn)) <= -128.0f;
-  float sl[32];
   if (__any_sync(0xFFFFFFFFu, far)) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const uint32_t b = (j & 1) ? (gw[j >> 1] >> 16) : (gw[j >> 1] & 0xFFFFu);
-      sl[j] = __bfloat162float(__float2bfloat16_rn(silu_ieee(__uint_as_float(b << 16))));
+    for (int j = 0; j < 16; ++j) {
+      const float s0 = __bfloat162float(__float2bfloat16_rn(silu_ieee(__uint_as_float(gw[j] << 16))));
+      const float s1 = __bfloat162float(__float2bfloat16_rn(silu_ieee(__uint_as_float(gw[j] & 0xFFFF0000u))));
+      const uint32_t uw = pack_bf16x2(v[32 + 2 * j], v[32 + 2 * j + 1]);
+      w[j] = pack_bf16x2(s0 * __uint_as_float(uw << 16), s1 * __uint_as_float(uw & 0xFFFF0000u));
     }
   } else {
+    // silu(g) * u on bf16x2 pairs: the product of two bf16 values is exact in fp32, so one bf16
+    // multiply rounds it exactly as the fp32 product rounded to bf16.
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const uint32_t b = (j & 1) ? (gw[j >> 1] >> 16) : (gw[j >> 1] & 0xFFFFu);
-      sl[j] = silu_lookup(b, __uint_as_float(b << 16), tab);
+    for (int j = 0; j < 16; ++j) {
+      const uint32_t sw = silu_lookup2(gw[j], tab);
+      const __nv_bfloat162 u2 = __floats2bfloat162_rn(v[32 + 2 * j], v[32 + 2 * j + 1]);
+      const __nv_bfloat162 h2 = __hmul2_rn(*reinterpret_cast<const __nv_bfloat162*>(&sw), u2);
+      w[j] = *reinterpret_cast<const uint32_t*>(&h2);
     }
   }
-  uint32_t w[16];
-#pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    const uint32_t uw = pack_bf16x2(v[32 + 2 * j], v[32 + 2 * j + 1]);
-    w[j] = pack_bf16x2(sl[2 * j] * __uint_as_float(uw << 16), sl[2 * j + 1] * __uint_as_float(uw & 0xFFFF0000u));
-  }
   if (row >= row_end) return;
+  uint32_t m2 = 0;
 #pragma unroll
-  for (int j = 0; j < 16; ++j)
-    hmax = max(hmax, max(w[j] & 0x7FFFu, (w[j] >> 16) & 0x7FFFu));  // |h| as bf16 bits (NaN above inf)
-  uint8_t* p = reinterpret_cast<uint8_t*>(g.h) + (row * g.ldh + (col0 >> 1)) * 2;
-#pragma unroll
-  for (int q = 0; q < 4; ++q) st_global_v4(p + 16 * q, w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+  for (int j = 0; j < 16; ++j) m2 = __vmaxu2(m2, w[j] & 0x7FFF7FFFu);  // |h| as bf16 bits (NaN above inf)
+  hmax = max(hmax, max(m2 & 0xFFFFu, m2 >> 16));
 }
 
-// Compares the epilogue's silu (silu_lookup, and the IEEE evaluation at or below -128) with
-// bf16(silu_ieee(g)) on all 65536 bf16 inputs: mismatches[0] counts bf16 results that differ (NaNs
+// Compares the epilogue's silu (silu_lookup and silu_lookup2 in both halves, and the IEEE
+// evaluation at or below -128) with bf16(silu_ieee(g)) on all 65536 bf16 inputs: mismatches[0] counts bf16 results that differ (NaNs
 // compare equal), mismatches[1] keeps the largest failing bit pattern plus one.
 __global__ void __launch_bounds__(256) selftest_silu_kernel(uint32_t* mismatches) {
   __shared__ __align__(16) uint16_t tab[2 * kSiluTab];
@@ -331,9 +355,15 @@ __global__ void __launch_bounds__(256) selftest_silu_kernel(uint32_t* mismatches
     const __nv_bfloat16 r = __float2bfloat16_rn(silu_ieee(gf));
     const uint32_t want = *reinterpret_cast<const uint16_t*>(&r);
     const float sv = gf <= -128.0f ? __bfloat162float(r) : silu_lookup(b, gf, tab_addr);
+    // The packed form, with b in the low half next to another gate above -128 in the high half,
+    // and in the high half next to that gate.
+    const uint32_t o = (b * 40503u + 12345u) & 0x7FFFu;
+    const uint32_t lo2 = silu_lookup2(b | (o << 16), tab_addr) & 0xFFFFu;
+    const uint32_t hi2 = silu_lookup2(o | (b << 16), tab_addr) >> 16;
     const uint32_t got = __float_as_uint(sv) >> 16;
-    const bool nan_w = (want & 0x7FFFu) > 0x7F80u, nan_g = (got & 0x7FFFu) > 0x7F80u;
-    if (got != want && !(nan_w && nan_g)) {
+    const bool nan_w = (want & 0x7FFFu) > 0x7F80u;
+    const auto differs = [&](uint32_t x) { return x != want && !(nan_w && (x & 0x7FFFu) > 0x7F80u); };
+    if (differs(got) || (gf > -128.0f && (differs(lo2) || differs(hi2)))) {
       atomicAdd(&mismatches[0], 1u);
       atomicMax(&mismatches[1], b + 1u);
     }
@@ -361,11 +391,17 @@ __device__ __forceinline__ void swiglu_finish(const GemmArgs& g, uint32_t hmax, 
 
 // kOneBox (SwiGLU mode): the warp stages every bf16 piece through the one box at `slots`;
 // otherwise bf16 pieces alternate between the warp's two boxes.
-template <bool kSwiglu, bool kOneBox = kSwiglu>
+//
+// kHStage (SwiGLU mode): the piece's h (32 rows x 64 bytes) is staged in the warp's 2 KB box at
+// `hbox`, 64-byte swizzled (16-byte chunk c of row r at r * 64 + (c ^ ((r / 2) % 4)) * 16: the
+// layout of the h tensor map, and bank-conflict free for the 32 lanes' writes), and written by one
+// TMA store with the output box; otherwise each lane stores its row's 64 bytes of h directly.
+template <bool kSwiglu, bool kOneBox = kSwiglu, bool kHStage = false>
 __device__ __forceinline__ void epilogue_piece(const uint32_t (&r)[kEpiChunk], float alpha, const GemmArgs& g,
                                                const CUtensorMap* tmO, uint32_t slots, int& slot, int col0,
                                                int64_t row0, int64_t row_end, int lane, uint32_t& hmax,
-                                               uint32_t tab) {
+                                               uint32_t tab, const CUtensorMap* tmH = nullptr,
+                                               uint32_t hbox = 0) {
   float v[kEpiChunk];
 #pragma unroll
   for (int j = 0; j < kEpiChunk; ++j) v[j] = __fmul_rn(__uint_as_float(r[j]), alpha);
@@ -394,7 +430,17 @@ __device__ __forceinline__ void epilogue_piece(const uint32_t (&r)[kEpiChunk], f
       }
     }
   }
-  if constexpr (kSwiglu) swiglu_piece(v, g, col0, row0 + lane, row_end, hmax, tab);
+  uint32_t hw[16];
+  if constexpr (kSwiglu) {
+    swiglu_piece(v, row0 + lane, row_end, hmax, tab, hw);
+    if constexpr (!kHStage) {
+      if (row0 + lane < row_end) {
+        uint8_t* p = reinterpret_cast<uint8_t*>(g.h) + ((row0 + lane) * g.ldh + (col0 >> 1)) * 2;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) st_global_v4(p + 16 * q, hw[4 * q], hw[4 * q + 1], hw[4 * q + 2], hw[4 * q + 3]);
+      }
+    }
+  }
   const bool store = row0 < row_end;
   const uint32_t row_off = (uint32_t)lane * 128u, sw = (uint32_t)(lane & 7);
   // Copies a staged box (32 rows x 128 B) to every peer output with coalesced 16-byte stores:
@@ -445,10 +491,17 @@ __device__ __forceinline__ void epilogue_piece(const uint32_t (&r)[kEpiChunk], f
       st_shared_v4(box + row_off + ((c ^ sw) << 4), pack_bf16x2(v[8 * c], v[8 * c + 1]),
                    pack_bf16x2(v[8 * c + 2], v[8 * c + 3]), pack_bf16x2(v[8 * c + 4], v[8 * c + 5]),
                    pack_bf16x2(v[8 * c + 6], v[8 * c + 7]));
+    if constexpr (kHStage) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        st_shared_v4(hbox + (uint32_t)lane * 64u + ((uint32_t)(c ^ ((lane >> 1) & 3)) << 4), hw[4 * c], hw[4 * c + 1],
+                     hw[4 * c + 2], hw[4 * c + 3]);
+    }
     fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0 && store) {
       tma_store_2d(tmO, box, col0, (int)row0);
+      if constexpr (kHStage) tma_store_2d(tmH, hbox, col0 >> 1, (int)row0);
       bulk_commit_group();
     }
     if (g.npeers > 0 && store) to_peers(box, (int64_t)col0 * 2);
@@ -701,7 +754,8 @@ struct Gemm2Smem {
   uint8_t sfa[S][kSfStep];         // scale atoms of this CTA's A rows
   uint8_t sfb[S][2 * kSfStep];     // scale atoms of all 256 B rows: [half][k block]
   uint8_t out[4][2][4096];  // staged output boxes: two per epilogue warp, or one in SwiGLU mode
-  uint16_t silu_tab[kSwiglu ? 2 * kSiluTab : 8];  // SwiGLU mode: the silu table
+  uint8_t hbox[kSwiglu ? 8 : 1][kSwiglu ? 2048 : 16];  // SwiGLU mode: each epilogue warp's staged h box
+  uint16_t silu_tab[kSwiglu ? 2 * kSiluTab : 8];        // SwiGLU mode: the silu table
   int tile_prefix[kMaxGroups + 1];  // grouped mode: tiles of groups 0..g-1
   uint64_t full[S];                 // leader: both CTAs' loads of a stage
   uint64_t empty[S];                // each CTA: the leader's MMAs finished with a stage
@@ -847,7 +901,8 @@ template <bool kSwiglu>
 __global__ void __launch_bounds__(Gemm2Cfg<kSwiglu>::kThreads, 1)
     nvfp4_gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                        const __grid_constant__ CUtensorMap tmSA, const __grid_constant__ CUtensorMap tmSB,
-                       const __grid_constant__ CUtensorMap tmO, const GemmArgs g) {
+                       const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmH,
+                       const GemmArgs g) {
   extern __shared__ uint8_t smem_raw[];
   using Smem = Gemm2Smem<kSwiglu>;
   constexpr int kS = Gemm2Cfg<kSwiglu>::kStages;
@@ -896,6 +951,7 @@ __global__ void __launch_bounds__(Gemm2Cfg<kSwiglu>::kThreads, 1)
     prefetch_tensormap(&tmSA);
     prefetch_tensormap(&tmSB);
     prefetch_tensormap(&tmO);
+    if constexpr (kSwiglu) prefetch_tensormap(&tmH);
   }
   if (warp == 1) {
     tmem_alloc2(&sm.tmem_base, 512);
@@ -1030,6 +1086,7 @@ __global__ void __launch_bounds__(Gemm2Cfg<kSwiglu>::kThreads, 1)
     int slot = 0;
     uint32_t hmax = 0;  // SwiGLU mode: this lane's max |h| (bf16 bits)
     const uint32_t tab = smem_u32(&sm.silu_tab[0]);
+    const uint32_t hbox = smem_u32(&sm.hbox[kSwiglu ? warp - 2 : 0][0]);
     if constexpr (kSwiglu) {  // the epilogue warps (threads 64 ..) build the silu table
       silu_table_build(tab, (int)threadIdx.x - 64, 32 * kEW);
       asm volatile("bar.sync 1, %0;" ::"n"(32 * kEW) : "memory");
@@ -1077,8 +1134,8 @@ __global__ void __launch_bounds__(Gemm2Cfg<kSwiglu>::kThreads, 1)
           __syncwarp();
           if (lane == 0) release();
         }
-        epilogue_piece<kSwiglu>(r, alpha, g, &tmO, slots, slot, T.ncol0 + c * kEpiChunk, row0, T.row_end, lane,
-                                hmax, tab);
+        epilogue_piece<kSwiglu, kSwiglu, kSwiglu>(r, alpha, g, &tmO, slots, slot, T.ncol0 + c * kEpiChunk, row0,
+                                                  T.row_end, lane, hmax, tab, &tmH, hbox);
       }
     }
     if constexpr (kSwiglu) swiglu_finish(g, hmax, gridDim.x * (uint32_t)kEW, lane);
@@ -1110,7 +1167,7 @@ namespace {
 template <bool kSwiglu>
 int launch_two_sm(GemmArgs& g, const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmO,
                   const void* a_scale, int64_t a_rows, const void* b_scale, int64_t b_rows, int clusters_wanted,
-                  int dev, cudaStream_t st) {
+                  int dev, cudaStream_t st, const CUtensorMap* tmH = nullptr) {
   CUtensorMap tmSA, tmSB;
   if (!rb_host::make_tmap_2d(&tmSA, a_scale, CU_TENSOR_MAP_DATA_TYPE_UINT8, 256,
                              (uint64_t)(a_rows / 128) * (uint64_t)g.kb_total * 2, 256, 256, 8,
@@ -1151,7 +1208,9 @@ int launch_two_sm(GemmArgs& g, const CUtensorMap& tmA, const CUtensorMap& tmB, c
   const int clusters = clusters_wanted < cap ? clusters_wanted : cap;
   if (clusters < 1) return RB_OK;
   cfg.gridDim = dim3(2 * clusters, 1, 1);
-  cudaError_t e = cudaLaunchKernelEx(&cfg, nvfp4_gemm2_kernel<kSwiglu>, tmA, tmB, tmSA, tmSB, tmO, g);
+  // tmH (SwiGLU mode: the h output) is unused by the plain kernel, which gets tmO in its place.
+  cudaError_t e = cudaLaunchKernelEx(&cfg, nvfp4_gemm2_kernel<kSwiglu>, tmA, tmB, tmSA, tmSB, tmO,
+                                     tmH != nullptr ? *tmH : tmO, g);
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) {
     rb_host::set_error("nvfp4 gemm launch failed: %s", cudaGetErrorString(e));
@@ -1338,8 +1397,15 @@ static int gemm_impl(const void* a_packed, const void* a_scale, const void* b_pa
   if (two_sm) {
     g.tiles_m = (int)((m + 255) / 256);
     g.n_tiles = g.tiles_m * g.tiles_n;
-    return swiglu ? launch_two_sm<true>(g, tmA, tmB, tmO, a_scale, m, b_scale, n, g.n_tiles, dev, st)
-                  : launch_two_sm<false>(g, tmA, tmB, tmO, a_scale, m, b_scale, n, g.n_tiles, dev, st);
+    if (swiglu) {
+      // h boxes: 32 rows x 32 bf16 (64 bytes), 64-byte swizzled; rows past m are clipped.
+      CUtensorMap tmH;
+      if (!rb_host::make_tmap_2d(&tmH, sw.h, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)(n / 2), (uint64_t)m,
+                                 (uint64_t)sw.ldh * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
+        return RB_ERR_CUDA;
+      return launch_two_sm<true>(g, tmA, tmB, tmO, a_scale, m, b_scale, n, g.n_tiles, dev, st, &tmH);
+    }
+    return launch_two_sm<false>(g, tmA, tmB, tmO, a_scale, m, b_scale, n, g.n_tiles, dev, st);
   }
   g.tiles_m = (int)(m / kBM);
   g.n_tiles = g.tiles_m * g.tiles_n;
