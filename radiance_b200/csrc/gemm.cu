@@ -486,6 +486,7 @@ __device__ __forceinline__ void epilogue_piece(const uint32_t (&r)[kEpiChunk], f
     }
     __syncwarp();
     const uint32_t box = kOneBox ? slots : slots + (uint32_t)slot * kOutBox;
+    const uint32_t hb = kOneBox ? hbox : hbox + (uint32_t)slot * 2048u;  // kHStage: this piece's h box
 #pragma unroll
     for (int c = 0; c < 8; ++c)
       st_shared_v4(box + row_off + ((c ^ sw) << 4), pack_bf16x2(v[8 * c], v[8 * c + 1]),
@@ -494,14 +495,14 @@ __device__ __forceinline__ void epilogue_piece(const uint32_t (&r)[kEpiChunk], f
     if constexpr (kHStage) {
 #pragma unroll
       for (int c = 0; c < 4; ++c)
-        st_shared_v4(hbox + (uint32_t)lane * 64u + ((uint32_t)(c ^ ((lane >> 1) & 3)) << 4), hw[4 * c], hw[4 * c + 1],
+        st_shared_v4(hb + (uint32_t)lane * 64u + ((uint32_t)(c ^ ((lane >> 1) & 3)) << 4), hw[4 * c], hw[4 * c + 1],
                      hw[4 * c + 2], hw[4 * c + 3]);
     }
     fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0 && store) {
       tma_store_2d(tmO, box, col0, (int)row0);
-      if constexpr (kHStage) tma_store_2d(tmH, hbox, col0 >> 1, (int)row0);
+      if constexpr (kHStage) tma_store_2d(tmH, hb, col0 >> 1, (int)row0);
       bulk_commit_group();
     }
     if (g.npeers > 0 && store) to_peers(box, (int64_t)col0 * 2);
@@ -736,14 +737,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 constexpr int kSfStep = 2048;  // one K step's scale atoms for 128 rows (4 x 512 B)
 
 // Per instantiation: the plain GEMM keeps five operand stages and four epilogue warps.  The SwiGLU
-// GEMM is bound by its epilogue (the per-element SwiGLU work on top of the output), so it runs two
-// epilogue warps on each TMEM lane quarter -- eight in all, two per scheduler, each taking every
-// other 64-column chunk -- and pays for their staging boxes and the silu table with one stage less.
+// GEMM's epilogue also computes and stores h, so it runs two epilogue warps on each TMEM lane
+// quarter -- eight in all, two per scheduler, each taking every other 64-column chunk -- and pays
+// for their staging boxes, the h boxes and the silu table with one stage less.  Measured at 16384 x
+// 11264 x 2048: four stages with one (output, h) box pair per warp 211 us; three stages 231 us with
+// one pair or two.
 template <bool kSwiglu>
 struct Gemm2Cfg {
   static constexpr int kStages = kSwiglu ? 4 : 5;
   static constexpr int kEpiWarps = kSwiglu ? 8 : 4;
   static constexpr int kThreads = 64 + 32 * kEpiWarps;  // producer, MMA issuer, epilogue
+  static constexpr int kSwBoxes = 1;                    // SwiGLU mode: staged (output, h) box pairs per warp
 };
 
 template <bool kSwiglu>
@@ -753,8 +757,10 @@ struct Gemm2Smem {
   uint8_t b[S][kBM * kStepBytes];  // this CTA's 128 of the tile's 256 B rows (16 KB)
   uint8_t sfa[S][kSfStep];         // scale atoms of this CTA's A rows
   uint8_t sfb[S][2 * kSfStep];     // scale atoms of all 256 B rows: [half][k block]
-  uint8_t out[4][2][4096];  // staged output boxes: two per epilogue warp, or one in SwiGLU mode
-  uint8_t hbox[kSwiglu ? 8 : 1][kSwiglu ? 2048 : 16];  // SwiGLU mode: each epilogue warp's staged h box
+  // Staged output boxes: two per epilogue warp, or kSwBoxes per warp in SwiGLU mode, with as many h
+  // boxes.
+  uint8_t out[kSwiglu ? Gemm2Cfg<kSwiglu>::kEpiWarps * Gemm2Cfg<kSwiglu>::kSwBoxes : 8][4096];
+  uint8_t hbox[kSwiglu ? Gemm2Cfg<kSwiglu>::kEpiWarps * Gemm2Cfg<kSwiglu>::kSwBoxes : 1][kSwiglu ? 2048 : 16];
   uint16_t silu_tab[kSwiglu ? 2 * kSiluTab : 8];        // SwiGLU mode: the silu table
   int tile_prefix[kMaxGroups + 1];  // grouped mode: tiles of groups 0..g-1
   uint64_t full[S];                 // leader: both CTAs' loads of a stage
@@ -1079,14 +1085,14 @@ __global__ void __launch_bounds__(Gemm2Cfg<kSwiglu>::kThreads, 1)
     const int q = warp & 3;  // TMEM lanes 32q .. 32q+31
     constexpr int kStride = kEW / 4;
     const int half = (warp - 2) / 4;
-    // Staging: two boxes per warp (pieces alternate between them), or in SwiGLU mode one box per
-    // warp, box w - 2 of the eight (two boxes each measured slower: the stores are not the limit).
-    const uint32_t slots =
-        kSwiglu ? smem_u32(&sm.out[0][0][0]) + (uint32_t)(warp - 2) * kOutBox : smem_u32(&sm.out[q][0][0]);
+    // Staging: two boxes per warp (pieces alternate between them), or in SwiGLU mode kSwBoxes
+    // (output, h) box pairs per warp.
+    constexpr int kBoxes = kSwiglu ? Gemm2Cfg<kSwiglu>::kSwBoxes : 2;
+    const uint32_t slots = smem_u32(&sm.out[(kSwiglu ? warp - 2 : q) * kBoxes][0]);
     int slot = 0;
     uint32_t hmax = 0;  // SwiGLU mode: this lane's max |h| (bf16 bits)
     const uint32_t tab = smem_u32(&sm.silu_tab[0]);
-    const uint32_t hbox = smem_u32(&sm.hbox[kSwiglu ? warp - 2 : 0][0]);
+    const uint32_t hbox = smem_u32(&sm.hbox[kSwiglu ? (warp - 2) * kBoxes : 0][0]);
     if constexpr (kSwiglu) {  // the epilogue warps (threads 64 ..) build the silu table
       silu_table_build(tab, (int)threadIdx.x - 64, 32 * kEW);
       asm volatile("bar.sync 1, %0;" ::"n"(32 * kEW) : "memory");
@@ -1134,8 +1140,9 @@ __global__ void __launch_bounds__(Gemm2Cfg<kSwiglu>::kThreads, 1)
           __syncwarp();
           if (lane == 0) release();
         }
-        epilogue_piece<kSwiglu, kSwiglu, kSwiglu>(r, alpha, g, &tmO, slots, slot, T.ncol0 + c * kEpiChunk, row0,
-                                                  T.row_end, lane, hmax, tab, &tmH, hbox);
+        epilogue_piece<kSwiglu, kSwiglu && kBoxes == 1, kSwiglu>(r, alpha, g, &tmO, slots, slot,
+                                                                 T.ncol0 + c * kEpiChunk, row0, T.row_end, lane,
+                                                                 hmax, tab, &tmH, hbox);
       }
     }
     if constexpr (kSwiglu) swiglu_finish(g, hmax, gridDim.x * (uint32_t)kEW, lane);
