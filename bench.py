@@ -1174,7 +1174,10 @@ def measure_config4(args, rank, world, device, barrier, max_over_ranks, steps):
     peaks, peak_kind = _peaks()
     fp4_peak = 4.0 * peaks["bf16_tflops"]
     gemm = per_kind.get("gemm", {"launches": 0, "ms": 0.0, "work": 0.0})
-    gemm_tflops = gemm["work"] / (gemm["ms"] * 1e-3) / 1e12 if gemm["ms"] else None
+    # The grouped launches' group sizes live on the device, so the kernel timer carries no work for
+    # them: the GEMM work of this rank's step is its routed rows through both expert linears.
+    gemm_work = gemm["work"] or 6.0 * plan.routed * (C4_D * 2 * C4_FFN + C4_FFN * C4_D)
+    gemm_tflops = gemm_work / (gemm["ms"] * 1e-3) / 1e12 if gemm["ms"] else None
     rec = {
         "metric": C4_METRIC,
         "value": round(C4_FLOPS / (ms * 1e-3) / 1e12, 2),
