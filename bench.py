@@ -1075,7 +1075,7 @@ def _c4_source_pairs(top, s, world):
 
 class _MoEFFN:
     """The expert FFN of config 4 for the experts of one rank: dispatch -> gate/up (grouped NVFP4)
-    -> SwiGLU (torch) -> down (grouped NVFP4) -> combine, the expert half of radiance's MoE layer
+    -> SwiGLU (one kernel, eager torch's roundings) -> down (grouped NVFP4) -> combine, the expert half of radiance's MoE layer
     (BatchedExperts.forward, src/radiance/model/ffn.py:148-153, with its [gate | up] split)."""
 
     def __init__(self, plan, w_gu, w_dn, device, recipe=None):
@@ -1094,13 +1094,12 @@ class _MoEFFN:
         self.down.refresh_fp4_cache()
 
     def __call__(self, x_send, group=None):
-        import torch.nn.functional as F
-
+        from radiance_b200.nvfp4 import swiglu
         from radiance_b200.nvfp4.expert_parallel import combine, dispatch
 
         x_exp = dispatch(x_send, self.plan, group)
         y_gu = self.gate_up(x_exp, self.plan.offsets)
-        h = F.silu(y_gu[:, :C4_FFN]) * y_gu[:, C4_FFN:]
+        h = swiglu(y_gu, "split")  # F.silu(g) * u on the [gate | up] halves, one kernel each way
         return combine(self.down(h, self.plan.offsets), self.plan, group)
 
 
@@ -1188,7 +1187,7 @@ def measure_config4(args, rank, world, device, barrier, max_over_ranks, steps):
         "higher_is_better": True,
         "scaling": "strong",
         "config": {
-            "workload": "config4: MoE expert FFN (dispatch, grouped gate+up 2048->2816, SwiGLU, grouped down "
+            "workload": "config4: MoE expert FFN (dispatch, grouped gate+up 2048->2816, fused SwiGLU, grouped down "
                         "1408->2048, combine) fwd+dgrad+wgrad via FP4GroupedLinear",
             "experts": C4_E, "experts_per_rank": C4_E // world, "top_k": C4_TOPK, "tokens_per_job": C4_TOKENS,
             "routed_rows_rank0": plan.routed, "padded_rows_rank0": plan.rows, "rank0_expert_rows": plan.expert_rows,

@@ -31,7 +31,7 @@
 extern "C" {
 #endif
 
-#define RB_NVFP4_ABI_VERSION 6
+#define RB_NVFP4_ABI_VERSION 7
 
 /* Input element types. */
 #define RB_DTYPE_BF16 0
@@ -252,6 +252,27 @@ int rb_nvfp4_gemm_swiglu(const void* a_packed, const void* a_scale, const void* 
 int rb_nvfp4_swiglu_backward(const void* grad_h, int64_t ldgh, const void* gu, int64_t ldgu, int64_t rows,
                              int64_t hidden, void* grad_gu, int64_t ldgg, float* gs_out, void* workspace,
                              void* stream);
+
+/*
+ * SwiGLU on pre-activations in any layout of 32-unit groups (no reference counterpart as an entry
+ * point; it replaces the eager F.silu(g) * u of radiance's expert FFN, src/radiance/model/ffn.py:148-153,
+ * and its autograd backward).  The gate value of (row r, hidden unit j) is
+ * gate[r * ld + (j / 32) * blk + j % 32] and the up value sits at the same offset from `up`:
+ *   radiance's split [gate | up] halves: up = gate + hidden, blk = 32;
+ *   the interleaved order of rb_nvfp4_gemm_swiglu: up = gate + 32, blk = 64.
+ * forward:  h[r, j] = bf16(bf16(silu(g)) * u), *gs_out = the global scale of h.
+ * backward: grad_gate / grad_up (same scheme with blko, ldo) as rb_nvfp4_swiglu_backward computes
+ *           them, *gs_out = the global scale of the whole gradient.
+ * Roundings are those of the eager torch ops.  hidden % 32 == 0; bf16 tensors 16-byte aligned;
+ * strides, blk and the up offsets multiples of 8 elements, up at or above gate; workspace: the
+ * 8-byte workspace of rb_nvfp4_global_scale (zero on entry, left zero).
+ */
+int rb_nvfp4_swiglu_forward_strided(const void* gate, const void* up, int64_t ld, int64_t blk, int64_t rows,
+                                    int64_t hidden, void* h, int64_t ldh, float* gs_out, void* workspace,
+                                    void* stream);
+int rb_nvfp4_swiglu_backward_strided(const void* grad_h, int64_t ldgh, const void* gate, const void* up, int64_t ld,
+                                     int64_t blk, int64_t rows, int64_t hidden, void* grad_gate, void* grad_up,
+                                     int64_t ldo, int64_t blko, float* gs_out, void* workspace, void* stream);
 
 /*
  * Test aid: the SwiGLU epilogue takes silu(g), rounded to bf16, from a table and three closed forms

@@ -76,6 +76,13 @@ SIGNATURES: dict[str, tuple] = {
     "rb_nvfp4_swiglu_backward": (
         _int, [_c_void_p, _i64, _c_void_p, _i64, _i64, _i64, _c_void_p, _i64, _c_void_p, _c_void_p, _c_void_p],
     ),
+    "rb_nvfp4_swiglu_forward_strided": (
+        _int, [_c_void_p, _c_void_p, _i64, _i64, _i64, _i64, _c_void_p, _i64, _c_void_p, _c_void_p, _c_void_p],
+    ),
+    "rb_nvfp4_swiglu_backward_strided": (
+        _int, [_c_void_p, _i64, _c_void_p, _c_void_p, _i64, _i64, _i64, _i64, _c_void_p, _c_void_p, _i64, _i64,
+               _c_void_p, _c_void_p, _c_void_p],
+    ),
     "rb_nvfp4_selftest_wait_timeout": (_int, [_int, ctypes.c_longlong, _c_void_p, _c_void_p]),
     "rb_peer_alloc": (_int, [ctypes.c_size_t, ctypes.POINTER(_c_void_p)]),
     "rb_peer_free": (_int, [_c_void_p]),
@@ -86,7 +93,7 @@ SIGNATURES: dict[str, tuple] = {
 
 RB_PEER_HANDLE_BYTES = 64
 
-ABI_VERSION = 6
+ABI_VERSION = 7
 
 RB_DTYPE_BF16 = 0
 RB_DTYPE_F32 = 1

@@ -26,7 +26,6 @@ import weakref
 
 import torch
 import torch.nn as nn
-import torch.nn.functional as F
 
 from .. import _lib
 from . import _trace
@@ -44,6 +43,7 @@ from .quantize import (
     quantize_into_,
     require_nvfp4,
     row_scale_bytes,
+    swiglu,
 )
 
 ALIGN = 128
@@ -418,7 +418,8 @@ class FP4BatchedExperts(nn.Module):
     output ``(n_experts, capacity, d_model)``, ``silu(x W_gate + b_gate) * (x W_up + b_up)``, then
     ``W_down``.  Gate and up run as one fused ``d -> 2 * ffn`` grouped linear.  ``capacity`` must be
     a multiple of 128; ``forward_sorted`` takes expert-sorted tokens with arbitrary 128-aligned
-    group sizes instead."""
+    group sizes instead.  ``F.silu(g) * u`` and its backward run as one kernel each (``swiglu``),
+    bit-identical to the eager torch ops."""
 
     def __init__(self, n_experts: int, d_model: int, ffn_dim: int, recipe: FP4Recipe | None = None, device=None):
         super().__init__()
@@ -433,9 +434,7 @@ class FP4BatchedExperts(nn.Module):
         self.down.refresh_fp4_cache()
 
     def forward_sorted(self, x: torch.Tensor, offsets: torch.Tensor) -> torch.Tensor:
-        h = self.gate_up(x, offsets)
-        g, u = h.split(self.ffn_dim, dim=1)
-        return self.down((F.silu(g) * u).contiguous(), offsets)
+        return self.down(swiglu(self.gate_up(x, offsets), "split"), offsets)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         e, cap, d = x.shape
@@ -443,6 +442,5 @@ class FP4BatchedExperts(nn.Module):
             raise ValueError(f"FP4BatchedExperts: capacity must be a multiple of 128, got {cap}")
         offsets = torch.arange(e + 1, dtype=torch.int64, device=x.device) * cap
         h = self.gate_up(x.reshape(e * cap, d), offsets).view(e, cap, -1) + self.gate_up_b.to(x.dtype)
-        g, u = h.split(self.ffn_dim, dim=2)
-        hidden = (F.silu(g) * u).reshape(e * cap, self.ffn_dim)
+        hidden = swiglu(h.reshape(e * cap, 2 * self.ffn_dim), "split")  # one kernel, eager torch's roundings
         return self.down(hidden, offsets).view(e, cap, d) + self.down_b.to(x.dtype)

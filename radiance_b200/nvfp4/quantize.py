@@ -760,6 +760,101 @@ def swiglu_backward(grad_h: torch.Tensor, gu: torch.Tensor, out: torch.Tensor | 
     return out, out_scale
 
 
+def _swiglu_layout(gu: torch.Tensor, layout: str, what: str):
+    """(rows x 2*hidden bf16 view, hidden, up offset in elements, group stride) of a gate/up tensor:
+    ``"split"`` is radiance's [gate | up] halves (ffn.py:148-153), ``"interleaved"`` the
+    [32 gate | 32 up] order of ``swiglu_mm``."""
+    _require_cuda(gu, what)
+    g2 = gu.reshape(-1, gu.shape[-1])
+    if g2.stride(-1) != 1 or g2.data_ptr() % 16 or g2.stride(0) % 8:
+        g2 = g2.contiguous()
+    if g2.dtype != torch.bfloat16:
+        raise ValueError(f"{what}: bf16 pre-activations expected")
+    if g2.shape[1] % 64:
+        raise ValueError(f"{what}: the gate/up width must be a multiple of 64, got {g2.shape[1]}")
+    hidden = g2.shape[1] // 2
+    if layout == "split":
+        return g2, hidden, hidden, 32
+    if layout == "interleaved":
+        return g2, hidden, 32, 64
+    raise ValueError(f"{what}: layout must be 'split' or 'interleaved', got {layout!r}")
+
+
+def swiglu_forward(gu: torch.Tensor, layout: str = "split", out: torch.Tensor | None = None,
+                   out_scale: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """``h = F.silu(g) * u`` from the gate/up pre-activations ``gu`` (``layout`` as in
+    ``_swiglu_layout``), bit-identical to the eager bf16 torch ops, and ``global_scale_of(h)``, in
+    one kernel.  Returns ``(h, scale)`` with h of shape ``gu.shape[:-1] + (hidden,)``."""
+    what = "nvfp4.swiglu_forward"
+    g2, hidden, du, blk = _swiglu_layout(gu, layout, what)
+    rows = g2.shape[0]
+    if out is None:
+        out = torch.empty(rows, hidden, dtype=torch.bfloat16, device=g2.device)
+    if out_scale is None:
+        out_scale = torch.empty((), dtype=torch.float32, device=g2.device)
+    lib = _lib.load()
+    _lib.check(
+        lib.rb_nvfp4_swiglu_forward_strided(
+            g2.data_ptr(), g2.data_ptr() + 2 * du, g2.stride(0), blk, rows, hidden, out.data_ptr(), out.stride(0),
+            out_scale.data_ptr(), _workspace(g2.device).data_ptr(), _stream_ptr(g2.device),
+        ),
+        what,
+    )
+    return out.reshape(*gu.shape[:-1], hidden), out_scale
+
+
+def swiglu_backward_strided(grad_h: torch.Tensor, gu: torch.Tensor, layout: str = "split",
+                            out: torch.Tensor | None = None,
+                            out_scale: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """The gradient of ``swiglu_forward`` with respect to ``gu``, in ``gu``'s layout, and its global
+    scale; bit-identical to eager autograd's backward of ``F.silu(g) * u``."""
+    what = "nvfp4.swiglu_backward"
+    g2, hidden, du, blk = _swiglu_layout(gu, layout, what)
+    gh = grad_h.reshape(-1, hidden)
+    if gh.stride(-1) != 1 or gh.data_ptr() % 16 or gh.stride(0) % 8:
+        gh = gh.contiguous()
+    if gh.dtype != torch.bfloat16 or gh.shape[0] != g2.shape[0]:
+        raise ValueError(f"{what}: a bf16 gradient of {g2.shape[0]} x {hidden} expected, got "
+                         f"{tuple(grad_h.shape)} {grad_h.dtype}")
+    rows = g2.shape[0]
+    if out is None:
+        out = torch.empty(rows, 2 * hidden, dtype=torch.bfloat16, device=g2.device)
+    if out_scale is None:
+        out_scale = torch.empty((), dtype=torch.float32, device=g2.device)
+    lib = _lib.load()
+    _lib.check(
+        lib.rb_nvfp4_swiglu_backward_strided(
+            gh.data_ptr(), gh.stride(0), g2.data_ptr(), g2.data_ptr() + 2 * du, g2.stride(0), blk, rows, hidden,
+            out.data_ptr(), out.data_ptr() + 2 * du, out.stride(0), blk, out_scale.data_ptr(),
+            _workspace(g2.device).data_ptr(), _stream_ptr(g2.device),
+        ),
+        what,
+    )
+    return out.reshape(gu.shape), out_scale
+
+
+class _SwiGLUFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, gu, layout):
+        h, _ = swiglu_forward(gu, layout)
+        ctx.save_for_backward(gu)
+        ctx.layout = layout
+        return h
+
+    @staticmethod
+    def backward(ctx, grad_h):
+        (gu,) = ctx.saved_tensors
+        grad_gu, _ = swiglu_backward_strided(grad_h, gu, ctx.layout)
+        return grad_gu, None
+
+
+def swiglu(gu: torch.Tensor, layout: str = "split") -> torch.Tensor:
+    """Differentiable ``F.silu(g) * u`` on gate/up pre-activations (``layout`` "split": radiance's
+    ``[gate | up]`` halves, ffn.py:148-153; "interleaved": ``swiglu_mm``'s order): one kernel
+    forward and one backward, outputs and gradients bit-identical to the eager torch ops."""
+    return _SwiGLUFn.apply(gu, layout)
+
+
 def mm(a: NVFP4Tensor, b: NVFP4Tensor, *, out_dtype: torch.dtype = torch.bfloat16, bias=None) -> torch.Tensor:
     """``a @ b.T`` with the global scales folded back in (quantize.py:400-409).
 

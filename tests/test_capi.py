@@ -174,3 +174,24 @@ def test_wait_selftest_rejects_bad_arguments_on_the_host():
     assert lib.rb_nvfp4_selftest_wait_timeout(0, 0, buf, None) == 2
     assert lib.rb_nvfp4_selftest_wait_timeout(0, 1 << 40, buf, None) == 2
     assert "limit_cycles" in lib.rb_nvfp4_last_error().decode()
+
+
+def test_strided_swiglu_contract_is_checked_on_the_host():
+    """The strided SwiGLU entries refuse layouts they cannot serve before touching memory."""
+    lib = _lib.load()
+    gate, up, out = ctypes.c_void_p(4096), ctypes.c_void_p(4096 + 2 * 64), ctypes.c_void_p(1 << 20)
+    ws = ctypes.c_void_p(256)
+    # null workspace
+    assert lib.rb_nvfp4_swiglu_forward_strided(gate, up, 128, 32, 16, 64, out, 64, ws, None, None) == 2
+    # hidden not a multiple of 32
+    assert lib.rb_nvfp4_swiglu_forward_strided(gate, up, 128, 32, 16, 48, out, 64, ws, ws, None) == 1
+    # row stride shorter than the split layout's 2 * hidden
+    assert lib.rb_nvfp4_swiglu_forward_strided(gate, up, 96, 32, 16, 64, out, 64, ws, ws, None) == 1
+    assert "row strides" in lib.rb_nvfp4_last_error().decode()
+    # up below gate
+    assert lib.rb_nvfp4_swiglu_forward_strided(up, gate, 128, 32, 16, 64, out, 64, ws, ws, None) == 1
+    # misaligned gradient output
+    bad = ctypes.c_void_p((1 << 20) + 2)
+    assert lib.rb_nvfp4_swiglu_backward_strided(out, 64, gate, up, 128, 32, 16, 64, bad, ctypes.c_void_p((1 << 20) + 128),
+                                                128, 32, ws, ws, None) == 2
+    assert "aligned" in lib.rb_nvfp4_last_error().decode()

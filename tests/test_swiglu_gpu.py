@@ -232,3 +232,70 @@ def test_swiglu_backward_on_every_bf16_gate_value(nv):
         got, _ = nv.swiglu_backward(grad_h, gu)
         want = _torch_swiglu_backward(nv, grad_h, gu)
         assert torch.equal(got.view(torch.int16), want.view(torch.int16)), (dh_val, u_val)
+
+
+def _eager_swiglu(gu: torch.Tensor, layout: str) -> torch.Tensor:
+    """radiance's eager ``F.silu(g) * u`` (ffn.py:32, :148-153) on either layout."""
+    import radiance_b200.nvfp4 as nv
+
+    g, u = gu.chunk(2, dim=-1) if layout == "split" else nv.split_gate_up(gu)
+    return F.silu(g) * u
+
+
+@pytest.mark.parametrize("layout", ["split", "interleaved"])
+@pytest.mark.parametrize("rows,hidden", [(128, 32), (640, 1408), (2048, 5632)])
+def test_swiglu_forward_matches_eager(nv, layout, rows, hidden):
+    gen = torch.Generator(device="cuda").manual_seed(rows + hidden + len(layout))
+    gu = (torch.randn(rows, 2 * hidden, device="cuda", generator=gen) * 3).bfloat16()
+    h, gs = nv.swiglu_forward(gu, layout)
+    want = _eager_swiglu(gu, layout)
+    assert torch.equal(h.view(torch.int16), want.view(torch.int16))
+    assert gs.view(torch.int32).item() == nv.global_scale_of(want).view(torch.int32).item()
+    h2, gs2 = nv.swiglu_forward(gu, layout)  # the workspace came back zeroed
+    assert torch.equal(h2, h) and torch.equal(gs2, gs)
+    _status_ok()
+
+
+@pytest.mark.parametrize("layout", ["split", "interleaved"])
+def test_swiglu_forward_on_every_bf16_gate_value(nv, layout):
+    """Every bf16 bit pattern of g against up values that make normal, subnormal and overflowing
+    products."""
+    g = torch.arange(0, 65536, dtype=torch.int32, device="cuda").to(torch.int16).view(torch.bfloat16).view(-1, 32)
+    for u_val in (1.0, -0.75, 3e-38, -1e-39, 2e38):
+        u = torch.full_like(g, u_val)
+        gu = torch.cat([g, u], dim=1) if layout == "split" else nv.merge_gate_up(g, u)
+        h, _ = nv.swiglu_forward(gu, layout)
+        want = _eager_swiglu(gu, layout)
+        same = h.view(torch.int16) == want.view(torch.int16)
+        both_nan = torch.isnan(h.float()) & torch.isnan(want.float())
+        assert bool((same | both_nan).all()), u_val
+
+
+@pytest.mark.parametrize("layout", ["split", "interleaved"])
+def test_swiglu_autograd_matches_eager(nv, layout):
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    rows, hidden = 1024, 1408
+    gu = (torch.randn(rows, 2 * hidden, device="cuda", generator=gen) * 2).bfloat16()
+    dh = (torch.randn(rows, hidden, device="cuda", generator=gen) * 1e-2).bfloat16()
+    a = gu.clone().requires_grad_(True)
+    b = gu.clone().requires_grad_(True)
+    ya = nv.swiglu(a, layout)
+    yb = _eager_swiglu(b, layout)
+    ya.backward(dh)
+    yb.backward(dh)
+    assert torch.equal(ya.view(torch.int16), yb.view(torch.int16))
+    assert torch.equal(a.grad.view(torch.int16), b.grad.view(torch.int16))
+    grad, gs = nv.swiglu_backward_strided(dh, gu, layout)
+    assert torch.equal(grad, a.grad)
+    assert gs.view(torch.int32).item() == nv.global_scale_of(b.grad).view(torch.int32).item()
+    _status_ok()
+
+
+def test_swiglu_layout_contract(nv):
+    gu = torch.zeros(128, 96, dtype=torch.bfloat16, device="cuda")  # width not a multiple of 64
+    with pytest.raises(ValueError, match="multiple of 64"):
+        nv.swiglu_forward(gu)
+    with pytest.raises(ValueError, match="layout"):
+        nv.swiglu_forward(torch.zeros(128, 128, dtype=torch.bfloat16, device="cuda"), "rows")
+    with pytest.raises(ValueError, match="bf16"):
+        nv.swiglu_forward(torch.zeros(128, 128, dtype=torch.float32, device="cuda"))
