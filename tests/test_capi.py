@@ -65,6 +65,11 @@ def test_ops_refuse_cpu_tensors():
         nv.quantize(x, -1)
     with pytest.raises(RuntimeError, match="no CPU"):
         nv.global_scale_of(x)
+    gu = torch.randn(128, 128).bfloat16()
+    with pytest.raises(RuntimeError, match="no CPU"):
+        nv.swiglu(gu, "split")
+    with pytest.raises(RuntimeError, match="no CPU"):
+        nv.swiglu_backward_strided(gu[:, :64], gu, "split")
     assert not nv.nvfp4_supported("cpu")
 
 
