@@ -1438,10 +1438,29 @@ def measure_config5(args, rank, world, device, barrier, max_over_ranks, steps):
     if C5_TOKENS % (128 * world):
         raise SystemExit(f"config 5 needs 65536 tokens to shard into multiples of 128 over {world} ranks")
     m_local = C5_TOKENS // world
-    # The N-split layer's rows (all 65536 tokens of the job) are replicated over the group: every
-    # rank computes its column slice of gate_up for all of them.
-    m_ffn = C5_TOKENS
+    # gate_up is N-split over groups of `nsr` ranks (all of them by default).  With nsr < N the split
+    # is 2-D: the job's tokens are divided over the N / nsr groups, each group N-splits gate_up over
+    # its own tokens (replicated inside the group), and each weight slice's fp32 gradient is
+    # reduce-scattered over the groups (the ranks holding the same slice).
+    nsr = args.c5_nsplit_ranks if 0 < args.c5_nsplit_ranks < world else world
+    if world % nsr or (C5_NSPLIT[0][2] // nsr) % (128 * (world // nsr)):
+        raise SystemExit(f"config 5: --c5-nsplit-ranks {nsr} does not divide {world} ranks and gate_up's rows")
+    n_groups = world // nsr
+    split_group, slice_group = None, None
+    if n_groups > 1:
+        for g0 in range(n_groups):  # every rank creates every group, in the same order
+            grp = dist.new_group(list(range(g0 * nsr, (g0 + 1) * nsr)))
+            if rank // nsr == g0:
+                split_group = grp
+        for s0 in range(nsr):
+            grp = dist.new_group(list(range(s0, world, nsr)))
+            if rank % nsr == s0:
+                slice_group = grp
+    # The N-split layer's rows (this group's share of the job's tokens) are replicated over the
+    # group: every rank computes its column slice of gate_up for all of them.
+    m_ffn = C5_TOKENS // n_groups
     gen = torch.Generator(device=device).manual_seed(777)  # same on every rank: replicated weights/rows
+    gen_ffn = gen if n_groups == 1 else torch.Generator(device=device).manual_seed(5000 + rank // nsr)
     layers, inputs, grads = [], [], []
     side = torch.cuda.Stream(device)
     shards, pending = [], []
@@ -1466,18 +1485,30 @@ def measure_config5(args, rank, world, device, barrier, max_over_ranks, steps):
         grads.append((torch.randn(m_local, n, device=device, generator=g_local) * 1e-3).to(torch.bfloat16))
     full_w = None
     for name, k, n in C5_NSPLIT:
-        lin = FP4ColumnParallelLinear(k, n, device=device, fused_gather=args.nsplit == "fused")
+        lin = FP4ColumnParallelLinear(k, n, group=split_group, device=device, fused_gather=args.nsplit == "fused")
         full_w = torch.randn(n, k, device=device, generator=gen) * 0.02
         lin.load_full_weight(full_w)
         lin.refresh_fp4_cache()
+        if n_groups > 1:
+            shard = torch.empty(n // nsr // n_groups, k, device=device)
+            shards.append(shard)
+
+            def slice_hook(grad_w, shard=shard):
+                side.wait_stream(torch.cuda.current_stream())
+                with torch.cuda.stream(side):
+                    dist.reduce_scatter_tensor(shard, grad_w, group=slice_group)
+                pending.append(grad_w)
+            lin.local.wgrad_hook = slice_hook
         layers.append((lin, lin.local.weight))
-        inputs.append(torch.randn(m_ffn, k, device=device, generator=gen).to(torch.bfloat16))
-        grads.append((torch.randn(m_ffn, n, device=device, generator=gen) * 1e-3).to(torch.bfloat16))
+        inputs.append(torch.randn(m_ffn, k, device=device, generator=gen_ffn).to(torch.bfloat16))
+        grads.append((torch.randn(m_ffn, n, device=device, generator=gen_ffn) * 1e-3).to(torch.bfloat16))
     flops_rank = 6.0 * (m_local * sum(k * n for _, k, n in C5_TOKEN_SHARDED)
-                        + m_ffn * sum(k * n for _, k, n in C5_NSPLIT) / world)
-    gather_bytes = sum(m_ffn * n * 2 * (world - 1) // world for _, k, n in C5_NSPLIT) if world > 1 else 0
-    reduce_bytes = sum(m_ffn * k * 2 for _, k, n in C5_NSPLIT) if world > 1 else 0
+                        + m_ffn * sum(k * n for _, k, n in C5_NSPLIT) / nsr)
+    gather_bytes = sum(m_ffn * n * 2 * (nsr - 1) // nsr for _, k, n in C5_NSPLIT) if nsr > 1 else 0
+    reduce_bytes = sum(m_ffn * k * 2 for _, k, n in C5_NSPLIT) if nsr > 1 else 0
     wgrad_rs_bytes = sum(n * k * 4 for _, k, n in C5_TOKEN_SHARDED) if world > 1 else 0
+    if n_groups > 1:
+        wgrad_rs_bytes += sum(n // nsr * k * 4 for _, k, n in C5_NSPLIT)
 
     def step():
         for (lin, w), x0, dy in zip(layers, inputs, grads):
@@ -1524,6 +1555,7 @@ def measure_config5(args, rank, world, device, barrier, max_over_ranks, steps):
         barrier()
         for lin, _w in layers:
             if isinstance(lin, FP4ColumnParallelLinear):
+                lin.local.wgrad_hook = None
                 lin.close()
             else:
                 lin.wgrad_hook = None
@@ -1552,7 +1584,9 @@ def measure_config5(args, rank, world, device, barrier, max_over_ranks, steps):
             "allgather_bytes_received_per_rank_per_step": gather_bytes,
             "dgrad_allreduce_bytes_per_rank_per_step": reduce_bytes,
             "wgrad_reduce_scatter_bytes_per_step": wgrad_rs_bytes,
-            "parallelism": f"gate_up N-split over {world} + token-sharded QKV/O/down",
+            "parallelism": (f"gate_up N-split over {world} + token-sharded QKV/O/down" if n_groups == 1 else
+                            f"2-D: gate_up N-split over groups of {nsr} ranks, the job's tokens over the {n_groups} "
+                            f"groups, each slice's fp32 dW reduce-scattered over the groups; token-sharded QKV/O/down"),
             "nsplit_gather": ("GEMM epilogue stores each tile into every rank's output over NVLink "
                               "(rb_nvfp4_gemm_allgather, IPC-shared buffers)") if args.nsplit == "fused"
             else "NCCL all_gather_into_tensor + column permute",
@@ -1869,6 +1903,9 @@ def main():
                     help="config 3: time the Python step loop instead of a captured CUDA graph of the step")
     ap.add_argument("--nsplit", choices=["fused", "nccl"], default="fused",
                     help="config 5: the N-split layer's output all-gather (fused into the GEMM, or NCCL)")
+    ap.add_argument("--c5-nsplit-ranks", type=int, default=0,
+                    help="config 5: N-split gate_up over groups of this many ranks and divide the tokens over the "
+                         "groups (a 2-D split); 0 = one group of all ranks")
     ap.add_argument("--config", choices=["2", "3", "4", "5"], default="3",
                     help="2: one linear forward (8192 x 4096 x 4096); 3: dense block linears (the headline "
                          "line); 4: MoE expert linears; 5: d_model 4096 block with the FFN N-split")
