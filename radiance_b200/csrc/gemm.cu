@@ -209,11 +209,9 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 // The output is written once and not read again by this kernel, so its lines are marked to leave
 // L2 first: the operand tiles that later tiles re-read stay resident.
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t smem_src, int x, int y) {
-  uint64_t policy;
-  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%2, %3}], [%1], %4;" ::"l"(
                    map),
-               "r"(smem_src), "r"(x), "r"(y), "l"(policy)
+               "r"(smem_src), "r"(x), "r"(y), "l"(policy_evict_first())
                : "memory");
 }
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
